@@ -1,0 +1,454 @@
+"""Benchmark: Flash-Next MoE-layer decode on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c2|c1]
+
+Workload (N = 1, default ``c2``): one qwen4_exp sparse-MoE
+layer -- hidden 2048, 512 experts of intermediate 512 (Q4/G32), top-10 with
+softmax renorm, one Q4/G32 shared expert with a sigmoid gate -- decoding a
+ragged batch of 64 tokens whose routing follows Zipf(1.1).  A step is one
+full layer: router GEMV, softmax/top-k, GPU grouping, grouped gate/up+SwiGLU,
+down, slot-ordered combine + shared expert.  Inputs are seeded synthetic
+tensors of those shapes and distributions (no checkpoint exists here).
+
+Four distinct layers (4 x 1.0 GB of experts, more than the 126 MB L2) are
+rotated step by step, each with its own 64-token batch, so every step streams
+its weights from HBM.
+
+``value`` = tokens/s of the whole job with inputs resident in HBM (device
+time, CUDA events, max over ranks).  ``e2e`` = the same through the public
+API with the batch copied from pinned host memory and the output copied back
+inside the timed region.  N > 1 runs one independent replica per GPU
+(weak scaling: 64 tokens per GPU).
+
+``--impl reference`` times the reference-semantics CPU implementation (the
+NumPy oracle port; MLX, the reference's own runtime, is not installable
+here) on the host cores with a bounded sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "macqwen-releases_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "MoE-layer decode tokens/s (batch 1, 64) and HBM GB/s vs roofline at 1/2/4/8 B200"
+HIDDEN, INTER, EXPERTS, TOP_K, GROUP = 2048, 512, 512, 10, 32
+LAYERS = 4
+# bytes of one expert's three Q4/G32 projections at 2048/512
+EXPERT_BYTES = 3 * (INTER * HIDDEN // 2 + 2 * INTER * (HIDDEN // GROUP) * 2)
+GATE_UP_BYTES = 2 * (INTER * HIDDEN // 2 + 2 * INTER * (HIDDEN // GROUP) * 2)
+ROUTER_BYTES = EXPERTS * HIDDEN * 2
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# DRAM traffic per gate_up launch at this workload, from the ncu capture
+# summarised in profiles/ (None until a capture exists).
+NCU_GATE_UP_TRAFFIC_BYTES = None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _max_over_ranks(value: float, world: int):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# --------------------------------------------------------------------------
+# CPU reference arm / baseline (oracle port, host cores)
+# --------------------------------------------------------------------------
+
+
+def cpu_sample_inputs(tokens: int, seed: int = 0):
+    """NumPy inputs with the workload's shapes, restricted to the experts the
+    sampled tokens route to (the oracle only touches those)."""
+    import numpy as np
+
+    from oracle import bf16, moe
+
+    rng = np.random.default_rng(seed)
+    u = rng.standard_normal(HIDDEN)
+    u /= np.linalg.norm(u)
+    ranks = rng.permutation(EXPERTS) + 1.0
+    p = ranks ** -1.1
+    p /= p.sum()
+    x = bf16.round_f32((rng.standard_normal((tokens, HIDDEN)) + 8.0 * u).astype(np.float32))
+    w = bf16.round_f32((rng.standard_normal((EXPERTS, HIDDEN)) * 0.02 + (0.43 * np.log(p) / 8.0)[:, None] * u).astype(np.float32))
+    inds, _, _, _ = moe.router(x, w, TOP_K)
+    used = np.unique(inds)
+
+    def proj(o, k, n=EXPERTS):
+        # Only routed experts are materialised; the rest are never read.
+        words = np.zeros((n, o, k // 8), np.uint32)
+        s = np.zeros((n, o, k // GROUP), np.float32)
+        for e in (used if n == EXPERTS else range(n)):
+            words[e] = rng.integers(0, 2 ** 32, (o, k // 8), dtype=np.uint32)
+            s[e] = bf16.round_f32(np.abs(rng.normal(0, 0.01, (o, k // GROUP))).astype(np.float32))
+        return words, s, bf16.round_f32(-8 * s)
+
+    gate, up, down = proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER)
+    sh = tuple(tuple(a[0] for a in t) for t in (proj(INTER, HIDDEN, 1), proj(INTER, HIDDEN, 1), proj(HIDDEN, INTER, 1)))
+    wg = bf16.round_f32((rng.standard_normal(HIDDEN) * 0.02).astype(np.float32))
+    return x, w, gate, up, down, sh, wg, len(used)
+
+
+def cpu_baseline(target_s: float = 15.0):
+    """Time the oracle port on a bounded sample; returns (tokens/s, sample, cores)."""
+    from oracle import moe
+
+    tokens = 4
+    x, w, gate, up, down, sh, wg, used = cpu_sample_inputs(tokens)
+    t0 = time.perf_counter()
+    done = 0
+    while True:
+        moe.moe_block(x, w, TOP_K, gate, up, down, sh, wg)
+        done += tokens
+        if time.perf_counter() - t0 >= target_s:
+            break
+    el = time.perf_counter() - t0
+    return done / el, f"{done} tokens ({tokens}-token batches, {used} distinct experts) of the workload in {el:.1f} s", os.cpu_count()
+
+
+def reference_arm(args):
+    world, rank, _ = _dist()
+    if rank != 0:
+        return 0
+    sample_s = max(2.0, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
+    from oracle import moe
+
+    tokens = 4
+    x, w, gate, up, down, sh, wg, used = cpu_sample_inputs(tokens)
+    for _ in range(args.warmup):
+        moe.moe_block(x, w, TOP_K, gate, up, down, sh, wg)
+    rates = []
+    total_tokens, total_s = 0, 0.0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        done = 0
+        while True:
+            moe.moe_block(x, w, TOP_K, gate, up, down, sh, wg)
+            done += tokens
+            if time.perf_counter() - t0 >= sample_s:
+                break
+        el = time.perf_counter() - t0
+        rates.append(done / el)
+        total_tokens += done
+        total_s += el
+    value = total_tokens / total_s
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total_s / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "C2: one MoE layer, 64-token ragged decode, Zipf(1.1) routing, H2048/I512/E512 top-10 Q4/G32 + shared",
+                   "sample": f"{tokens}-token batches"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"each step: {tokens}-token batches for {sample_s:.1f} s ({used} distinct experts)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "NumPy restatement of the reference semantics on host cores (MLX runtime not installable here)",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------
+# GPU arm
+# --------------------------------------------------------------------------
+
+
+def _build_layers(tokens, layers, seed):
+    from flashnext_b200 import synthetic
+    from flashnext_b200.moe_block import SparseMoEBlock
+
+    blocks, xs = [], []
+    for i in range(layers):
+        L = synthetic.moe_layer(tokens, HIDDEN, INTER, EXPERTS, TOP_K, GROUP, zipf=1.1, seed=seed + 101 * i)
+        blocks.append(SparseMoEBlock(L.router_weight, L.experts, top_k=TOP_K, shared=L.shared,
+                                     shared_expert_gate=L.shared_expert_gate))
+        xs.append(L.x)
+    return blocks, xs
+
+
+def _distinct_experts(block):
+    import torch
+
+    return int(torch.unique(block.last_inds).numel())
+
+
+def gpu_arm(args):
+    import torch
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    from flashnext_b200 import _lib
+
+    _lib.ensure_device()
+    tokens = 64 if args.workload == "c2" else 1
+    blocks, xs = _build_layers(tokens, LAYERS, seed=17 + rank)
+    outs = [torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device="cuda") for _ in range(LAYERS)]
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        j = i % LAYERS
+        blocks[j](xs[j], out=outs[j])
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    used = [(_distinct_experts(b)) for b in blocks]
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    _barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    ms = start.elapsed_time(end)
+    clocks = sampler.stop()
+    ms = _max_over_ranks(ms, world)
+    value = tokens * args.steps * world / (ms / 1000.0)
+
+    # e2e: pinned host batch -> device -> layer -> host, per step
+    host_x = [x.cpu().pin_memory() for x in xs]
+    host_out = [torch.empty((tokens, HIDDEN), dtype=torch.bfloat16).pin_memory() for _ in range(LAYERS)]
+    dev_x = [torch.empty_like(x) for x in xs]
+
+    def e2e_step(i):
+        j = i % LAYERS
+        dev_x[j].copy_(host_x[j], non_blocking=True)
+        blocks[j](dev_x[j], out=outs[j])
+        host_out[j].copy_(outs[j], non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_value = tokens * args.steps * world / (e2e_ms / 1000.0)
+
+    # per-kernel device times (separate pass of the same steps, events per launch)
+    _lib.profile_enable(True)
+    _lib.profile_read(reset=True)
+    for i in range(args.steps):
+        step(i)
+    torch.cuda.synchronize()
+    prof = _lib.profile_read(reset=True)
+    _lib.profile_enable(False)
+    launches_per_step = sum(c for c, _ in prof.values()) / max(1, args.steps)
+
+    hbm_peak, peak_kind = _peaks()
+    avg_used = sum(used) / len(used)
+    gu_count, gu_ms = prof.get("gate_up", (0, 0.0))
+    gu_avg_s = (gu_ms / max(1, gu_count)) / 1000.0
+    gu_bytes = (avg_used + 1) * GATE_UP_BYTES + tokens * HIDDEN * 2 * (TOP_K + 1)
+    achieved = gu_bytes / gu_avg_s / 1e9 if gu_avg_s > 0 else None
+    layer_bytes = (avg_used + 1) * EXPERT_BYTES + ROUTER_BYTES + HIDDEN * 2 + 2 * tokens * HIDDEN * 2
+    step_s = ms / args.steps / 1000.0
+
+    batch1 = None
+    if world == 1 and args.workload == "c2":
+        batch1 = batch1_numbers(hbm_peak)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, sample, cores = cpu_baseline()
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": "C2: one qwen4_exp MoE layer, 64-token ragged decode, Zipf(1.1) routing, "
+                            "H2048/I512/E512 top-10 Q4/G32 + Q4/G32 shared expert" if tokens == 64 else
+                            "C1: one MoE layer, batch-1 decode",
+                "tokens_per_gpu": tokens, "layers_rotated": LAYERS,
+                "l2": "inputs larger than L2: 4 distinct 1.0 GB layers rotated per step",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "distinct_experts_per_layer": avg_used,
+            },
+            "layer_hbm_gbs": layer_bytes / step_s / 1e9,
+            "layer_roofline_frac": (layer_bytes / step_s / 1e9) / hbm_peak,
+            "roofline": {"bound": "hbm", "kernel": "gate_up", "achieved": achieved, "peak": hbm_peak,
+                         "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": (achieved / hbm_peak) if achieved else None,
+                         "traffic": NCU_GATE_UP_TRAFFIC_BYTES,
+                         "algorithmic_bytes": gu_bytes, "avg_launch_us": gu_avg_s * 1e6},
+            "kernels": {k: {"launches": c, "avg_us": 1000.0 * t / max(1, c)} for k, (c, t) in prof.items()},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": tokens * HIDDEN * 2,
+                    "d2h_bytes_per_step": tokens * HIDDEN * 2},
+            "gpu_launches": int(round(launches_per_step * args.steps)),
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        if batch1 is not None:
+            line["batch1"] = batch1
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def batch1_numbers(hbm_peak):
+    """Batch-1 (config 1) tokens/s over 8 distinct layers via one CUDA graph."""
+    import torch
+
+    layers = 8
+    blocks, xs = _build_layers(1, layers, seed=900)
+    outs = [torch.empty((1, HIDDEN), dtype=torch.bfloat16, device="cuda") for _ in range(layers)]
+    for j in range(layers):
+        blocks[j](xs[j], out=outs[j])
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for j in range(layers):
+                blocks[j](xs[j], out=outs[j])
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = 20
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / (reps * layers)
+    layer_bytes = (TOP_K + 1) * EXPERT_BYTES + ROUTER_BYTES + HIDDEN * 2 * 3
+    gbs = layer_bytes / (ms / 1000.0) / 1e9
+    return {"layer_tokens_per_s": 1000.0 / ms, "us_per_layer": ms * 1000.0, "hbm_gbs": gbs,
+            "roofline_frac": gbs / hbm_peak, "bytes_per_layer": layer_bytes,
+            "note": "8 distinct layers in one CUDA graph, 20 replays"}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c2", "c1"], default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        return reference_arm(args)
+    return gpu_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

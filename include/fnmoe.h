@@ -1,0 +1,268 @@
+/*
+ * fnmoe.h -- C ABI of the B200 (sm_100a) Flash-Next sparse-MoE decode path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as `void*` (NULL = legacy default stream).  Nothing here allocates
+ * device memory: scratch comes from a caller-provided workspace whose size
+ * the matching *_workspace_size call reports.  Each call returns FNMOE_OK (0)
+ * or a negative FNMOE_ERR_* code; fnmoe_get_last_error() returns the message
+ * of the calling thread's last failure.
+ *
+ * Reference interfaces replaced (paths inside 1architect/macqwen-releases):
+ *   fnmoe_available / fnmoe_get_last_error
+ *       flashnext_native_available / flashnext_native_get_last_error
+ *       (models/flashnext/tests/bench/metal_runtime_native.mm:196-209)
+ *   FnMoEArgs + fnmoe_moe_execute
+ *       FlashNextMoEArgs + flashnext_native_moe_execute
+ *       (metal_runtime_native.mm:175-194, :258-396) and the op-level
+ *       MetalMoEExecutor.execute (models/flashnext/metal_runtime.py:764-932)
+ *   fnmoe_weighted_combine   weighted_combine (metal_runtime.py:145-191)
+ *   fnmoe_router_topk        adaptive_topk._moe_call router chain
+ *       (models/flashnext/adaptive_topk.py:53-64,256-261; compiled.py:61-71)
+ *   fnmoe_group_tokens       _gather_sort grouping for ragged batches
+ *       (models/flashnext/expert_cache.py:1790-1810)
+ *   fnmoe_moe_layer          the patched sparse-MoE block
+ *       (adaptive_topk.py:53-292 with StreamingSwitchGLU, expert_cache.py:1584-1810)
+ *   fnmoe_dequantize         mx.dequantize affine Q4 (metal_runtime.py:751-758)
+ *   fnmoe_swiglu             fused up-SwiGLU bfloat16 epilogue (metal_runtime.py:262-285)
+ *   fnmoe_paged_decode       paged_attention decode (models/qwen27b/paged_kv.py:417-495)
+ */
+#ifndef FNMOE_H
+#define FNMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FNMOE_API __attribute__((visibility("default")))
+#else
+#define FNMOE_API
+#endif
+
+#define FNMOE_ABI_VERSION 1u
+
+/* Status codes (negative = failure), mirroring the native bridge's
+ * "0 ok / negative specific failure" convention. */
+#define FNMOE_OK 0
+#define FNMOE_ERR_NULL (-1)        /* a required pointer is NULL            */
+#define FNMOE_ERR_SHAPE (-2)       /* a size is zero, misaligned or too big */
+#define FNMOE_ERR_UNSUPPORTED (-3) /* dtype / group size / layout           */
+#define FNMOE_ERR_DEVICE (-4)      /* no usable sm_100 device               */
+#define FNMOE_ERR_WORKSPACE (-5)   /* workspace missing or too small        */
+#define FNMOE_ERR_LAUNCH (-6)      /* CUDA launch or runtime error          */
+#define FNMOE_ERR_ABI (-7)         /* abi_version mismatch                  */
+#define FNMOE_ERR_VALUE (-8)       /* argument value out of range           */
+
+/* Element types. */
+#define FNMOE_DTYPE_BF16 0u
+#define FNMOE_DTYPE_F32 1u
+
+/* FnMoEArgs.flags */
+#define FNMOE_FLAG_RETURN_ALL 0x1u   /* write gate/up/down per slot, no combine */
+#define FNMOE_FLAG_NO_COMBINE 0x2u   /* scores absent: write per-slot down only */
+
+/* Part order inside an expert record (slab_pack.py:96-153). */
+#define FNMOE_PART_GATE_W 0
+#define FNMOE_PART_GATE_S 1
+#define FNMOE_PART_GATE_B 2
+#define FNMOE_PART_UP_W 3
+#define FNMOE_PART_UP_S 4
+#define FNMOE_PART_UP_B 5
+#define FNMOE_PART_DOWN_W 6
+#define FNMOE_PART_DOWN_S 7
+#define FNMOE_PART_DOWN_B 8
+
+/* HBM-resident expert table: a header followed by fixed-stride expert
+ * records, each holding the nine tensors at `part_offset`.  A route with bit
+ * 31 set addresses record (route & 0x7FFFFFFF) (expert_pool.py:38,
+ * metal_runtime.py:198-228). */
+typedef struct FnExpertTable {
+  const void *base;
+  uint64_t header_bytes;
+  uint64_t record_stride;
+  uint64_t part_offset[9];
+  uint32_t records;
+  uint32_t reserved;
+} FnExpertTable;
+
+/* One MoE executor call: gate -> up -> SwiGLU -> down -> combine.
+ * The first 19 fields follow FlashNextMoEArgs' order. */
+typedef struct FnMoEArgs {
+  uint32_t abi_version;        /* FNMOE_ABI_VERSION */
+  uint32_t flags;              /* FNMOE_FLAG_* */
+  const void *x;               /* [tokens, hidden]  (x_dtype) */
+  const uint32_t *gate_weight; /* [experts, inter, hidden/8] packed Q4 */
+  const void *gate_scales;     /* [experts, inter, hidden/group] bf16 */
+  const void *gate_biases;
+  const uint32_t *up_weight;
+  const void *up_scales;
+  const void *up_biases;
+  const uint32_t *down_weight; /* [experts, hidden, inter/8] */
+  const void *down_scales;     /* [experts, hidden, inter/group] bf16 */
+  const void *down_biases;
+  const uint32_t *routes;      /* [tokens, slots]; bit 31 = table record */
+  const void *scores;          /* [tokens, slots] (scores_dtype) or NULL */
+  void *output;                /* [tokens, hidden] bf16 (combined) */
+  uint32_t tokens;
+  uint32_t slots;
+  uint32_t hidden_size;
+  uint32_t inter_size;
+  uint32_t expert_count;       /* experts in the *_weight arrays */
+  /* extensions */
+  uint32_t group_size;         /* 32 or 64 */
+  uint32_t x_dtype;            /* FNMOE_DTYPE_BF16 */
+  uint32_t scores_dtype;       /* FNMOE_DTYPE_F32 or FNMOE_DTYPE_BF16 */
+  uint32_t reserved0;
+  const void *shared_y;        /* [tokens, hidden] bf16 or NULL */
+  const void *shared;          /* [tokens, hidden] bf16 or NULL (with shared_gate) */
+  const void *shared_gate;     /* [tokens] bf16 or NULL */
+  FnExpertTable table;         /* base NULL = no table */
+  /* Optional records for routes WITHOUT bit 31 (the reference's stream pack,
+   * metal_runtime.py:202-207): when base != NULL such a route r addresses
+   * record r of this table instead of the *_weight arrays. */
+  FnExpertTable stream_table;
+  void *gate_out;              /* RETURN_ALL: [tokens, slots, inter] bf16 */
+  void *up_out;                /* RETURN_ALL: [tokens, slots, inter] bf16 */
+  void *down_out;              /* RETURN_ALL / NO_COMBINE: [tokens, slots, hidden] bf16 */
+  void *workspace;
+  uint64_t workspace_bytes;
+} FnMoEArgs;
+
+/* A whole sparse-MoE block: router -> top-k -> renorm -> routed experts +
+ * sigmoid-gated shared expert -> combine. */
+typedef struct FnMoELayerArgs {
+  uint32_t abi_version;
+  uint32_t top_k;
+  const void *x;               /* [tokens, hidden] bf16 */
+  const void *router_weight;   /* [experts, hidden] bf16 */
+  float renorm_blend;          /* 1.0 = shipped renorm */
+  uint32_t tokens;
+  uint32_t hidden_size;
+  uint32_t inter_size;         /* routed expert intermediate */
+  uint32_t expert_count;
+  uint32_t group_size;
+  uint32_t shared_inter_size;  /* 0 = no shared expert */
+  const uint32_t *gate_weight; const void *gate_scales; const void *gate_biases;
+  const uint32_t *up_weight; const void *up_scales; const void *up_biases;
+  const uint32_t *down_weight; const void *down_scales; const void *down_biases;
+  const uint32_t *shared_gate_weight; const void *shared_gate_scales; const void *shared_gate_biases;
+  const uint32_t *shared_up_weight; const void *shared_up_scales; const void *shared_up_biases;
+  const uint32_t *shared_down_weight; const void *shared_down_scales; const void *shared_down_biases;
+  const void *shared_expert_gate; /* [hidden] bf16 (w_g of sigmoid(x.w_g)) */
+  FnExpertTable table;         /* when base != NULL, experts come from the table */
+  const uint32_t *table_routes_of_expert; /* [expert_count] route per expert, or NULL */
+  void *output;                /* [tokens, hidden] bf16 */
+  void *logits_out;            /* optional [tokens, experts] bf16 */
+  uint32_t *inds_out;          /* optional [tokens, top_k] */
+  void *scores_out;            /* optional [tokens, top_k] bf16 (renormalised) */
+  void *workspace;
+  uint64_t workspace_bytes;
+} FnMoELayerArgs;
+
+/* Paged-KV decode attention (one query token per sequence). */
+typedef struct FnPagedArgs {
+  uint32_t abi_version;
+  uint32_t batch;              /* sequences */
+  uint32_t q_heads;
+  uint32_t kv_heads;
+  uint32_t head_dim;           /* 64..256, multiple of 64 */
+  uint32_t page_size;          /* tokens per page */
+  uint32_t max_pages;          /* block_table row length */
+  uint32_t num_pages;          /* physical pages in k/v caches */
+  float scale;
+  uint32_t split_tokens;       /* tokens per split-K chunk (multiple of page_size) */
+  const void *q;               /* [batch, q_heads, head_dim] bf16 */
+  const void *k_cache;         /* [num_pages, page_size, kv_heads, head_dim] bf16 */
+  const void *v_cache;
+  const int32_t *block_table;  /* [batch, max_pages] */
+  const int32_t *context_lens; /* [batch] */
+  void *out;                   /* [batch, q_heads, head_dim] bf16 */
+  void *workspace;
+  uint64_t workspace_bytes;
+} FnPagedArgs;
+
+/* 1 when an sm_100 device is current and the library initialised, else 0.
+ * Replaces flashnext_native_available (metal_runtime_native.mm:196-201). */
+FNMOE_API int fnmoe_available(void);
+
+/* Copy the calling thread's last error message (NUL-terminated).
+ * Replaces flashnext_native_get_last_error (metal_runtime_native.mm:203-209). */
+FNMOE_API int fnmoe_get_last_error(char *buf, uint32_t max_len);
+
+/* FNMOE_ABI_VERSION of the loaded library. */
+FNMOE_API uint32_t fnmoe_abi_version(void);
+
+/* Workspace bytes fnmoe_moe_execute needs for these sizes. */
+FNMOE_API int fnmoe_moe_workspace_size(const FnMoEArgs *args, uint64_t *bytes);
+
+/* Executor: replaces flashnext_native_moe_execute (metal_runtime_native.mm:258)
+ * and MetalMoEExecutor.execute's packed path (metal_runtime.py:764-932). */
+FNMOE_API int fnmoe_moe_execute(const FnMoEArgs *args, void *stream);
+
+/* Combine-only probe: out[t,h] = sum_s outputs[t,s,h]*scores[t,s] (float32),
+ * or outputs[t, routes[t,s], h] when experts > 0 (metal_runtime.py:145-191). */
+FNMOE_API int fnmoe_weighted_combine(const float *outputs, const int32_t *routes,
+                           const float *scores, float *out, uint32_t tokens,
+                           uint32_t slots, uint32_t experts, uint32_t hidden,
+                           void *stream);
+
+/* Router chain: logits = bf16(x W^T); softmax (precise) -> top-k (ties to the
+ * lower expert) -> renorm.  Writes inds [tokens,k] (uint32), scores [tokens,k]
+ * bf16 (renormalised), mass [tokens] bf16 (top-k mass) and optionally logits. */
+FNMOE_API int fnmoe_router_topk(const void *x, const void *router_weight, uint32_t tokens,
+                      uint32_t hidden, uint32_t experts, uint32_t top_k,
+                      float renorm_blend, uint32_t *inds, void *scores,
+                      void *mass, void *logits, void *stream);
+
+/* Softmax (precise) -> top-k -> renorm on given bf16 logits [tokens, experts]
+ * (compiled.router + compiled.renorm, compiled.py:61-71,96-112).  raw_scores
+ * (optional) receives the un-normalised top-k probabilities, scores
+ * (optional) the renormalised ones. */
+FNMOE_API int fnmoe_softmax_topk(const void *logits, uint32_t tokens, uint32_t experts,
+                                 uint32_t top_k, float renorm_blend, uint32_t *inds,
+                                 void *raw_scores, void *scores, void *mass, void *stream);
+
+/* Stable grouping of routes by key: counts [n_keys], offsets [n_keys+1],
+ * order [tokens*slots] (pair indices sorted by key).  Routes with bit 31 map
+ * to key array_experts + (route & 0x7FFFFFFF). */
+FNMOE_API int fnmoe_group_tokens(const uint32_t *routes, uint32_t pairs,
+                       uint32_t array_experts, uint32_t table_records,
+                       int32_t *counts, int32_t *offsets, int32_t *order,
+                       void *workspace, uint64_t workspace_bytes, void *stream);
+
+FNMOE_API int fnmoe_moe_layer_workspace_size(const FnMoELayerArgs *args, uint64_t *bytes);
+FNMOE_API int fnmoe_moe_layer(const FnMoELayerArgs *args, void *stream);
+
+/* Affine Q4 dequantisation to bf16: out[r, k] = bf16(s*q + b), rounded once. */
+FNMOE_API int fnmoe_dequantize(const uint32_t *weight, const void *scales,
+                     const void *biases, void *out, uint64_t rows,
+                     uint32_t in_width, uint32_t group_size, void *stream);
+
+/* Elementwise bf16 SwiGLU: out = (g*sigmoid(g))*u, one rounding per op. */
+FNMOE_API int fnmoe_swiglu(const void *gate, const void *up, void *out, uint64_t n,
+                 void *stream);
+
+FNMOE_API int fnmoe_paged_decode_workspace_size(const FnPagedArgs *args, uint64_t *bytes);
+FNMOE_API int fnmoe_paged_decode(const FnPagedArgs *args, void *stream);
+
+/* Device error word of the library: bit 0 = an out-of-range route was
+ * skipped, bit 1 = a non-finite activation reached the fixed-point stage.
+ * Reading synchronises the device; `clear` resets it. */
+FNMOE_API int fnmoe_read_device_errors(uint32_t *flags, int clear);
+
+/* Per-kernel device timing for benchmarks: while enabled, every kernel the
+ * library launches is bracketed by CUDA events on its stream.
+ * fnmoe_profile_read synchronises those events and writes
+ * "name count total_ms\n" lines for each kernel into buf. */
+FNMOE_API int fnmoe_profile_enable(int on);
+FNMOE_API int fnmoe_profile_read(char *buf, uint32_t max_len, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FNMOE_H */

@@ -1,0 +1,641 @@
+// api.cu -- extern "C" entry points of libfnmoe (declared in include/fnmoe.h).
+//
+// Host-side responsibilities: argument validation (mirroring the checks of
+// MetalMoEExecutor.execute, metal_runtime.py:803-859), workspace carving and
+// kernel sequencing on the caller's stream.  No entry point allocates device
+// memory; none synchronises except fnmoe_available (first use per device) and
+// fnmoe_read_device_errors.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/fnmoe.h"
+#include "attention.cuh"
+#include "moe_kernels.cuh"
+
+using namespace fnmoe;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+// ---- optional per-kernel event timing (fnmoe_profile_*) ----
+struct ProfRecord {
+  const char *name;
+  cudaEvent_t start, stop;
+};
+std::mutex g_prof_mutex;
+bool g_prof_on = false;
+std::vector<ProfRecord> g_prof;
+
+struct Prof {
+  ProfRecord rec{};
+  cudaStream_t s;
+  bool on;
+  Prof(const char *name, cudaStream_t stream) : s(stream) {
+    std::lock_guard<std::mutex> lock(g_prof_mutex);
+    on = g_prof_on;
+    if (!on) return;
+    rec.name = name;
+    cudaEventCreate(&rec.start);
+    cudaEventCreate(&rec.stop);
+    cudaEventRecord(rec.start, s);
+  }
+  ~Prof() {
+    if (!on) return;
+    cudaEventRecord(rec.stop, s);
+    std::lock_guard<std::mutex> lock(g_prof_mutex);
+    g_prof.push_back(rec);
+  }
+};
+
+int fail(int code, const std::string &msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *where) {
+  return fail(FNMOE_ERR_LAUNCH, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+// Bump allocator over the caller's workspace (or a size probe when base is
+// null).  Every carve is 256-byte aligned.
+struct Carver {
+  uint8_t *base;
+  uint64_t off = 0;
+  explicit Carver(void *b) : base(static_cast<uint8_t *>(b)) {}
+  template <typename T>
+  T *take(uint64_t count) {
+    off = (off + 255) & ~uint64_t(255);
+    T *p = base ? reinterpret_cast<T *>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+bool device_ok(std::string &why) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    why = "no CUDA device";
+    return false;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int major = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) {
+    why = "device is not sm_100 (compute capability " + std::to_string(major) + ".x)";
+    return false;
+  }
+  return true;
+}
+
+struct Layout {
+  // activations
+  uint16_t *xl;
+  float4 *xm;
+  // grouping
+  GroupView gv;
+  // intermediates
+  uint16_t *act;
+  uint16_t *al;
+  float4 *am;
+  uint16_t *d;
+};
+
+// Carve the shared part of the executor / layer workspace.
+void carve_core(Carver &cv, Layout &L, int T, int H, int I, int G, int n_total, int n_bins,
+                bool need_d) {
+  const int Gh = H / G, Gi = I / G;
+  L.xl = cv.take<uint16_t>(static_cast<uint64_t>(T) * Gh * 2 * G);
+  L.xm = cv.take<float4>(static_cast<uint64_t>(T) * Gh);
+  L.gv.n_bins = n_bins;
+  L.gv.max_tiles = n_total / kTokPerItem + (n_bins < n_total ? n_bins : n_total) + 1;
+  L.gv.counts = cv.take<int32_t>(n_bins);
+  L.gv.offsets = cv.take<int32_t>(static_cast<uint64_t>(n_bins) + 1);
+  L.gv.order = cv.take<int32_t>(n_total);
+  L.gv.tiles = cv.take<int4>(L.gv.max_tiles);
+  L.gv.n_tiles = cv.take<int32_t>(1);
+  L.gv.bin_key = cv.take<uint32_t>(n_bins);
+  L.act = cv.take<uint16_t>(static_cast<uint64_t>(n_total) * I);
+  L.al = cv.take<uint16_t>(static_cast<uint64_t>(n_total) * Gi * 2 * G);
+  L.am = cv.take<float4>(static_cast<uint64_t>(n_total) * Gi);
+  L.d = need_d ? cv.take<uint16_t>(static_cast<uint64_t>(n_total) * H) : nullptr;
+}
+
+constexpr int kMaxBins = 16384;
+
+// Range of route values without bit 31: stream-pack records or array experts.
+uint32_t non_slot_keys(const FnMoEArgs *a) {
+  if (a->stream_table.base != nullptr) return a->stream_table.records;
+  return a->gate_weight != nullptr ? a->expert_count : 0u;
+}
+constexpr uint32_t kMaxTopK = 16;
+
+int validate_moe(const FnMoEArgs *a) {
+  if (a == nullptr) return fail(FNMOE_ERR_NULL, "args is NULL");
+  if (a->abi_version != FNMOE_ABI_VERSION)
+    return fail(FNMOE_ERR_ABI, "abi_version mismatch: library " + std::to_string(FNMOE_ABI_VERSION) +
+                                   ", caller " + std::to_string(a->abi_version));
+  if (a->tokens == 0 || a->slots == 0 || a->hidden_size == 0 || a->inter_size == 0)
+    return fail(FNMOE_ERR_SHAPE, "tokens, slots, hidden_size and inter_size must be positive");
+  if (a->group_size != 32 && a->group_size != 64)
+    return fail(FNMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64");
+  if (a->hidden_size % a->group_size || a->inter_size % a->group_size)
+    return fail(FNMOE_ERR_SHAPE, "Q4 projection inputs must be group aligned");
+  if (a->x_dtype != FNMOE_DTYPE_BF16)
+    return fail(FNMOE_ERR_UNSUPPORTED, "x must be bfloat16");
+  if (a->x == nullptr || a->routes == nullptr) return fail(FNMOE_ERR_NULL, "x and routes are required");
+  const bool has_table = a->table.base != nullptr;
+  const bool has_stream = a->stream_table.base != nullptr;
+  if (has_stream && !has_table) return fail(FNMOE_ERR_VALUE, "stream pack requires a resident slab pack");
+  if (!has_table && (a->gate_weight == nullptr || a->up_weight == nullptr || a->down_weight == nullptr))
+    return fail(FNMOE_ERR_NULL, "packed execution needs gate, up, and down projections");
+  if (a->gate_weight && (!a->gate_scales || !a->gate_biases || !a->up_scales || !a->up_biases ||
+                         !a->down_scales || !a->down_biases))
+    return fail(FNMOE_ERR_NULL, "Q4 projections need scales and biases");
+  if ((a->shared == nullptr) != (a->shared_gate == nullptr))
+    return fail(FNMOE_ERR_VALUE, "shared and shared_gate must be provided together");
+  if (a->shared_y != nullptr && a->shared != nullptr)
+    return fail(FNMOE_ERR_VALUE, "provide shared_y or shared parts, not both");
+  const bool ret_all = a->flags & FNMOE_FLAG_RETURN_ALL;
+  const bool per_slot = ret_all || (a->flags & FNMOE_FLAG_NO_COMBINE) || a->scores == nullptr;
+  if (ret_all && (!a->gate_out || !a->up_out || !a->down_out))
+    return fail(FNMOE_ERR_NULL, "return_all needs gate_out, up_out and down_out");
+  if (per_slot && !a->down_out) return fail(FNMOE_ERR_NULL, "per-slot execution needs down_out");
+  if (!per_slot && !a->output) return fail(FNMOE_ERR_NULL, "output is NULL");
+  if (!per_slot && a->scores_dtype != FNMOE_DTYPE_F32 && a->scores_dtype != FNMOE_DTYPE_BF16)
+    return fail(FNMOE_ERR_UNSUPPORTED, "scores must be float32 or bfloat16");
+  const uint64_t bins = static_cast<uint64_t>(non_slot_keys(a)) + (has_table ? a->table.records : 0);
+  if (bins == 0 || bins > kMaxBins)
+    return fail(FNMOE_ERR_SHAPE, "expert_count + table records must be in 1.." + std::to_string(kMaxBins));
+  if (static_cast<uint64_t>(a->tokens) * a->slots > (1u << 24))
+    return fail(FNMOE_ERR_SHAPE, "too many (token, slot) pairs");
+  return FNMOE_OK;
+}
+
+uint64_t moe_workspace(const FnMoEArgs *a) {
+  Carver cv(nullptr);
+  Layout L{};
+  const bool has_table = a->table.base != nullptr;
+  const int n_bins = static_cast<int>(non_slot_keys(a) + (has_table ? a->table.records : 0));
+  const int n_total = static_cast<int>(a->tokens * a->slots);
+  const bool per_slot = (a->flags & (FNMOE_FLAG_RETURN_ALL | FNMOE_FLAG_NO_COMBINE)) || a->scores == nullptr;
+  carve_core(cv, L, a->tokens, a->hidden_size, a->inter_size, a->group_size, n_total, n_bins, !per_slot);
+  return cv.off + 256;
+}
+
+ExpertCallArgs make_call(const FnMoEArgs *a) {
+  ExpertCallArgs c{};
+  c.gate = {a->gate_weight, static_cast<const uint16_t *>(a->gate_scales), static_cast<const uint16_t *>(a->gate_biases)};
+  c.up = {a->up_weight, static_cast<const uint16_t *>(a->up_scales), static_cast<const uint16_t *>(a->up_biases)};
+  c.down = {a->down_weight, static_cast<const uint16_t *>(a->down_scales), static_cast<const uint16_t *>(a->down_biases)};
+  c.sh_gate = c.sh_up = c.sh_down = {nullptr, nullptr, nullptr};
+  c.table.base = static_cast<const uint8_t *>(a->table.base);
+  c.table.header = a->table.header_bytes;
+  c.table.stride = a->table.record_stride;
+  for (int i = 0; i < 9; ++i) c.table.off[i] = a->table.part_offset[i];
+  c.table.records = a->table.base ? a->table.records : 0;
+  c.stream.base = static_cast<const uint8_t *>(a->stream_table.base);
+  c.stream.header = a->stream_table.header_bytes;
+  c.stream.stride = a->stream_table.record_stride;
+  for (int i = 0; i < 9; ++i) c.stream.off[i] = a->stream_table.part_offset[i];
+  c.stream.records = a->stream_table.base ? a->stream_table.records : 0;
+  c.array_experts = a->stream_table.base ? static_cast<int>(a->stream_table.records)
+                    : (a->gate_weight ? static_cast<int>(a->expert_count) : 0);
+  c.tokens = static_cast<int>(a->tokens);
+  c.slots = static_cast<int>(a->slots);
+  c.n_pairs = c.tokens * c.slots;
+  c.H = static_cast<int>(a->hidden_size);
+  c.I = static_cast<int>(a->inter_size);
+  c.I_shared = c.I;
+  c.G = static_cast<int>(a->group_size);
+  return c;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fnmoe_available(void) {
+  std::string why;
+  if (!device_ok(why)) {
+    g_last_error = why;
+    return 0;
+  }
+  cudaError_t e = ensure_exp_table(0);
+  if (e != cudaSuccess) {
+    g_last_error = std::string("initialisation failed: ") + cudaGetErrorString(e);
+    return 0;
+  }
+  return 1;
+}
+
+int fnmoe_get_last_error(char *buf, uint32_t max_len) {
+  if (buf == nullptr || max_len == 0) return FNMOE_ERR_NULL;
+  std::strncpy(buf, g_last_error.c_str(), max_len - 1);
+  buf[max_len - 1] = '\0';
+  return FNMOE_OK;
+}
+
+uint32_t fnmoe_abi_version(void) { return FNMOE_ABI_VERSION; }
+
+int fnmoe_moe_workspace_size(const FnMoEArgs *args, uint64_t *bytes) {
+  if (bytes == nullptr) return fail(FNMOE_ERR_NULL, "bytes is NULL");
+  const int v = validate_moe(args);
+  if (v != FNMOE_OK) return v;
+  *bytes = moe_workspace(args);
+  return FNMOE_OK;
+}
+
+int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
+  const int v = validate_moe(a);
+  if (v != FNMOE_OK) return v;
+  std::string why;
+  if (!device_ok(why)) return fail(FNMOE_ERR_DEVICE, why);
+  const uint64_t need = moe_workspace(a);
+  if (a->workspace == nullptr || a->workspace_bytes < need)
+    return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = ensure_exp_table(s);
+  if (e != cudaSuccess) return cuda_fail(e, "exp table");
+
+  const bool has_table = a->table.base != nullptr;
+  const bool ret_all = a->flags & FNMOE_FLAG_RETURN_ALL;
+  const bool per_slot = ret_all || (a->flags & FNMOE_FLAG_NO_COMBINE) || a->scores == nullptr;
+  const int T = static_cast<int>(a->tokens), S = static_cast<int>(a->slots);
+  const int H = static_cast<int>(a->hidden_size), I = static_cast<int>(a->inter_size);
+  const int G = static_cast<int>(a->group_size);
+  const int n_pairs = T * S;
+  const int n_bins = static_cast<int>(non_slot_keys(a) + (has_table ? a->table.records : 0));
+  Carver cv(a->workspace);
+  Layout L{};
+  carve_core(cv, L, T, H, I, G, n_pairs, n_bins, !per_slot);
+  uint16_t *d = per_slot ? static_cast<uint16_t *>(a->down_out) : L.d;
+  ExpertCallArgs call = make_call(a);
+
+  {
+    Prof p("prep_x", s);
+    e = launch_prep_rows(static_cast<const uint16_t *>(a->x), T, H, G, L.xl, L.xm, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "prep x");
+  {
+    Prof p("group", s);
+    e = launch_group(a->routes, n_pairs, 0, call.array_experts, static_cast<int>(call.table.records), L.gv, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "group");
+  {
+    Prof p("gate_up", s);
+    e = launch_gate_up(call, L.gv, L.xl, L.xm, L.act,
+                       ret_all ? static_cast<uint16_t *>(a->gate_out) : nullptr,
+                       ret_all ? static_cast<uint16_t *>(a->up_out) : nullptr, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "gate_up");
+  {
+    Prof p("prep_act", s);
+    e = launch_prep_rows(L.act, n_pairs, I, G, L.al, L.am, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "prep act");
+  {
+    Prof p("down", s);
+    e = launch_down(call, L.gv, L.al, L.am, d, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "down");
+  if (per_slot) return FNMOE_OK;
+  int mode = kCombineNone;
+  if (a->shared_y) mode = kCombineSharedY;
+  else if (a->shared) mode = kCombineParts;
+  {
+    Prof p("combine", s);
+    e = launch_combine(d, a->routes, a->scores, a->scores_dtype == FNMOE_DTYPE_F32, T, S, H, mode,
+                       static_cast<const uint16_t *>(a->shared_y), static_cast<const uint16_t *>(a->shared),
+                       static_cast<const uint16_t *>(a->shared_gate), call.array_experts,
+                       static_cast<int>(call.table.records), static_cast<uint16_t *>(a->output), s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "combine");
+  return FNMOE_OK;
+}
+
+int fnmoe_weighted_combine(const float *outputs, const int32_t *routes, const float *scores,
+                           float *out, uint32_t tokens, uint32_t slots, uint32_t experts,
+                           uint32_t hidden, void *stream) {
+  if (!outputs || !scores || !out || (experts > 0 && !routes))
+    return fail(FNMOE_ERR_NULL, "outputs, scores, out (and routes when experts > 0) are required");
+  if (tokens == 0 || slots == 0 || hidden == 0) return fail(FNMOE_ERR_SHAPE, "empty combine");
+  cudaError_t e = launch_weighted_combine(outputs, routes, scores, out, tokens, slots, experts,
+                                          hidden, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FNMOE_OK : cuda_fail(e, "weighted_combine");
+}
+
+int fnmoe_router_topk(const void *x, const void *router_weight, uint32_t tokens, uint32_t hidden,
+                      uint32_t experts, uint32_t top_k, float renorm_blend, uint32_t *inds,
+                      void *scores, void *mass, void *logits, void *stream) {
+  if (!x || !router_weight || !inds || !scores || !logits)
+    return fail(FNMOE_ERR_NULL, "x, router_weight, inds, scores and logits are required");
+  if (tokens == 0 || hidden == 0 || hidden % 8) return fail(FNMOE_ERR_SHAPE, "hidden must be a positive multiple of 8");
+  if (hidden > 4096) return fail(FNMOE_ERR_SHAPE, "hidden must be <= 4096");
+  if (experts == 0 || experts > 1024) return fail(FNMOE_ERR_SHAPE, "experts must be in 1..1024");
+  if (top_k == 0 || top_k > kMaxTopK || top_k > experts) return fail(FNMOE_ERR_VALUE, "top_k out of range");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = ensure_exp_table(s);
+  if (e != cudaSuccess) return cuda_fail(e, "exp table");
+  e = launch_router_logits(static_cast<const uint16_t *>(x), static_cast<const uint16_t *>(router_weight),
+                           tokens, hidden, experts, nullptr, static_cast<uint16_t *>(logits), nullptr, s);
+  if (e != cudaSuccess) return cuda_fail(e, "router logits");
+  // `inds` doubles as the route output (identity mapping).
+  e = launch_softmax_topk(static_cast<const uint16_t *>(logits), tokens, experts, top_k, renorm_blend,
+                          nullptr, 0, inds, inds, nullptr, static_cast<uint16_t *>(scores),
+                          static_cast<uint16_t *>(mass), nullptr, nullptr, s);
+  return e == cudaSuccess ? FNMOE_OK : cuda_fail(e, "softmax_topk");
+}
+
+int fnmoe_softmax_topk(const void *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
+                       float renorm_blend, uint32_t *inds, void *raw_scores, void *scores, void *mass,
+                       void *stream) {
+  if (!logits || !inds || (!scores && !raw_scores))
+    return fail(FNMOE_ERR_NULL, "logits, inds and raw_scores or scores are required");
+  if (tokens == 0) return fail(FNMOE_ERR_SHAPE, "tokens must be positive");
+  if (experts == 0 || experts > 1024) return fail(FNMOE_ERR_SHAPE, "experts must be in 1..1024");
+  if (top_k == 0 || top_k > kMaxTopK || top_k > experts) return fail(FNMOE_ERR_VALUE, "top_k out of range");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = ensure_exp_table(s);
+  if (e != cudaSuccess) return cuda_fail(e, "exp table");
+  e = launch_softmax_topk(static_cast<const uint16_t *>(logits), tokens, experts, top_k, renorm_blend,
+                          nullptr, 0, inds, inds, static_cast<uint16_t *>(raw_scores),
+                          static_cast<uint16_t *>(scores), static_cast<uint16_t *>(mass), nullptr,
+                          nullptr, s);
+  return e == cudaSuccess ? FNMOE_OK : cuda_fail(e, "softmax_topk");
+}
+
+int fnmoe_group_tokens(const uint32_t *routes, uint32_t pairs, uint32_t array_experts,
+                       uint32_t table_records, int32_t *counts, int32_t *offsets, int32_t *order,
+                       void *workspace, uint64_t workspace_bytes, void *stream) {
+  if (!routes || !counts || !offsets || !order) return fail(FNMOE_ERR_NULL, "routes, counts, offsets, order required");
+  const uint64_t bins = static_cast<uint64_t>(array_experts) + table_records;
+  if (pairs == 0 || bins == 0 || bins > kMaxBins) return fail(FNMOE_ERR_SHAPE, "invalid pairs or key count");
+  const int n_bins = static_cast<int>(bins);
+  GroupView gv{};
+  gv.n_bins = n_bins;
+  gv.max_tiles = static_cast<int>(pairs) / kTokPerItem + (n_bins < static_cast<int>(pairs) ? n_bins : static_cast<int>(pairs)) + 1;
+  Carver cv(workspace);
+  gv.tiles = cv.take<int4>(gv.max_tiles);
+  gv.n_tiles = cv.take<int32_t>(1);
+  gv.bin_key = cv.take<uint32_t>(n_bins);
+  if (workspace == nullptr || workspace_bytes < cv.off)
+    return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(cv.off) + " bytes");
+  gv.counts = counts;
+  gv.offsets = offsets;
+  gv.order = order;
+  cudaError_t e = launch_group(routes, static_cast<int>(pairs), 0, static_cast<int>(array_experts),
+                               static_cast<int>(table_records), gv, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FNMOE_OK : cuda_fail(e, "group");
+}
+
+namespace {
+
+int validate_layer(const FnMoELayerArgs *a) {
+  if (a == nullptr) return fail(FNMOE_ERR_NULL, "args is NULL");
+  if (a->abi_version != FNMOE_ABI_VERSION) return fail(FNMOE_ERR_ABI, "abi_version mismatch");
+  if (!a->x || !a->router_weight || !a->output) return fail(FNMOE_ERR_NULL, "x, router_weight and output are required");
+  if (a->tokens == 0 || a->hidden_size == 0 || a->inter_size == 0) return fail(FNMOE_ERR_SHAPE, "empty layer");
+  if (a->group_size != 32 && a->group_size != 64) return fail(FNMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64");
+  if (a->hidden_size % a->group_size || a->inter_size % a->group_size)
+    return fail(FNMOE_ERR_SHAPE, "Q4 projection inputs must be group aligned");
+  if (a->hidden_size > 4096) return fail(FNMOE_ERR_SHAPE, "hidden must be <= 4096");
+  if (a->expert_count == 0 || a->expert_count > 1024) return fail(FNMOE_ERR_SHAPE, "expert_count must be in 1..1024");
+  if (a->top_k == 0 || a->top_k > kMaxTopK || a->top_k > a->expert_count) return fail(FNMOE_ERR_VALUE, "top_k out of range");
+  const bool has_table = a->table.base != nullptr;
+  if (!has_table && (!a->gate_weight || !a->up_weight || !a->down_weight))
+    return fail(FNMOE_ERR_NULL, "routed experts need gate, up and down projections or a table");
+  if (a->shared_inter_size) {
+    if (a->shared_inter_size != a->inter_size)
+      return fail(FNMOE_ERR_UNSUPPORTED, "shared expert intermediate must equal the routed intermediate");
+    if (!a->shared_gate_weight || !a->shared_up_weight || !a->shared_down_weight || !a->shared_expert_gate)
+      return fail(FNMOE_ERR_NULL, "shared expert needs gate, up, down and its sigmoid gate weight");
+  }
+  const uint64_t bins = (has_table ? a->table.records : a->expert_count) + 1ull;
+  if (bins > kMaxBins) return fail(FNMOE_ERR_SHAPE, "too many experts/records");
+  return FNMOE_OK;
+}
+
+struct LayerLayout {
+  Layout core;
+  uint16_t *logits, *shared_logit, *shared_gate, *scores, *mass;
+  uint32_t *inds, *routes;
+};
+
+uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL) {
+  Carver cv(base);
+  const int T = a->tokens, k = a->top_k, E = a->expert_count;
+  const bool has_table = a->table.base != nullptr;
+  const bool shared = a->shared_inter_size != 0;
+  const int n_pairs = T * k;
+  const int n_total = n_pairs + (shared ? T : 0);
+  const int array_experts = has_table ? 0 : E;
+  const int records = has_table ? static_cast<int>(a->table.records) : 0;
+  const int n_bins = array_experts + records + (shared ? 1 : 0);
+  LL.logits = cv.take<uint16_t>(static_cast<uint64_t>(T) * E);
+  LL.shared_logit = cv.take<uint16_t>(T);
+  LL.shared_gate = cv.take<uint16_t>(T);
+  LL.scores = cv.take<uint16_t>(static_cast<uint64_t>(T) * k);
+  LL.mass = cv.take<uint16_t>(T);
+  LL.inds = cv.take<uint32_t>(static_cast<uint64_t>(T) * k);
+  LL.routes = cv.take<uint32_t>(static_cast<uint64_t>(T) * k);
+  carve_core(cv, LL.core, T, a->hidden_size, a->inter_size, a->group_size, n_total, n_bins, true);
+  return cv.off + 256;
+}
+
+}  // namespace
+
+int fnmoe_moe_layer_workspace_size(const FnMoELayerArgs *args, uint64_t *bytes) {
+  if (bytes == nullptr) return fail(FNMOE_ERR_NULL, "bytes is NULL");
+  const int v = validate_layer(args);
+  if (v != FNMOE_OK) return v;
+  LayerLayout LL{};
+  *bytes = carve_layer(args, nullptr, LL);
+  return FNMOE_OK;
+}
+
+int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
+  const int v = validate_layer(a);
+  if (v != FNMOE_OK) return v;
+  std::string why;
+  if (!device_ok(why)) return fail(FNMOE_ERR_DEVICE, why);
+  LayerLayout LL{};
+  const uint64_t need = carve_layer(a, nullptr, LL);
+  if (a->workspace == nullptr || a->workspace_bytes < need)
+    return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes");
+  carve_layer(a, a->workspace, LL);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = ensure_exp_table(s);
+  if (e != cudaSuccess) return cuda_fail(e, "exp table");
+
+  const int T = a->tokens, k = a->top_k, E = a->expert_count;
+  const int H = a->hidden_size, I = a->inter_size, G = a->group_size;
+  const bool has_table = a->table.base != nullptr;
+  const bool shared = a->shared_inter_size != 0;
+  const int n_pairs = T * k;
+
+  ExpertCallArgs call{};
+  call.gate = {a->gate_weight, static_cast<const uint16_t *>(a->gate_scales), static_cast<const uint16_t *>(a->gate_biases)};
+  call.up = {a->up_weight, static_cast<const uint16_t *>(a->up_scales), static_cast<const uint16_t *>(a->up_biases)};
+  call.down = {a->down_weight, static_cast<const uint16_t *>(a->down_scales), static_cast<const uint16_t *>(a->down_biases)};
+  call.sh_gate = {a->shared_gate_weight, static_cast<const uint16_t *>(a->shared_gate_scales), static_cast<const uint16_t *>(a->shared_gate_biases)};
+  call.sh_up = {a->shared_up_weight, static_cast<const uint16_t *>(a->shared_up_scales), static_cast<const uint16_t *>(a->shared_up_biases)};
+  call.sh_down = {a->shared_down_weight, static_cast<const uint16_t *>(a->shared_down_scales), static_cast<const uint16_t *>(a->shared_down_biases)};
+  call.table.base = static_cast<const uint8_t *>(a->table.base);
+  call.table.header = a->table.header_bytes;
+  call.table.stride = a->table.record_stride;
+  for (int i = 0; i < 9; ++i) call.table.off[i] = a->table.part_offset[i];
+  call.table.records = has_table ? a->table.records : 0;
+  call.array_experts = has_table ? 0 : E;
+  call.tokens = T;
+  call.slots = k;
+  call.n_pairs = n_pairs;
+  call.H = H;
+  call.I = I;
+  call.I_shared = shared ? static_cast<int>(a->shared_inter_size) : I;
+  call.G = G;
+
+  Layout &L = LL.core;
+  uint16_t *logits = a->logits_out ? static_cast<uint16_t *>(a->logits_out) : LL.logits;
+  uint32_t *inds = a->inds_out ? a->inds_out : LL.inds;
+  uint16_t *scores = a->scores_out ? static_cast<uint16_t *>(a->scores_out) : LL.scores;
+
+  {
+    Prof p("prep_x", s);
+    e = launch_prep_rows(static_cast<const uint16_t *>(a->x), T, H, G, L.xl, L.xm, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "prep x");
+  {
+    Prof p("router_logits", s);
+    e = launch_router_logits(static_cast<const uint16_t *>(a->x), static_cast<const uint16_t *>(a->router_weight),
+                             T, H, E, shared ? static_cast<const uint16_t *>(a->shared_expert_gate) : nullptr,
+                             logits, LL.shared_logit, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "router logits");
+  {
+    Prof p("softmax_topk", s);
+    e = launch_softmax_topk(logits, T, E, k, a->renorm_blend, a->table_routes_of_expert, has_table ? 1 : 0,
+                            inds, LL.routes, nullptr, scores, LL.mass, shared ? LL.shared_logit : nullptr,
+                            shared ? LL.shared_gate : nullptr, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "softmax_topk");
+  {
+    Prof p("group", s);
+    e = launch_group(LL.routes, n_pairs, shared ? T : 0, call.array_experts,
+                     static_cast<int>(call.table.records), L.gv, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "group");
+  {
+    Prof p("gate_up", s);
+    e = launch_gate_up(call, L.gv, L.xl, L.xm, L.act, nullptr, nullptr, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "gate_up");
+  {
+    Prof p("prep_act", s);
+    e = launch_prep_rows(L.act, n_pairs + (shared ? T : 0), I, G, L.al, L.am, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "prep act");
+  {
+    Prof p("down", s);
+    e = launch_down(call, L.gv, L.al, L.am, L.d, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "down");
+  {
+    Prof p("combine", s);
+    e = launch_combine(L.d, LL.routes, scores, 0, T, k, H, shared ? kCombineParts : kCombineNone, nullptr,
+                       shared ? L.d + static_cast<size_t>(n_pairs) * H : nullptr,
+                       shared ? LL.shared_gate : nullptr, call.array_experts,
+                       static_cast<int>(call.table.records), static_cast<uint16_t *>(a->output), s);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "combine");
+  return FNMOE_OK;
+}
+
+int fnmoe_dequantize(const uint32_t *weight, const void *scales, const void *biases, void *out,
+                     uint64_t rows, uint32_t in_width, uint32_t group_size, void *stream) {
+  if (!weight || !scales || !biases || !out) return fail(FNMOE_ERR_NULL, "dequantize needs all pointers");
+  if (group_size != 32 && group_size != 64) return fail(FNMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64");
+  if (in_width == 0 || in_width % group_size) return fail(FNMOE_ERR_SHAPE, "in_width must be group aligned");
+  cudaError_t e = launch_dequant(weight, static_cast<const uint16_t *>(scales), static_cast<const uint16_t *>(biases),
+                                 static_cast<uint16_t *>(out), rows, in_width, group_size,
+                                 static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FNMOE_OK : cuda_fail(e, "dequantize");
+}
+
+int fnmoe_swiglu(const void *gate, const void *up, void *out, uint64_t n, void *stream) {
+  if (!gate || !up || !out) return fail(FNMOE_ERR_NULL, "swiglu needs gate, up and out");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = ensure_exp_table(s);
+  if (e != cudaSuccess) return cuda_fail(e, "exp table");
+  e = launch_swiglu(static_cast<const uint16_t *>(gate), static_cast<const uint16_t *>(up),
+                    static_cast<uint16_t *>(out), n, s);
+  return e == cudaSuccess ? FNMOE_OK : cuda_fail(e, "swiglu");
+}
+
+int fnmoe_read_device_errors(uint32_t *flags, int clear) {
+  if (flags == nullptr) return fail(FNMOE_ERR_NULL, "flags is NULL");
+  uint32_t *p = device_error_word();
+  if (p == nullptr) return fail(FNMOE_ERR_DEVICE, "device error word unavailable");
+  cudaError_t e = cudaMemcpy(flags, p, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read device errors");
+  if (clear) {
+    e = cudaMemset(p, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "clear device errors");
+  }
+  return FNMOE_OK;
+}
+
+int fnmoe_profile_enable(int on) {
+  std::lock_guard<std::mutex> lock(g_prof_mutex);
+  g_prof_on = on != 0;
+  return FNMOE_OK;
+}
+
+int fnmoe_profile_read(char *buf, uint32_t max_len, int reset) {
+  if (buf == nullptr || max_len == 0) return fail(FNMOE_ERR_NULL, "buf is NULL");
+  std::lock_guard<std::mutex> lock(g_prof_mutex);
+  std::map<std::string, std::pair<int, double>> agg;
+  for (auto &r : g_prof) {
+    float ms = 0.0f;
+    if (cudaEventSynchronize(r.stop) == cudaSuccess && cudaEventElapsedTime(&ms, r.start, r.stop) == cudaSuccess) {
+      auto &v = agg[r.name];
+      v.first += 1;
+      v.second += ms;
+    }
+  }
+  std::string text;
+  for (auto &kv : agg) {
+    char line[160];
+    std::snprintf(line, sizeof(line), "%s %d %.6f\n", kv.first.c_str(), kv.second.first, kv.second.second);
+    text += line;
+  }
+  if (reset) {
+    for (auto &r : g_prof) {
+      cudaEventDestroy(r.start);
+      cudaEventDestroy(r.stop);
+    }
+    g_prof.clear();
+  }
+  std::strncpy(buf, text.c_str(), max_len - 1);
+  buf[max_len - 1] = '\0';
+  return FNMOE_OK;
+}
+
+int fnmoe_paged_decode_workspace_size(const FnPagedArgs *args, uint64_t *bytes) {
+  return paged_workspace_size(args, bytes, g_last_error);
+}
+
+int fnmoe_paged_decode(const FnPagedArgs *args, void *stream) {
+  return paged_decode(args, static_cast<cudaStream_t>(stream), g_last_error);
+}
+
+}  // extern "C"

@@ -1,0 +1,138 @@
+// common.cuh -- shared device helpers for the fnmoe sm_100a kernels.
+//
+// Rounding conventions (identical to the CPU oracle):
+//   * bfloat16 results are float32 results rounded to nearest even;
+//   * float32 arithmetic uses the explicit _rn intrinsics wherever the oracle
+//     fixes the operation order, so the compiler cannot contract to FMA;
+//   * exp() feeding bfloat16 is correctly rounded through a 64 Ki-entry table
+//     built once per device from double-precision exp().
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fnmoe {
+
+constexpr uint32_t kSlotBit = 0x80000000u;
+constexpr int kWarp = 32;
+
+// Device error word bits (fnmoe_read_device_errors).
+constexpr uint32_t kErrBadRoute = 1u;
+constexpr uint32_t kErrNonFinite = 2u;
+constexpr uint32_t kErrTimeout = 4u;
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__device__ __forceinline__ float round_bf16(float f) {
+  return bf16_to_f32(f32_to_bf16(f));
+}
+
+// double -> bfloat16 bits with a single rounding (nearest even).
+__device__ __forceinline__ uint16_t f64_to_bf16_once(double d) {
+  if (isnan(d)) return 0x7FC0u;
+  const uint64_t u = static_cast<uint64_t>(__double_as_longlong(d));
+  const uint16_t sign = static_cast<uint16_t>((u >> 48) & 0x8000u);
+  const double a = fabs(d);
+  // (2 - 2^-8) * 2^127: at or above it bfloat16 rounds to infinity.
+  if (a >= 0x1.FEp+127) return sign | 0x7F80u;
+  if (a >= 0x1p-126) {  // bfloat16 normal range
+    uint64_t bits = u & 0x7FFFFFFFFFFFFFFFull;
+    const uint64_t lsb = (bits >> 45) & 1ull;
+    bits += (1ull << 44) - 1ull + lsb;
+    bits &= ~((1ull << 45) - 1ull);
+    const float f = static_cast<float>(__longlong_as_double(static_cast<long long>(bits)));
+    return sign | static_cast<uint16_t>(__float_as_uint(f) >> 16);
+  }
+  // subnormal bfloat16: multiples of 2^-133.
+  const long long n = __double2ll_rn(a * 0x1p133);  // a * 2^133 (exact scaling)
+  return sign | static_cast<uint16_t>(n);
+}
+
+// exp() of a bfloat16 value rounded once to bfloat16, read from a 64 Ki-entry
+// table (built once per device by the translation unit that owns it).
+__device__ __forceinline__ float exp_bf16(const uint16_t *tab, float v) {
+  return bf16_to_f32(tab[f32_to_bf16(v)]);
+}
+
+// One bfloat16 operation: float32 op then round (Metal bfloat semantics).
+__device__ __forceinline__ float badd(float a, float b) { return round_bf16(__fadd_rn(a, b)); }
+__device__ __forceinline__ float bsub(float a, float b) { return round_bf16(__fsub_rn(a, b)); }
+__device__ __forceinline__ float bmul(float a, float b) { return round_bf16(__fmul_rn(a, b)); }
+__device__ __forceinline__ float bdiv(float a, float b) { return round_bf16(__fdiv_rn(a, b)); }
+
+// Stable bfloat16 sigmoid: |g| -> exp -> 1+e -> 1/d -> select
+// (metal_runtime.py:272-281).
+__device__ __forceinline__ float sigmoid_bf16(const uint16_t *tab, float g) {
+  const float mag = fabsf(g);
+  const float ex = exp_bf16(tab, mag);
+  const float den = badd(1.0f, ex);
+  const float small = bdiv(1.0f, den);
+  return (g < 0.0f) ? small : bsub(1.0f, small);
+}
+
+// (g * sigmoid(g)) * u, each op rounded to bfloat16 (metal_runtime.py:282).
+__device__ __forceinline__ float swiglu_bf16(const uint16_t *tab, float g, float u) {
+  return bmul(bmul(g, sigmoid_bf16(tab, g)), u);
+}
+
+// fl(t * 2^k), one rounding; `scale` = 2^k as float when k >= -126, else 0.
+__device__ __forceinline__ float scale_pow2(float t, float scale, int k) {
+  if (scale != 0.0f) return __fmul_rn(t, scale);
+  return __double2float_rn(static_cast<double>(t) * ldexp(1.0, k));
+}
+
+// m16n8k16 fp16 MMA, fp32 accumulate (exact here: all operands are small
+// integers and every partial sum stays below 2^24).
+__device__ __forceinline__ void mma_16816(float c[4], const uint32_t a[4],
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Nibbles j and j+4 of a packed word as an fp16x2 pair (low half = nibble j).
+// (w >> 4j) & 0x000F000F | 0x6400 6400 encodes 1024+q; subtracting 1024 is
+// exact in fp16.
+__device__ __forceinline__ uint32_t nibble_pair(uint32_t w, int j) {
+  const uint32_t v = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+  __half2 h = *reinterpret_cast<const __half2 *>(&v);
+  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+  h = __hsub2(h, k1024);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Load helpers with read-only caching.
+__device__ __forceinline__ uint32_t ldg_u32(const uint32_t *p) { return __ldg(p); }
+__device__ __forceinline__ uint16_t ldg_u16(const uint16_t *p) { return __ldg(p); }
+__device__ __forceinline__ uint4 ldg_u128(const uint4 *p) { return __ldg(p); }
+
+__device__ __forceinline__ void set_error(uint32_t *err, uint32_t bit) {
+  if (err) atomicOr(err, bit);
+}
+
+// Chains: P = min(4, 2^floor(log2 G)); chain of group g = (g*P)/G.
+__host__ __device__ __forceinline__ int chain_count(int groups) {
+  return groups >= 4 ? 4 : (groups >= 2 ? 2 : 1);
+}
+__host__ __device__ __forceinline__ int chain_begin(int chain, int P, int groups) {
+  // smallest g with (g*P)/groups >= chain  ->  ceil(chain*groups/P)
+  return (chain * groups + P - 1) / P;
+}
+
+__device__ __forceinline__ float chain_tree(const float c[4], int P) {
+  if (P == 4) return __fadd_rn(__fadd_rn(c[0], c[2]), __fadd_rn(c[1], c[3]));
+  if (P == 2) return __fadd_rn(c[0], c[1]);
+  return c[0];
+}
+
+}  // namespace fnmoe

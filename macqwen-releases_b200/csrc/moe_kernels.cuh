@@ -1,0 +1,112 @@
+// moe_kernels.cuh -- launch-side declarations shared by moe_kernels.cu and api.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fnmoe {
+
+// Key assigned to the shared expert's bin in grouping.
+constexpr uint32_t kSharedKey = 0xFFFFFFFFu;
+// Pairs per grouped work item (a multiple of the 4-token MMA tile).
+constexpr int kTokPerItem = 32;
+
+// Pointers of one Q4 projection family.
+struct ProjArrays {
+  const uint32_t *w;   // [experts, rows, cols/8]
+  const uint16_t *s;   // [experts, rows, cols/G]
+  const uint16_t *b;
+};
+
+// HBM-resident expert table (device view of FnExpertTable).
+struct TableView {
+  const uint8_t *base;
+  uint64_t header;
+  uint64_t stride;
+  uint64_t off[9];
+  uint32_t records;
+};
+
+// Grouping results living in the workspace.
+struct GroupView {
+  int32_t *counts;     // [n_bins]
+  int32_t *offsets;    // [n_bins + 1]
+  int32_t *order;      // [n_total]   pair ids sorted by bin
+  int4 *tiles;         // [max_tiles] {bin, start, len, 0}
+  int32_t *n_tiles;    // [1]
+  uint32_t *bin_key;   // [n_bins]    route key of each bin
+  int n_bins;
+  int max_tiles;
+};
+
+struct DeviceInfo {
+  int device;
+  int sms;
+};
+
+DeviceInfo device_info();
+cudaError_t ensure_exp_table(cudaStream_t stream);
+uint32_t *device_error_word();
+
+// Fixed-point limbs of bf16 rows: limbs [rows][groups][2][G] fp16 (fragment
+// order), meta [rows][groups] float4 {fl(SX), 2^k or 0, k, 0}.
+cudaError_t launch_prep_rows(const uint16_t *rows, int n_rows, int K, int G,
+                             uint16_t *limbs, float4 *meta, cudaStream_t s);
+
+// Stable counting-sort grouping of routes (+ optional shared bin).
+cudaError_t launch_group(const uint32_t *routes, int n_pairs, int shared_tokens,
+                         int array_experts, int table_records, GroupView gv,
+                         cudaStream_t s);
+
+struct ExpertCallArgs {
+  ProjArrays gate, up, down;          // routed arrays (may be null if table-only)
+  ProjArrays sh_gate, sh_up, sh_down; // shared expert (bin key kSharedKey)
+  TableView table;
+  TableView stream;                   // records for routes without bit 31 (optional)
+  int array_experts;                  // valid non-slot route range
+  int tokens, slots, n_pairs;         // n_pairs = tokens*slots (routed)
+  int H, I, I_shared, G;
+};
+
+// gate/up + SwiGLU over all grouped tiles -> act [n_total, I] bf16.
+cudaError_t launch_gate_up(const ExpertCallArgs &a, const GroupView &gv,
+                           const uint16_t *x_limbs, const float4 *x_meta,
+                           uint16_t *act, uint16_t *g_out, uint16_t *u_out,
+                           cudaStream_t s);
+// down projection -> d [n_total, H] bf16.
+cudaError_t launch_down(const ExpertCallArgs &a, const GroupView &gv,
+                        const uint16_t *act_limbs, const float4 *act_meta,
+                        uint16_t *d, cudaStream_t s);
+
+// Combine modes.
+enum CombineMode { kCombineNone = 0, kCombineSharedY = 1, kCombineParts = 2 };
+cudaError_t launch_combine(const uint16_t *d, const uint32_t *routes,
+                           const void *scores, int scores_f32, int tokens,
+                           int slots, int H, int mode, const uint16_t *shared_y,
+                           const uint16_t *shared, const uint16_t *shared_gate,
+                           int array_experts, int table_records,
+                           uint16_t *out, cudaStream_t s);
+
+// Router.
+cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T,
+                                 int H, int E, const uint16_t *w_shared_gate,
+                                 uint16_t *logits, uint16_t *shared_logit,
+                                 cudaStream_t s);
+cudaError_t launch_softmax_topk(const uint16_t *logits, int T, int E, int k,
+                                float blend, const uint32_t *route_map,
+                                int table_routes, uint32_t *inds,
+                                uint32_t *routes, uint16_t *raw_scores,
+                                uint16_t *scores, uint16_t *mass,
+                                const uint16_t *shared_logit,
+                                uint16_t *shared_gate, cudaStream_t s);
+
+cudaError_t launch_dequant(const uint32_t *w, const uint16_t *sc,
+                           const uint16_t *bi, uint16_t *out, uint64_t rows,
+                           int K, int G, cudaStream_t s);
+cudaError_t launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out,
+                          uint64_t n, cudaStream_t s);
+cudaError_t launch_weighted_combine(const float *outputs, const int32_t *routes,
+                                    const float *scores, float *out, int T,
+                                    int S, int E, int H, cudaStream_t s);
+
+}  // namespace fnmoe

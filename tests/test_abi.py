@@ -1,0 +1,111 @@
+"""The C-ABI library loads, exports every declared symbol, and its structs
+match the ctypes mirror (no GPU, no compute calls)."""
+from __future__ import annotations
+
+import ctypes
+import re
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from flashnext_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "fnmoe.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"FNMOE_API\s+\w+\s+(fnmoe_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_bound_surface():
+    assert set(declared_symbols()) == set(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\b(fnmoe_\w+)\b", out))
+    assert set(declared_symbols()) <= exported
+
+
+def test_abi_version_and_error_channel():
+    lib = _lib.load()
+    assert lib.fnmoe_abi_version() == _lib.ABI_VERSION
+    # argument validation runs before any device call
+    need = ctypes.c_uint64(0)
+    assert lib.fnmoe_moe_workspace_size(None, ctypes.byref(need)) == _lib.ERR_NULL
+    assert "NULL" in _lib.last_error(lib)
+    a = _lib.FnMoEArgs()
+    a.abi_version = 999
+    assert lib.fnmoe_moe_workspace_size(ctypes.byref(a), ctypes.byref(need)) == _lib.ERR_ABI
+    assert "abi_version" in _lib.last_error(lib)
+
+
+def _shapes_args(**kw):
+    a = _lib.FnMoEArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.tokens, a.slots, a.hidden_size, a.inter_size, a.expert_count = 2, 3, 64, 32, 4
+    a.group_size = 32
+    dummy = 0x1000
+    for f in ("x", "routes", "gate_weight", "gate_scales", "gate_biases", "up_weight", "up_scales",
+              "up_biases", "down_weight", "down_scales", "down_biases", "scores", "output"):
+        setattr(a, f, dummy)
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_workspace_size_and_validation_without_gpu():
+    lib = _lib.load()
+    need = ctypes.c_uint64(0)
+    assert lib.fnmoe_moe_workspace_size(ctypes.byref(_shapes_args()), ctypes.byref(need)) == _lib.OK
+    assert need.value > 0
+    assert lib.fnmoe_moe_workspace_size(ctypes.byref(_shapes_args(group_size=16)), ctypes.byref(need)) == \
+        _lib.ERR_UNSUPPORTED
+    assert lib.fnmoe_moe_workspace_size(ctypes.byref(_shapes_args(hidden_size=48)), ctypes.byref(need)) == \
+        _lib.ERR_SHAPE
+    bad = _shapes_args(shared=0x2000)
+    assert lib.fnmoe_moe_workspace_size(ctypes.byref(bad), ctypes.byref(need)) == _lib.ERR_VALUE
+    assert "shared_gate" in _lib.last_error(lib)
+
+
+C_PROBE = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "fnmoe.h"
+int main(void) {
+  printf("FnExpertTable %zu\n", sizeof(FnExpertTable));
+  printf("FnMoEArgs %zu %zu %zu %zu %zu\n", sizeof(FnMoEArgs), offsetof(FnMoEArgs, tokens),
+         offsetof(FnMoEArgs, table), offsetof(FnMoEArgs, stream_table), offsetof(FnMoEArgs, workspace));
+  printf("FnMoELayerArgs %zu %zu %zu\n", sizeof(FnMoELayerArgs), offsetof(FnMoELayerArgs, table),
+         offsetof(FnMoELayerArgs, workspace));
+  printf("FnPagedArgs %zu %zu\n", sizeof(FnPagedArgs), offsetof(FnPagedArgs, q));
+  return 0;
+}
+"""
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
+def test_struct_layout_matches_c_compiler(tmp_path):
+    src = tmp_path / "probe.c"
+    src.write_text(C_PROBE)
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    lines = dict(line.split(" ", 1) for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                                check=True).stdout.strip().splitlines())
+    s = ctypes.sizeof
+    assert int(lines["FnExpertTable"]) == s(_lib.FnExpertTable)
+    got = [int(v) for v in lines["FnMoEArgs"].split()]
+    assert got == [s(_lib.FnMoEArgs), _lib.FnMoEArgs.tokens.offset, _lib.FnMoEArgs.table.offset,
+                   _lib.FnMoEArgs.stream_table.offset, _lib.FnMoEArgs.workspace.offset]
+    got = [int(v) for v in lines["FnMoELayerArgs"].split()]
+    assert got == [s(_lib.FnMoELayerArgs), _lib.FnMoELayerArgs.table.offset, _lib.FnMoELayerArgs.workspace.offset]
+    got = [int(v) for v in lines["FnPagedArgs"].split()]
+    assert got == [s(_lib.FnPagedArgs), _lib.FnPagedArgs.q.offset]
