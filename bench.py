@@ -279,15 +279,17 @@ def gpu_arm(args):
 
     _lib.ensure_device()
     tokens = 64 if args.workload == "c2" else 1
-    blocks, xs = _build_layers(tokens, LAYERS, seed=17 + rank)
-    outs = [torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device="cuda") for _ in range(LAYERS)]
+    layers = max(1, args.layers)
+    blocks, xs = _build_layers(tokens, layers, seed=17 + rank)
+    outs = [torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device="cuda") for _ in range(layers)]
     stream = torch.cuda.current_stream()
 
     def step(i):
-        j = i % LAYERS
+        j = i % layers
         blocks[j](xs[j], out=outs[j])
 
-    for i in range(max(3, args.warmup)):
+    warm = max(3, args.warmup, layers)
+    for i in range(warm):
         step(i)
     torch.cuda.synchronize()
     used = [(_distinct_experts(b)) for b in blocks]
@@ -311,11 +313,11 @@ def gpu_arm(args):
 
     # e2e: pinned host batch -> device -> layer -> host, per step
     host_x = [x.cpu().pin_memory() for x in xs]
-    host_out = [torch.empty((tokens, HIDDEN), dtype=torch.bfloat16).pin_memory() for _ in range(LAYERS)]
+    host_out = [torch.empty((tokens, HIDDEN), dtype=torch.bfloat16).pin_memory() for _ in range(layers)]
     dev_x = [torch.empty_like(x) for x in xs]
 
     def e2e_step(i):
-        j = i % LAYERS
+        j = i % layers
         dev_x[j].copy_(host_x[j], non_blocking=True)
         blocks[j](dev_x[j], out=outs[j])
         host_out[j].copy_(outs[j], non_blocking=True)
@@ -353,7 +355,7 @@ def gpu_arm(args):
     step_s = ms / args.steps / 1000.0
 
     batch1 = None
-    if world == 1 and args.workload == "c2":
+    if world == 1 and args.workload == "c2" and not args.no_batch1:
         batch1 = batch1_numbers(hbm_peak)
 
     cpu = None
@@ -364,14 +366,14 @@ def gpu_arm(args):
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "warmup": warm, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {
                 "workload": "C2: one qwen4_exp MoE layer, 64-token ragged decode, Zipf(1.1) routing, "
                             "H2048/I512/E512 top-10 Q4/G32 + Q4/G32 shared expert" if tokens == 64 else
                             "C1: one MoE layer, batch-1 decode",
-                "tokens_per_gpu": tokens, "layers_rotated": LAYERS,
-                "l2": "inputs larger than L2: 4 distinct 1.0 GB layers rotated per step",
+                "tokens_per_gpu": tokens, "layers_rotated": layers,
+                "l2": f"inputs larger than L2: {layers} distinct 1.0 GB layers rotated per step",
                 "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                 "distinct_experts_per_layer": avg_used,
             },
@@ -444,6 +446,8 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c2", "c1"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="distinct layers rotated per step")
+    ap.add_argument("--no-batch1", action="store_true", help="skip the batch-1 CUDA-graph sub-measure")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return reference_arm(args)

@@ -83,10 +83,16 @@ __device__ __forceinline__ float swiglu_bf16(const uint16_t *tab, float g, float
   return bmul(bmul(g, sigmoid_bf16(tab, g)), u);
 }
 
+// fl(t * 2^k) for k < -126 (groups whose largest activation is below 2^-104),
+// kept out of line so the common path stays a single multiply.
+static __device__ __noinline__ float scale_pow2_slow(float t, int k) {
+  return __double2float_rn(static_cast<double>(t) * ldexp(1.0, k));
+}
+
 // fl(t * 2^k), one rounding; `scale` = 2^k as float when k >= -126, else 0.
 __device__ __forceinline__ float scale_pow2(float t, float scale, int k) {
   if (scale != 0.0f) return __fmul_rn(t, scale);
-  return __double2float_rn(static_cast<double>(t) * ldexp(1.0, k));
+  return scale_pow2_slow(t, k);
 }
 
 // m16n8k16 fp16 MMA, fp32 accumulate (exact here: all operands are small
@@ -109,6 +115,28 @@ __device__ __forceinline__ uint32_t nibble_pair(uint32_t w, int j) {
   const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
   h = __hsub2(h, k1024);
   return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// All four nibble pairs (j, j+4), j = 0..3, of a packed word as fp16x2.
+// Odd pairs are taken unshifted from bits 4-7 / 20-23: the encoded value is
+// 1024 + 16q, and 1024 + 16q scaled by 1/16 minus 64 is q exactly.
+__device__ __forceinline__ void nibble_pairs4(uint32_t w, uint32_t out[4]) {
+  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+  const __half2 k16th = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));  // 1/16
+  const __half2 km64 = __halves2half2(__ushort_as_half(0xD400), __ushort_as_half(0xD400));   // -64
+  const uint32_t w8 = w >> 8;
+  uint32_t v0 = (w & 0x000F000Fu) | 0x64006400u;
+  uint32_t v1 = (w & 0x00F000F0u) | 0x64006400u;
+  uint32_t v2 = (w8 & 0x000F000Fu) | 0x64006400u;
+  uint32_t v3 = (w8 & 0x00F000F0u) | 0x64006400u;
+  __half2 h0 = __hsub2(*reinterpret_cast<const __half2 *>(&v0), k1024);
+  __half2 h1 = __hfma2(*reinterpret_cast<const __half2 *>(&v1), k16th, km64);
+  __half2 h2 = __hsub2(*reinterpret_cast<const __half2 *>(&v2), k1024);
+  __half2 h3 = __hfma2(*reinterpret_cast<const __half2 *>(&v3), k16th, km64);
+  out[0] = *reinterpret_cast<uint32_t *>(&h0);
+  out[1] = *reinterpret_cast<uint32_t *>(&h1);
+  out[2] = *reinterpret_cast<uint32_t *>(&h2);
+  out[3] = *reinterpret_cast<uint32_t *>(&h3);
 }
 
 // Load helpers with read-only caching.

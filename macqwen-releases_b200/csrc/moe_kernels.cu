@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *__restrict__ 
     const int k = emax - 22;
     const float scale = (k >= -126) ? __int_as_float((k + 127) << 23) : 0.0f;
     meta[static_cast<size_t>(row) * Gc + g] =
-        make_float4(__int2float_rn(sx), scale, static_cast<float>(k), 0.0f);
+        make_float4(__int2float_rn(sx), scale, __int_as_float(k), 0.0f);
   }
 }
 
@@ -255,9 +255,7 @@ __global__ void __launch_bounds__(1024) k_group(const uint32_t *__restrict__ rou
                     : (b < E_arr + records) ? (kSlotBit | static_cast<uint32_t>(b - E_arr))
                                             : kSharedKey;
     const int nt = (c + kTokPerItem - 1) / kTokPerItem;
-    for (int t = 0; t < nt && pre_t + t < gv.max_tiles; ++t) {
-      gv.tiles[pre_t + t] = make_int4(b, pre_c + t * kTokPerItem, min(kTokPerItem, c - t * kTokPerItem), 0);
-    }
+    cnt[b] = pre_t;  // first tile of the bin (counts now live in gv.counts)
     run[b] = pre_c;  // running write position
     pre_c += c;
     pre_t += nt;
@@ -284,6 +282,24 @@ __global__ void __launch_bounds__(1024) k_group(const uint32_t *__restrict__ rou
         if ((m >> lane) == 1u) run[b] += __popc(m);  // highest lane of the group
       }
       __syncwarp();
+    }
+  }
+  __syncthreads();
+  // Self-contained tile descriptors: {route key, start, len, bin} and the pair ids.
+  for (int b = b0; b < b1; ++b) {
+    const int c = gv.counts[b];
+    const int nt = (c + kTokPerItem - 1) / kTokPerItem;
+    const int first = cnt[b];
+    const int start_b = gv.offsets[b];
+    const uint32_t key = gv.bin_key[b];
+    for (int t = 0; t < nt && first + t < gv.max_tiles; ++t) {
+      const int st = start_b + t * kTokPerItem;
+      const int len = min(kTokPerItem, c - t * kTokPerItem);
+      int p[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) p[q] = q < len ? gv.order[st + q] : -1;
+      gv.tiles[2 * (first + t)] = make_int4(static_cast<int>(key), st, len, b);
+      gv.tiles[2 * (first + t) + 1] = make_int4(p[0], p[1], p[2], p[3]);
     }
   }
 }
@@ -352,335 +368,379 @@ __device__ __forceinline__ int token_of_pair(int pair, int n_pairs, int slots) {
 }
 
 // ---------------------------------------------------------------------------
-// gate/up + SwiGLU
+// grouped Q4 expert projections (gate/up + SwiGLU, and down)
 // ---------------------------------------------------------------------------
-// CTA = WR row-warps x 4 chain-warps.  A row-warp owns 8 intermediate rows;
-// its MMA A operand stacks 8 gate rows (M 0-7) over the same 8 up rows
-// (M 8-15).  B = fixed-point limbs of 4 tokens (N = 2 limbs x 4 tokens), so
-// thread (r, c) ends up holding gate and up results of row r, token c.
+// Work item = (expert bin, WARPS x RPW output rows, up to kTokPerItem pairs).
+// Each warp owns RPW rows over the full contraction width and keeps all P
+// summation chains in registers, so no cross-warp reduction is needed.  The
+// packed rows and their scales/biases stream straight from HBM into
+// registers, PF groups ahead of use; the item's activation limbs and
+// fixed-point metadata (shared by every warp of the CTA) are staged in
+// shared memory with cp.async, double-buffered across items.
+//
+// MMA row mapping: DUAL (gate/up) -- M rows 0-7 are 8 gate rows and M rows
+// 8-15 the same 8 up rows, so a thread ends with gate and up of the same
+// (row, token) and applies SwiGLU in registers.  Single (down) -- M rows
+// 0-7 and 8-15 are 16 consecutive hidden rows.
 
-template <int G, int WR>
-__global__ void __launch_bounds__(WR * 128) k_gate_up(ExpertCallArgs a, GroupView gv,
-                                                      const uint16_t *__restrict__ xl,
-                                                      const float4 *__restrict__ xm,
-                                                      uint16_t *__restrict__ act,
-                                                      uint16_t *__restrict__ g_out,
-                                                      uint16_t *__restrict__ u_out,
-                                                      uint32_t *err) {
-  constexpr int WPG = G / 8;     // packed words per group per row
-  constexpr int WB = G / 32;     // 32-value word blocks per group
-  constexpr int KSTEPS = G / 16;
-  constexpr int ROWS = 8 * WR;
-  constexpr int MT = kTokPerItem / 4;
-  extern __shared__ float part[];  // [WR][4][16][kTokPerItem]
-  const int H = a.H, I = a.I;
-  const int Gh = H / G;
-  const int P = chain_count(Gh);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wr = warp >> 2, ch = warp & 3;
-  const int r = lane >> 2, c = lane & 3;
-  const int row_tiles = (I + ROWS - 1) / ROWS;
-  const int n_items = gv.n_tiles[0] * row_tiles;
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-    const int tile = item / row_tiles, rt = item - tile * row_tiles;
-    const int4 td = gv.tiles[tile];
-    const int start = td.y, len = td.z;
-    const uint32_t key = gv.bin_key[td.x];
-    Ptrs pg, pu;
-    const bool ok = resolve(a, key, 0, I, H, pg) && resolve(a, key, 1, I, H, pu);
-    if (!ok && threadIdx.x == 0) set_error(err, kErrBadRoute);
-    if (ok && ch < P) {
-      const int o = rt * ROWS + wr * 8 + r;
-      const bool row_ok = o < I;
-      const int oc = row_ok ? o : 0;
-      const int nmt = (len + 3) >> 2;
-      int tokB[MT], tokE[MT];
+struct XStage {
+  int Gc;      // groups along the contraction width
+  int Xrow;    // limb bytes per pair
+  int Mp;      // padded metadata pitch per pair
+  int m_off;   // metadata offset in the stage
+  int bytes;   // stage size
+};
+
+__host__ __device__ inline XStage xstage_geom(int K, int G) {
+  XStage s{};
+  s.Gc = K / G;
+  s.Xrow = s.Gc * 4 * G;
+  s.Mp = s.Gc * 16 + 16;
+  s.m_off = kTokPerItem * s.Xrow;
+  s.bytes = ((s.m_off + kTokPerItem * s.Mp + 127) / 128) * 128;
+  return s;
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::); }
+
+struct RawDesc {
+  int4 d0, d1;
+};
+
+struct ItemInfo {
+  bool valid;   // item index in range
+  bool ok;      // expert pointers resolved
+  int len, rt;
+  int pair[4];  // pair ids of the token slots (-1 beyond len)
+  Ptrs p[2];
+};
+
+__device__ __forceinline__ RawDesc load_desc(const GroupView &gv, int item, int n_items, int row_tiles) {
+  RawDesc r{};
+  if (item < n_items) {
+    const int tile = item / row_tiles;
+    r.d0 = gv.tiles[2 * tile];
+    r.d1 = gv.tiles[2 * tile + 1];
+  }
+  return r;
+}
+
+template <bool DUAL>
+__device__ __forceinline__ ItemInfo item_info(const ExpertCallArgs &a, const RawDesc &rd, int item,
+                                              int n_items, int row_tiles, int out_rows, int in_cols) {
+  ItemInfo it{};
+  it.valid = item < n_items;
+  if (!it.valid) return it;
+  it.rt = item - (item / row_tiles) * row_tiles;
+  it.len = rd.d0.z;
+  it.pair[0] = rd.d1.x;
+  it.pair[1] = rd.d1.y;
+  it.pair[2] = rd.d1.z;
+  it.pair[3] = rd.d1.w;
+  const uint32_t key = static_cast<uint32_t>(rd.d0.x);
+  if (DUAL) {
+    it.ok = resolve(a, key, 0, out_rows, in_cols, it.p[0]) && resolve(a, key, 1, out_rows, in_cols, it.p[1]);
+  } else {
+    it.ok = resolve(a, key, 2, out_rows, in_cols, it.p[0]);
+  }
+  return it;
+}
+
+// Stage the activation limbs and metadata of an item's pairs (all threads).
+__device__ __forceinline__ void load_xstage(uint8_t *st, const XStage &xs, const ItemInfo &it,
+                                            const uint16_t *__restrict__ xl, const float4 *__restrict__ xm,
+                                            int n_pairs, int slots, bool by_token) {
+  if (!it.valid || !it.ok) return;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int cpx = xs.Xrow / 16;
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const int qb = 4 * mt + (r >> 1);
-        const int qe = 4 * mt + c;
-        tokB[mt] = (qb < len) ? token_of_pair(gv.order[start + qb], a.n_pairs, a.slots) : -1;
-        tokE[mt] = (qe < len) ? token_of_pair(gv.order[start + qe], a.n_pairs, a.slots) : -1;
-      }
-      float acc[MT][2];
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = -0.0f;
-      const uint32_t *wg_row = pg.w + static_cast<size_t>(oc) * (H / 8);
-      const uint32_t *wu_row = pu.w + static_cast<size_t>(oc) * (H / 8);
-      const uint16_t *sg_row = pg.s + static_cast<size_t>(oc) * Gh;
-      const uint16_t *bg_row = pg.b + static_cast<size_t>(oc) * Gh;
-      const uint16_t *su_row = pu.s + static_cast<size_t>(oc) * Gh;
-      const uint16_t *bu_row = pu.b + static_cast<size_t>(oc) * Gh;
-      const int g0 = chain_begin(ch, P, Gh), g1 = chain_begin(ch + 1, P, Gh);
-      for (int g = g0; g < g1; ++g) {
-        uint32_t wg[WB], wu[WB];
-#pragma unroll
-        for (int wb = 0; wb < WB; ++wb) {
-          wg[wb] = row_ok ? ldg_u32(wg_row + g * WPG + wb * 4 + c) : 0u;
-          wu[wb] = row_ok ? ldg_u32(wu_row + g * WPG + wb * 4 + c) : 0u;
-        }
-        const float sg = row_ok ? bf16_to_f32(ldg_u16(sg_row + g)) : 0.0f;
-        const float bg = row_ok ? bf16_to_f32(ldg_u16(bg_row + g)) : 0.0f;
-        const float su = row_ok ? bf16_to_f32(ldg_u16(su_row + g)) : 0.0f;
-        const float bu = row_ok ? bf16_to_f32(ldg_u16(bu_row + g)) : 0.0f;
-        uint32_t A[KSTEPS][4];
-#pragma unroll
-        for (int st = 0; st < KSTEPS; ++st) {
-          const int wb = st >> 1, j = (st & 1) * 2;
-          A[st][0] = nibble_pair(wg[wb], j);
-          A[st][1] = nibble_pair(wu[wb], j);
-          A[st][2] = nibble_pair(wg[wb], j + 1);
-          A[st][3] = nibble_pair(wu[wb], j + 1);
-        }
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          if (mt < nmt) {
-            float C[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            uint4 v[WB];
-            if (tokB[mt] >= 0) {
-              const uint16_t *base = xl + (static_cast<size_t>(tokB[mt]) * Gh + g) * 2 * G + (r & 1) * G;
-#pragma unroll
-              for (int wb = 0; wb < WB; ++wb)
-                v[wb] = ldg_u128(reinterpret_cast<const uint4 *>(base + wb * 32 + c * 8));
-            } else {
-#pragma unroll
-              for (int wb = 0; wb < WB; ++wb) v[wb] = make_uint4(0u, 0u, 0u, 0u);
-            }
-#pragma unroll
-            for (int st = 0; st < KSTEPS; ++st) {
-              const uint4 &vv = v[st >> 1];
-              if (st & 1) mma_16816(C, A[st], vv.z, vv.w);
-              else mma_16816(C, A[st], vv.x, vv.y);
-            }
-            if (tokE[mt] >= 0) {
-              const float4 m = xm[static_cast<size_t>(tokE[mt]) * Gh + g];
-              const int k = static_cast<int>(m.z);
-              const float Sg = __fmaf_rn(C[0], 4096.0f, C[1]);
-              const float tg = __fadd_rn(__fmul_rn(sg, Sg), __fmul_rn(bg, m.x));
-              acc[mt][0] = __fadd_rn(acc[mt][0], scale_pow2(tg, m.y, k));
-              const float Su = __fmaf_rn(C[2], 4096.0f, C[3]);
-              const float tu = __fadd_rn(__fmul_rn(su, Su), __fmul_rn(bu, m.x));
-              acc[mt][1] = __fadd_rn(acc[mt][1], scale_pow2(tu, m.y, k));
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const int qe = 4 * mt + c;
-        if (qe < len) {
-          part[((wr * 4 + ch) * 16 + r) * kTokPerItem + qe] = acc[mt][0];
-          part[((wr * 4 + ch) * 16 + r + 8) * kTokPerItem + qe] = acc[mt][1];
-        }
-      }
+  for (int q = 0; q < kTokPerItem; ++q) {
+    uint8_t *dst = st + q * xs.Xrow;
+    uint8_t *mdst = st + xs.m_off + q * xs.Mp;
+    if (q < it.len) {
+      const int pair = it.pair[q];
+      const int row = by_token ? token_of_pair(pair, n_pairs, slots) : pair;
+      const uint8_t *src = reinterpret_cast<const uint8_t *>(xl) + static_cast<size_t>(row) * xs.Xrow;
+      for (int cc = tid; cc < cpx; cc += nt) cp_async16(dst + cc * 16, src + cc * 16);
+      const float4 *msrc = xm + static_cast<size_t>(row) * xs.Gc;
+      for (int g = tid; g < xs.Gc; g += nt) cp_async16(mdst + g * 16, msrc + g);
+    } else {
+      // empty slot: zero limbs (the MMA adds nothing) and a neutral scale
+      for (int cc = tid; cc < cpx; cc += nt) *reinterpret_cast<uint4 *>(dst + cc * 16) = make_uint4(0u, 0u, 0u, 0u);
+      for (int g = tid; g < xs.Gc; g += nt) *reinterpret_cast<float4 *>(mdst + g * 16) = make_float4(0.0f, 1.0f, 0.0f, 0.0f);
     }
-    __syncthreads();
-    if (ok) {
-      for (int idx = threadIdx.x; idx < len * ROWS; idx += blockDim.x) {
-        const int q = idx / ROWS, ol = idx - q * ROWS;
-        const int o = rt * ROWS + ol;
-        if (o >= I) continue;
-        const int wr2 = ol >> 3, r2 = ol & 7;
-        float cg[4] = {-0.0f, -0.0f, -0.0f, -0.0f}, cu[4] = {-0.0f, -0.0f, -0.0f, -0.0f};
-        for (int k = 0; k < P; ++k) {
-          cg[k] = part[((wr2 * 4 + k) * 16 + r2) * kTokPerItem + q];
-          cu[k] = part[((wr2 * 4 + k) * 16 + r2 + 8) * kTokPerItem + q];
-        }
-        const float gvv = round_bf16(chain_tree(cg, P));
-        const float uvv = round_bf16(chain_tree(cu, P));
-        const float av = swiglu_bf16(g_exp_bf16, gvv, uvv);
-        const int pair = gv.order[start + q];
-        act[static_cast<size_t>(pair) * I + o] = f32_to_bf16(av);
-        if (g_out != nullptr && pair < a.n_pairs) {
-          g_out[static_cast<size_t>(pair) * I + o] = f32_to_bf16(gvv);
-          u_out[static_cast<size_t>(pair) * I + o] = f32_to_bf16(uvv);
-        }
-      }
-    }
-    __syncthreads();
   }
 }
 
-// ---------------------------------------------------------------------------
-// down projection
-// ---------------------------------------------------------------------------
-// CTA = WR row-warps x 4 chain-warps; a row-warp owns 16 hidden rows
-// (M 0-7 = rows r, M 8-15 = rows r+8).  B = limbs of 4 pairs' SwiGLU rows.
+// One group's epilogue term: fl(fl(s*fl(S)) + fl(b*fl(SX))) * 2^k.
+__device__ __forceinline__ float group_term(float c_hi, float c_lo, float s, float b, const float4 &m) {
+  const float S = __fmaf_rn(c_hi, 4096.0f, c_lo);
+  const float t = __fadd_rn(__fmul_rn(s, S), __fmul_rn(b, m.x));
+  return scale_pow2(t, m.y, __float_as_int(m.z));
+}
 
-template <int G, int WR>
-__global__ void __launch_bounds__(WR * 128) k_down(ExpertCallArgs a, GroupView gv,
-                                                   const uint16_t *__restrict__ al,
-                                                   const float4 *__restrict__ am,
-                                                   uint16_t *__restrict__ d, uint32_t *err) {
-  constexpr int WPG = G / 8;
-  constexpr int WB = G / 32;
-  constexpr int KSTEPS = G / 16;
-  constexpr int ROWS = 16 * WR;
-  constexpr int MT = kTokPerItem / 4;
-  extern __shared__ float part[];  // [WR][4][16][kTokPerItem]
+// PF consecutive bfloat16 scales (or biases) loaded as one vector.
+template <int PF>
+struct Vec16 {
+  uint32_t w[(PF + 1) / 2];
+  __device__ __forceinline__ void load(const uint16_t *p) {
+    if constexpr (PF == 8) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p));
+      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+    } else if constexpr (PF == 4) {
+      const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p));
+      w[0] = v.x; w[1] = v.y;
+    } else if constexpr (PF == 2) {
+      w[0] = __ldg(reinterpret_cast<const uint32_t *>(p));
+    } else {
+      w[0] = __ldg(p);
+    }
+  }
+  __device__ __forceinline__ float get(int j) const {  // j is a compile-time constant after unrolling
+    const uint32_t word = w[j >> 1];
+    return __uint_as_float((j & 1) ? (word & 0xFFFF0000u) : (word << 16));
+  }
+};
+
+template <int G, int WARPS, bool DUAL, int PF>
+__global__ void __launch_bounds__(WARPS * 32) k_expert_rows(ExpertCallArgs a, GroupView gv,
+                                                            const uint16_t *__restrict__ xl,
+                                                            const float4 *__restrict__ xm,
+                                                            uint16_t *__restrict__ out,
+                                                            uint16_t *__restrict__ g_out,
+                                                            uint16_t *__restrict__ u_out, uint32_t *err) {
+  constexpr int WB = G / 32;          // 16-byte word blocks per group
+  constexpr int WPG = G / 8;          // packed words per group
+  constexpr int RPW = DUAL ? 8 : 16;  // output rows per warp
+  constexpr int ROWS = RPW * WARPS;
+  extern __shared__ __align__(128) uint8_t smem[];
   const int H = a.H, I = a.I;
-  const int Gi = I / G;
-  const int P = chain_count(Gi);
+  const int K = DUAL ? H : I;
+  const int O = DUAL ? I : H;
+  const XStage xs = xstage_geom(K, G);
+  const int Gc = xs.Gc;
+  const int P = chain_count(Gc);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wr = warp >> 2, ch = warp & 3;
   const int r = lane >> 2, c = lane & 3;
-  const int row_tiles = (H + ROWS - 1) / ROWS;
+  const int row_tiles = (O + ROWS - 1) / ROWS;
   const int n_items = gv.n_tiles[0] * row_tiles;
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-    const int tile = item / row_tiles, rt = item - tile * row_tiles;
-    const int4 td = gv.tiles[tile];
-    const int start = td.y, len = td.z;
-    const uint32_t key = gv.bin_key[td.x];
-    Ptrs pd;
-    const bool ok = resolve(a, key, 2, H, I, pd);
-    if (!ok && threadIdx.x == 0) set_error(err, kErrBadRoute);
-    if (ok && ch < P) {
-      const int h0 = rt * ROWS + wr * 16 + r;
-      const int h1 = h0 + 8;
-      const bool ok0 = h0 < H, ok1 = h1 < H;
-      const int hc0 = ok0 ? h0 : 0, hc1 = ok1 ? h1 : 0;
-      const int nmt = (len + 3) >> 2;
-      int pB[MT], pE[MT];
+  const int wpr = K / 8;  // packed words per row
+
+  int item = blockIdx.x;
+  ItemInfo cur = item_info<DUAL>(a, load_desc(gv, item, n_items, row_tiles), item, n_items, row_tiles, O, K);
+  RawDesc raw_next = load_desc(gv, item + gridDim.x, n_items, row_tiles);
+  load_xstage(smem, xs, cur, xl, xm, a.n_pairs, a.slots, DUAL);
+  cp_async_commit();
+  for (int k = 0; cur.valid; ++k) {
+    const uint8_t *st = smem + (k & 1) * xs.bytes;
+    const int nitem = item + gridDim.x;
+    const ItemInfo nxt = item_info<DUAL>(a, raw_next, nitem, n_items, row_tiles, O, K);
+    raw_next = load_desc(gv, nitem + gridDim.x, n_items, row_tiles);
+    load_xstage(smem + ((k + 1) & 1) * xs.bytes, xs, nxt, xl, xm, a.n_pairs, a.slots, DUAL);
+    cp_async_commit();
+    if (!cur.ok) {
+      if (threadIdx.x == 0) set_error(err, kErrBadRoute);
+      cp_async_wait1();
+      __syncthreads();
+      __syncthreads();
+      item = nitem;
+      cur = nxt;
+      continue;
+    }
+    // This warp's two MMA rows (clamped in range; rows past O are not stored).
+    const int o0 = cur.rt * ROWS + warp * RPW + r;
+    const int oA = o0;
+    const int oB = DUAL ? o0 : o0 + 8;
+    const int cA = min(oA, O - 1), cB = min(oB, O - 1);
+    const Ptrs &pA = cur.p[0];
+    const Ptrs &pB = DUAL ? cur.p[1] : cur.p[0];
+    const uint32_t *wA = pA.w + static_cast<size_t>(cA) * wpr + c;
+    const uint32_t *wB = pB.w + static_cast<size_t>(cB) * wpr + c;
+    const uint16_t *sA = pA.s + static_cast<size_t>(cA) * Gc;
+    const uint16_t *bA = pA.b + static_cast<size_t>(cA) * Gc;
+    const uint16_t *sB = pB.s + static_cast<size_t>(cB) * Gc;
+    const uint16_t *bB = pB.b + static_cast<size_t>(cB) * Gc;
+    uint32_t qa[PF][WB], qb[PF][WB];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const int qb = 4 * mt + (r >> 1);
-        const int qe = 4 * mt + c;
-        pB[mt] = (qb < len) ? gv.order[start + qb] : -1;
-        pE[mt] = (qe < len) ? gv.order[start + qe] : -1;
+    for (int j = 0; j < PF; ++j) {
+#pragma unroll
+      for (int wb = 0; wb < WB; ++wb) {
+        qa[j][wb] = ldg_u32(wA + j * WPG + wb * 4);
+        qb[j][wb] = ldg_u32(wB + j * WPG + wb * 4);
       }
-      float acc[MT][2];
+    }
+    Vec16<PF> vsA, vbA, vsB, vbB;
+    vsA.load(sA);
+    vbA.load(bA);
+    vsB.load(sB);
+    vbB.load(bB);
+    cp_async_wait1();
+    __syncthreads();  // activation stage of this item is visible
+    const uint8_t *xb = st + (r >> 1) * xs.Xrow + (r & 1) * (G * 2) + c * 16;
+    const float4 *mrow = reinterpret_cast<const float4 *>(st + xs.m_off + c * xs.Mp);
+    float chA[4] = {-0.0f, -0.0f, -0.0f, -0.0f}, chB[4] = {-0.0f, -0.0f, -0.0f, -0.0f};
+    for (int ch = 0; ch < P; ++ch) {
+      float accA = -0.0f, accB = -0.0f;
+      const int gend = chain_begin(ch + 1, P, Gc);
+      for (int g0 = chain_begin(ch, P, Gc); g0 < gend; g0 += PF) {
+        const int gn0 = (g0 + PF < Gc) ? g0 + PF : g0;  // next block (re-read the last one at the end)
+        Vec16<PF> nsA, nbA, nsB, nbB;
+        nsA.load(sA + gn0);
+        nbA.load(bA + gn0);
+        nsB.load(sB + gn0);
+        nbB.load(bB + gn0);
+        const uint32_t *nwA = wA + gn0 * WPG;
+        const uint32_t *nwB = wB + gn0 * WPG;
+        const uint8_t *xg = xb + g0 * (4 * G);
+        const float4 *mg = mrow + g0;
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = -0.0f;
-      const uint32_t *w0 = pd.w + static_cast<size_t>(hc0) * (I / 8);
-      const uint32_t *w1 = pd.w + static_cast<size_t>(hc1) * (I / 8);
-      const uint16_t *s0 = pd.s + static_cast<size_t>(hc0) * Gi;
-      const uint16_t *b0 = pd.b + static_cast<size_t>(hc0) * Gi;
-      const uint16_t *s1 = pd.s + static_cast<size_t>(hc1) * Gi;
-      const uint16_t *b1 = pd.b + static_cast<size_t>(hc1) * Gi;
-      const int g0 = chain_begin(ch, P, Gi), g1 = chain_begin(ch + 1, P, Gi);
-      for (int g = g0; g < g1; ++g) {
-        uint32_t wa[WB], wb_[WB];
+        for (int j = 0; j < PF; ++j) {
+          uint32_t w0[WB], w1[WB];
 #pragma unroll
-        for (int wb = 0; wb < WB; ++wb) {
-          wa[wb] = ok0 ? ldg_u32(w0 + g * WPG + wb * 4 + c) : 0u;
-          wb_[wb] = ok1 ? ldg_u32(w1 + g * WPG + wb * 4 + c) : 0u;
+          for (int wb = 0; wb < WB; ++wb) {
+            w0[wb] = qa[j][wb];
+            w1[wb] = qb[j][wb];
+            qa[j][wb] = ldg_u32(nwA + j * WPG + wb * 4);
+            qb[j][wb] = ldg_u32(nwB + j * WPG + wb * 4);
+          }
+          float C[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+          for (int wb = 0; wb < WB; ++wb) {
+            uint32_t pa[4], pb[4];
+            nibble_pairs4(w0[wb], pa);
+            nibble_pairs4(w1[wb], pb);
+            const uint4 v = *reinterpret_cast<const uint4 *>(xg + j * (4 * G) + wb * 64);
+            const uint32_t A0[4] = {pa[0], pb[0], pa[1], pb[1]};
+            const uint32_t A1[4] = {pa[2], pb[2], pa[3], pb[3]};
+            mma_16816(C, A0, v.x, v.y);
+            mma_16816(C, A1, v.z, v.w);
+          }
+          const float4 m = mg[j];
+          accA = __fadd_rn(accA, group_term(C[0], C[1], vsA.get(j), vbA.get(j), m));
+          accB = __fadd_rn(accB, group_term(C[2], C[3], vsB.get(j), vbB.get(j), m));
         }
-        const float sa = ok0 ? bf16_to_f32(ldg_u16(s0 + g)) : 0.0f;
-        const float ba = ok0 ? bf16_to_f32(ldg_u16(b0 + g)) : 0.0f;
-        const float sb = ok1 ? bf16_to_f32(ldg_u16(s1 + g)) : 0.0f;
-        const float bb = ok1 ? bf16_to_f32(ldg_u16(b1 + g)) : 0.0f;
-        uint32_t A[KSTEPS][4];
-#pragma unroll
-        for (int st = 0; st < KSTEPS; ++st) {
-          const int wb = st >> 1, j = (st & 1) * 2;
-          A[st][0] = nibble_pair(wa[wb], j);
-          A[st][1] = nibble_pair(wb_[wb], j);
-          A[st][2] = nibble_pair(wa[wb], j + 1);
-          A[st][3] = nibble_pair(wb_[wb], j + 1);
-        }
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          if (mt < nmt) {
-            float C[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            uint4 v[WB];
-            if (pB[mt] >= 0) {
-              const uint16_t *base = al + (static_cast<size_t>(pB[mt]) * Gi + g) * 2 * G + (r & 1) * G;
-#pragma unroll
-              for (int wb = 0; wb < WB; ++wb)
-                v[wb] = ldg_u128(reinterpret_cast<const uint4 *>(base + wb * 32 + c * 8));
-            } else {
-#pragma unroll
-              for (int wb = 0; wb < WB; ++wb) v[wb] = make_uint4(0u, 0u, 0u, 0u);
-            }
-#pragma unroll
-            for (int st = 0; st < KSTEPS; ++st) {
-              const uint4 &vv = v[st >> 1];
-              if (st & 1) mma_16816(C, A[st], vv.z, vv.w);
-              else mma_16816(C, A[st], vv.x, vv.y);
-            }
-            if (pE[mt] >= 0) {
-              const float4 m = am[static_cast<size_t>(pE[mt]) * Gi + g];
-              const int k = static_cast<int>(m.z);
-              const float S0 = __fmaf_rn(C[0], 4096.0f, C[1]);
-              const float t0 = __fadd_rn(__fmul_rn(sa, S0), __fmul_rn(ba, m.x));
-              acc[mt][0] = __fadd_rn(acc[mt][0], scale_pow2(t0, m.y, k));
-              const float S1 = __fmaf_rn(C[2], 4096.0f, C[3]);
-              const float t1 = __fadd_rn(__fmul_rn(sb, S1), __fmul_rn(bb, m.x));
-              acc[mt][1] = __fadd_rn(acc[mt][1], scale_pow2(t1, m.y, k));
-            }
+        vsA = nsA;
+        vbA = nbA;
+        vsB = nsB;
+        vbB = nbB;
+      }
+      if (ch == 0) { chA[0] = accA; chB[0] = accB; }
+      else if (ch == 1) { chA[1] = accA; chB[1] = accB; }
+      else if (ch == 2) { chA[2] = accA; chB[2] = accB; }
+      else { chA[3] = accA; chB[3] = accB; }
+    }
+    if (c < cur.len) {
+      const int pair = c == 0 ? cur.pair[0] : c == 1 ? cur.pair[1] : c == 2 ? cur.pair[2] : cur.pair[3];
+      const float yA = chain_tree(chA, P);
+      const float yB = chain_tree(chB, P);
+      if (DUAL) {
+        if (oA < O) {
+          const float gvv = round_bf16(yA), uvv = round_bf16(yB);
+          out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(swiglu_bf16(g_exp_bf16, gvv, uvv));
+          if (g_out != nullptr && pair < a.n_pairs) {
+            g_out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(gvv);
+            u_out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(uvv);
           }
         }
-      }
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const int qe = 4 * mt + c;
-        if (qe < len) {
-          part[((wr * 4 + ch) * 16 + r) * kTokPerItem + qe] = acc[mt][0];
-          part[((wr * 4 + ch) * 16 + r + 8) * kTokPerItem + qe] = acc[mt][1];
-        }
+      } else {
+        if (oA < O) out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(yA);
+        if (oB < O) out[static_cast<size_t>(pair) * O + oB] = f32_to_bf16(yB);
       }
     }
-    __syncthreads();
-    if (ok) {
-      for (int idx = threadIdx.x; idx < len * ROWS; idx += blockDim.x) {
-        const int q = idx / ROWS, ol = idx - q * ROWS;
-        const int h = rt * ROWS + ol;
-        if (h >= H) continue;
-        const int wr2 = ol >> 4, rr = ol & 15;
-        float cc[4] = {-0.0f, -0.0f, -0.0f, -0.0f};
-        for (int k = 0; k < P; ++k) cc[k] = part[((wr2 * 4 + k) * 16 + rr) * kTokPerItem + q];
-        const int pair = gv.order[start + q];
-        d[static_cast<size_t>(pair) * H + h] = f32_to_bf16(chain_tree(cc, P));
-      }
-    }
-    __syncthreads();
+    __syncthreads();  // the stage is refilled two items later
+    item = nitem;
+    cur = nxt;
   }
+  asm volatile("cp.async.wait_all;\n" ::);
 }
 
 namespace {
-constexpr int kWR = 2;
-template <typename K>
-int persistent_grid(K kernel, int threads, size_t smem) {
+
+template <typename Kern>
+cudaError_t launch_rows(Kern kernel, int threads, size_t smem, const ExpertCallArgs &a, const GroupView &gv,
+                        const uint16_t *xl, const float4 *xm, uint16_t *out, uint16_t *g_out,
+                        uint16_t *u_out, cudaStream_t s) {
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
   const DeviceInfo di = device_info();
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
-      per_sm <= 0)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm <= 0)
     per_sm = 1;
-  return di.sms * per_sm;
+  kernel<<<di.sms * per_sm, threads, smem, s>>>(a, gv, xl, xm, out, g_out, u_out, device_error_word());
+  return cudaGetLastError();
 }
+
+constexpr size_t kSmemBudget = 200 * 1024;
+
 }  // namespace
 
+// Prefetch block: the largest of 8/4/2/1 that divides every chain length and
+// keeps the scales/biases vector loads aligned.
+int pick_pf(int K, int G) {
+  const int Gc = K / G;
+  const int P = chain_count(Gc);
+  for (int pf : {8, 4, 2}) {
+    bool ok = (Gc * 2) % (pf * 2) == 0;
+    for (int ch = 0; ch < P && ok; ++ch) ok = ((chain_begin(ch + 1, P, Gc) - chain_begin(ch, P, Gc)) % pf) == 0;
+    for (int ch = 0; ch < P && ok; ++ch) ok = (chain_begin(ch, P, Gc) % pf) == 0;
+    if (ok) return pf;
+  }
+  return 1;
+}
+
+template <int G, int WARPS, bool DUAL>
+cudaError_t launch_rows_pf(int pf, size_t smem, const ExpertCallArgs &a, const GroupView &gv, const uint16_t *xl,
+                           const float4 *xm, uint16_t *out, uint16_t *g_out, uint16_t *u_out, cudaStream_t s) {
+  const int threads = WARPS * 32;
+  switch (pf) {
+    case 8: return launch_rows(k_expert_rows<G, WARPS, DUAL, 8>, threads, smem, a, gv, xl, xm, out, g_out, u_out, s);
+    case 4: return launch_rows(k_expert_rows<G, WARPS, DUAL, 4>, threads, smem, a, gv, xl, xm, out, g_out, u_out, s);
+    case 2: return launch_rows(k_expert_rows<G, WARPS, DUAL, 2>, threads, smem, a, gv, xl, xm, out, g_out, u_out, s);
+    default: return launch_rows(k_expert_rows<G, WARPS, DUAL, 1>, threads, smem, a, gv, xl, xm, out, g_out, u_out, s);
+  }
+}
+
+// Expected pairs per launch decide the CTA width: many pairs -> 8 warps,
+// few pairs (batch-1 decode) -> 4 warps so that the handful of experts still
+// spreads over every SM.
 cudaError_t launch_gate_up(const ExpertCallArgs &a, const GroupView &gv,
                            const uint16_t *x_limbs, const float4 *x_meta,
                            uint16_t *act, uint16_t *g_out, uint16_t *u_out,
                            cudaStream_t s) {
-  const int threads = kWR * 128;
-  const size_t smem = static_cast<size_t>(kWR) * 4 * 16 * kTokPerItem * sizeof(float);
-  uint32_t *err = device_error_word();
+  const XStage xs = xstage_geom(a.H, a.G);
+  const size_t smem = 2 * static_cast<size_t>(xs.bytes);
+  if (smem > kSmemBudget) return cudaErrorInvalidValue;
+  const bool wide = (a.n_pairs + a.tokens) >= 64;
+  const int pf = pick_pf(a.H, a.G);
   if (a.G == 32) {
-    const int grid = persistent_grid(k_gate_up<32, kWR>, threads, smem);
-    k_gate_up<32, kWR><<<grid, threads, smem, s>>>(a, gv, x_limbs, x_meta, act, g_out, u_out, err);
-  } else {
-    const int grid = persistent_grid(k_gate_up<64, kWR>, threads, smem);
-    k_gate_up<64, kWR><<<grid, threads, smem, s>>>(a, gv, x_limbs, x_meta, act, g_out, u_out, err);
+    if (wide) return launch_rows_pf<32, 8, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
+    return launch_rows_pf<32, 4, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
   }
-  return cudaGetLastError();
+  if (wide) return launch_rows_pf<64, 8, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
+  return launch_rows_pf<64, 4, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
 }
 
 cudaError_t launch_down(const ExpertCallArgs &a, const GroupView &gv,
                         const uint16_t *act_limbs, const float4 *act_meta,
                         uint16_t *d, cudaStream_t s) {
-  const int threads = kWR * 128;
-  const size_t smem = static_cast<size_t>(kWR) * 4 * 16 * kTokPerItem * sizeof(float);
-  uint32_t *err = device_error_word();
+  const XStage xs = xstage_geom(a.I, a.G);
+  const size_t smem = 2 * static_cast<size_t>(xs.bytes);
+  if (smem > kSmemBudget) return cudaErrorInvalidValue;
+  const bool wide = (a.n_pairs + a.tokens) >= 64;
+  const int pf = pick_pf(a.I, a.G);
   if (a.G == 32) {
-    const int grid = persistent_grid(k_down<32, kWR>, threads, smem);
-    k_down<32, kWR><<<grid, threads, smem, s>>>(a, gv, act_limbs, act_meta, d, err);
-  } else {
-    const int grid = persistent_grid(k_down<64, kWR>, threads, smem);
-    k_down<64, kWR><<<grid, threads, smem, s>>>(a, gv, act_limbs, act_meta, d, err);
+    if (wide) return launch_rows_pf<32, 8, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
+    return launch_rows_pf<32, 4, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
   }
-  return cudaGetLastError();
+  if (wide) return launch_rows_pf<64, 8, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
+  return launch_rows_pf<64, 4, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -742,7 +802,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
     const uint16_t *__restrict__ x, const uint16_t *__restrict__ W, int T, int H, int E,
     const uint16_t *__restrict__ wsg, uint16_t *__restrict__ logits,
     uint16_t *__restrict__ shared_logit) {
-  extern __shared__ float xs[];  // [kRouterTokBlock][H]
+  extern __shared__ __align__(16) float xs[];  // [kRouterTokBlock][H]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kRouterWarps + warp;
   const int rows = E + (wsg != nullptr ? 1 : 0);
@@ -770,8 +830,15 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
   for (int t0 = 0; t0 < T; t0 += kRouterTokBlock) {
     const int tb = min(kRouterTokBlock, T - t0);
     __syncthreads();
-    for (int idx = threadIdx.x; idx < tb * H; idx += blockDim.x) {
-      xs[idx] = bf16_to_f32(x[static_cast<size_t>(t0) * H + idx]);
+    // 8 bf16 per 16-byte load -> two float4 stores (rows are contiguous)
+    const uint4 *xsrc = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t0) * H);
+    float4 *xdst = reinterpret_cast<float4 *>(xs);
+    for (int idx = threadIdx.x; idx < tb * H / 8; idx += blockDim.x) {
+      const uint4 v = ldg_u128(xsrc + idx);
+      xdst[2 * idx] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                                  __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+      xdst[2 * idx + 1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
+                                      __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
     }
     __syncthreads();
     if (wrow == nullptr) continue;
@@ -781,9 +848,16 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
       for (int m = 0; m < CH; ++m) {
         const int cidx = lane + 32 * m;
         if (cidx < nchunks) {
-          const float *xp = xs + tt * H + cidx * 8;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc = __fmaf_rn(w[m * 8 + i], xp[i], acc);
+          const float4 *xp = reinterpret_cast<const float4 *>(xs + tt * H + cidx * 8);
+          const float4 p0 = xp[0], p1 = xp[1];
+          acc = __fmaf_rn(w[m * 8 + 0], p0.x, acc);
+          acc = __fmaf_rn(w[m * 8 + 1], p0.y, acc);
+          acc = __fmaf_rn(w[m * 8 + 2], p0.z, acc);
+          acc = __fmaf_rn(w[m * 8 + 3], p0.w, acc);
+          acc = __fmaf_rn(w[m * 8 + 4], p1.x, acc);
+          acc = __fmaf_rn(w[m * 8 + 5], p1.y, acc);
+          acc = __fmaf_rn(w[m * 8 + 6], p1.z, acc);
+          acc = __fmaf_rn(w[m * 8 + 7], p1.w, acc);
         }
       }
 #pragma unroll
