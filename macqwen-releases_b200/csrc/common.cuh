@@ -83,16 +83,10 @@ __device__ __forceinline__ float swiglu_bf16(const uint16_t *tab, float g, float
   return bmul(bmul(g, sigmoid_bf16(tab, g)), u);
 }
 
-// fl(t * 2^k) for k < -126 (groups whose largest activation is below 2^-104),
-// kept out of line so the common path stays a single multiply.
-static __device__ __noinline__ float scale_pow2_slow(float t, int k) {
-  return __double2float_rn(static_cast<double>(t) * ldexp(1.0, k));
-}
-
-// fl(t * 2^k), one rounding; `scale` = 2^k as float when k >= -126, else 0.
-__device__ __forceinline__ float scale_pow2(float t, float scale, int k) {
-  if (scale != 0.0f) return __fmul_rn(t, scale);
-  return scale_pow2_slow(t, k);
+// fl(fl(t * A) * B) with A * B = 2^k, A = 2^max(k, -126): a single exact
+// scaling (B = 1) unless the group's activations are all below 2^-104.
+__device__ __forceinline__ float scale_pow2(float t, float A, float B) {
+  return __fmul_rn(__fmul_rn(t, A), B);
 }
 
 // m16n8k16 fp16 MMA, fp32 accumulate (exact here: all operands are small
@@ -115,6 +109,27 @@ __device__ __forceinline__ uint32_t nibble_pair(uint32_t w, int j) {
   const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
   h = __hsub2(h, k1024);
   return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// MMA A operands of one 32-value group for two rows: A0 = {a j0, b j0, a j1,
+// b j1} and A1 = {a j2, b j2, a j3, b j3}, where "x jN" is the fp16x2 pair of
+// nibbles (N, N+4) of word x (rows r and r+8 of the m16n8k16 fragment).
+// Even pairs use the 1024 + q encoding, odd pairs the unshifted 1024 + 16q.
+__device__ __forceinline__ void nibble_operands(uint32_t wa, uint32_t wb, uint32_t A0[4], uint32_t A1[4]) {
+  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+  const __half2 k16th = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));
+  const __half2 km64 = __halves2half2(__ushort_as_half(0xD400), __ushort_as_half(0xD400));
+  const uint32_t wa8 = wa >> 8, wb8 = wb >> 8;
+  uint32_t t;
+  __half2 h;
+  t = (wa & 0x000F000Fu) | 0x64006400u; h = __hsub2(*reinterpret_cast<const __half2 *>(&t), k1024); A0[0] = *reinterpret_cast<uint32_t *>(&h);
+  t = (wb & 0x000F000Fu) | 0x64006400u; h = __hsub2(*reinterpret_cast<const __half2 *>(&t), k1024); A0[1] = *reinterpret_cast<uint32_t *>(&h);
+  t = (wa & 0x00F000F0u) | 0x64006400u; h = __hfma2(*reinterpret_cast<const __half2 *>(&t), k16th, km64); A0[2] = *reinterpret_cast<uint32_t *>(&h);
+  t = (wb & 0x00F000F0u) | 0x64006400u; h = __hfma2(*reinterpret_cast<const __half2 *>(&t), k16th, km64); A0[3] = *reinterpret_cast<uint32_t *>(&h);
+  t = (wa8 & 0x000F000Fu) | 0x64006400u; h = __hsub2(*reinterpret_cast<const __half2 *>(&t), k1024); A1[0] = *reinterpret_cast<uint32_t *>(&h);
+  t = (wb8 & 0x000F000Fu) | 0x64006400u; h = __hsub2(*reinterpret_cast<const __half2 *>(&t), k1024); A1[1] = *reinterpret_cast<uint32_t *>(&h);
+  t = (wa8 & 0x00F000F0u) | 0x64006400u; h = __hfma2(*reinterpret_cast<const __half2 *>(&t), k16th, km64); A1[2] = *reinterpret_cast<uint32_t *>(&h);
+  t = (wb8 & 0x00F000F0u) | 0x64006400u; h = __hfma2(*reinterpret_cast<const __half2 *>(&t), k16th, km64); A1[3] = *reinterpret_cast<uint32_t *>(&h);
 }
 
 // All four nibble pairs (j, j+4), j = 0..3, of a packed word as fp16x2.

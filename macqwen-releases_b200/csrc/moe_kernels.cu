@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <climits>
 #include <mutex>
 
@@ -154,9 +155,10 @@ __global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *__restrict__ 
   for (int off = 16; off >= 1; off >>= 1) sx += __shfl_xor_sync(0xFFFFFFFFu, sx, off);
   if (lane == 0) {
     const int k = emax - 22;
-    const float scale = (k >= -126) ? __int_as_float((k + 127) << 23) : 0.0f;
-    meta[static_cast<size_t>(row) * Gc + g] =
-        make_float4(__int2float_rn(sx), scale, __int_as_float(k), 0.0f);
+    const int ka = max(k, -126);
+    const float A = __int_as_float((ka + 127) << 23);       // 2^ka, normal
+    const float B = __int_as_float((k - ka + 127) << 23);   // 2^(k-ka) in [2^-29, 1]
+    meta[static_cast<size_t>(row) * Gc + g] = make_float4(__int2float_rn(sx), A, B, 0.0f);
   }
 }
 
@@ -295,11 +297,12 @@ __global__ void __launch_bounds__(1024) k_group(const uint32_t *__restrict__ rou
     for (int t = 0; t < nt && first + t < gv.max_tiles; ++t) {
       const int st = start_b + t * kTokPerItem;
       const int len = min(kTokPerItem, c - t * kTokPerItem);
-      int p[4];
+      int p[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) p[q] = q < len ? gv.order[st + q] : -1;
-      gv.tiles[2 * (first + t)] = make_int4(static_cast<int>(key), st, len, b);
-      gv.tiles[2 * (first + t) + 1] = make_int4(p[0], p[1], p[2], p[3]);
+      for (int q = 0; q < 8; ++q) p[q] = q < len ? gv.order[st + q] : -1;
+      gv.tiles[3 * (first + t)] = make_int4(static_cast<int>(key), st, len, b);
+      gv.tiles[3 * (first + t) + 1] = make_int4(p[0], p[1], p[2], p[3]);
+      gv.tiles[3 * (first + t) + 2] = make_int4(p[4], p[5], p[6], p[7]);
     }
   }
 }
@@ -409,14 +412,14 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::); }
 
 struct RawDesc {
-  int4 d0, d1;
+  int4 d0, d1, d2;
 };
 
 struct ItemInfo {
   bool valid;   // item index in range
   bool ok;      // expert pointers resolved
   int len, rt;
-  int pair[4];  // pair ids of the token slots (-1 beyond len)
+  int pair[kTokPerItem];  // pair ids of the token slots (-1 beyond len)
   Ptrs p[2];
 };
 
@@ -424,8 +427,9 @@ __device__ __forceinline__ RawDesc load_desc(const GroupView &gv, int item, int 
   RawDesc r{};
   if (item < n_items) {
     const int tile = item / row_tiles;
-    r.d0 = gv.tiles[2 * tile];
-    r.d1 = gv.tiles[2 * tile + 1];
+    r.d0 = gv.tiles[3 * tile];
+    r.d1 = gv.tiles[3 * tile + 1];
+    r.d2 = gv.tiles[3 * tile + 2];
   }
   return r;
 }
@@ -442,6 +446,10 @@ __device__ __forceinline__ ItemInfo item_info(const ExpertCallArgs &a, const Raw
   it.pair[1] = rd.d1.y;
   it.pair[2] = rd.d1.z;
   it.pair[3] = rd.d1.w;
+  it.pair[4] = rd.d2.x;
+  it.pair[5] = rd.d2.y;
+  it.pair[6] = rd.d2.z;
+  it.pair[7] = rd.d2.w;
   const uint32_t key = static_cast<uint32_t>(rd.d0.x);
   if (DUAL) {
     it.ok = resolve(a, key, 0, out_rows, in_cols, it.p[0]) && resolve(a, key, 1, out_rows, in_cols, it.p[1]);
@@ -472,16 +480,17 @@ __device__ __forceinline__ void load_xstage(uint8_t *st, const XStage &xs, const
     } else {
       // empty slot: zero limbs (the MMA adds nothing) and a neutral scale
       for (int cc = tid; cc < cpx; cc += nt) *reinterpret_cast<uint4 *>(dst + cc * 16) = make_uint4(0u, 0u, 0u, 0u);
-      for (int g = tid; g < xs.Gc; g += nt) *reinterpret_cast<float4 *>(mdst + g * 16) = make_float4(0.0f, 1.0f, 0.0f, 0.0f);
+      for (int g = tid; g < xs.Gc; g += nt) *reinterpret_cast<float4 *>(mdst + g * 16) = make_float4(0.0f, 1.0f, 1.0f, 0.0f);
     }
   }
 }
 
-// One group's epilogue term: fl(fl(s*fl(S)) + fl(b*fl(SX))) * 2^k.
-__device__ __forceinline__ float group_term(float c_hi, float c_lo, float s, float b, const float4 &m) {
+// Fold one group into a chain: fS = fl(S); t = fma(s, fS, fl(b*fl(SX)));
+// acc = fma(fl(t*A), B, acc).  m = {fl(SX), A, B, -}.
+__device__ __forceinline__ float group_fold(float acc, float c_hi, float c_lo, float s, float b, const float4 &m) {
   const float S = __fmaf_rn(c_hi, 4096.0f, c_lo);
-  const float t = __fadd_rn(__fmul_rn(s, S), __fmul_rn(b, m.x));
-  return scale_pow2(t, m.y, __float_as_int(m.z));
+  const float t = __fmaf_rn(s, S, __fmul_rn(b, m.x));
+  return __fmaf_rn(__fmul_rn(t, m.y), m.z, acc);
 }
 
 // PF consecutive bfloat16 scales (or biases) loaded as one vector.
@@ -507,137 +516,121 @@ struct Vec16 {
   }
 };
 
-template <int G, int WARPS, bool DUAL, int PF>
-__global__ void __launch_bounds__(WARPS * 32) k_expert_rows(ExpertCallArgs a, GroupView gv,
-                                                            const uint16_t *__restrict__ xl,
-                                                            const float4 *__restrict__ xm,
-                                                            uint16_t *__restrict__ out,
-                                                            uint16_t *__restrict__ g_out,
-                                                            uint16_t *__restrict__ u_out, uint32_t *err) {
-  constexpr int WB = G / 32;          // 16-byte word blocks per group
-  constexpr int WPG = G / 8;          // packed words per group
-  constexpr int RPW = DUAL ? 8 : 16;  // output rows per warp
+// Pair id of token slot 4t + c without dynamic register-array indexing.
+__device__ __forceinline__ int item_pair(const ItemInfo &it, int t, int c) {
+  if (t == 0) return c == 0 ? it.pair[0] : c == 1 ? it.pair[1] : c == 2 ? it.pair[2] : it.pair[3];
+  return c == 0 ? it.pair[4] : c == 1 ? it.pair[5] : c == 2 ? it.pair[6] : it.pair[7];
+}
+
+// Multiply one item's rows for NT token tiles (4 pairs each) and write the
+// results.  The packed words of the two MMA rows stream through a PF-deep
+// register ring; scales/biases arrive as PF-wide vectors one block ahead.
+template <int G, int WARPS, bool DUAL, int PF, int NT>
+__device__ __forceinline__ void run_item(const ExpertCallArgs &a, const ItemInfo &cur, const uint8_t *st,
+                                         const XStage &xs, int O, int K, uint16_t *__restrict__ out,
+                                         uint16_t *__restrict__ g_out, uint16_t *__restrict__ u_out) {
+  constexpr int WB = G / 32;
+  constexpr int WPG = G / 8;
+  constexpr int RPW = DUAL ? 8 : 16;
   constexpr int ROWS = RPW * WARPS;
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int H = a.H, I = a.I;
-  const int K = DUAL ? H : I;
-  const int O = DUAL ? I : H;
-  const XStage xs = xstage_geom(K, G);
   const int Gc = xs.Gc;
   const int P = chain_count(Gc);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
-  const int row_tiles = (O + ROWS - 1) / ROWS;
-  const int n_items = gv.n_tiles[0] * row_tiles;
-  const int wpr = K / 8;  // packed words per row
-
-  int item = blockIdx.x;
-  ItemInfo cur = item_info<DUAL>(a, load_desc(gv, item, n_items, row_tiles), item, n_items, row_tiles, O, K);
-  RawDesc raw_next = load_desc(gv, item + gridDim.x, n_items, row_tiles);
-  load_xstage(smem, xs, cur, xl, xm, a.n_pairs, a.slots, DUAL);
-  cp_async_commit();
-  for (int k = 0; cur.valid; ++k) {
-    const uint8_t *st = smem + (k & 1) * xs.bytes;
-    const int nitem = item + gridDim.x;
-    const ItemInfo nxt = item_info<DUAL>(a, raw_next, nitem, n_items, row_tiles, O, K);
-    raw_next = load_desc(gv, nitem + gridDim.x, n_items, row_tiles);
-    load_xstage(smem + ((k + 1) & 1) * xs.bytes, xs, nxt, xl, xm, a.n_pairs, a.slots, DUAL);
-    cp_async_commit();
-    if (!cur.ok) {
-      if (threadIdx.x == 0) set_error(err, kErrBadRoute);
-      cp_async_wait1();
-      __syncthreads();
-      __syncthreads();
-      item = nitem;
-      cur = nxt;
-      continue;
+  const int wpr = K / 8;
+  const int o0 = cur.rt * ROWS + warp * RPW + r;
+  const int oA = o0;
+  const int oB = DUAL ? o0 : o0 + 8;
+  const int cA = min(oA, O - 1), cB = min(oB, O - 1);
+  const Ptrs &pA = cur.p[0];
+  const Ptrs &pB = DUAL ? cur.p[1] : cur.p[0];
+  const uint32_t *wA = pA.w + static_cast<size_t>(cA) * wpr + c;
+  const uint32_t *wB = pB.w + static_cast<size_t>(cB) * wpr + c;
+  const uint16_t *sA = pA.s + static_cast<size_t>(cA) * Gc;
+  const uint16_t *bA = pA.b + static_cast<size_t>(cA) * Gc;
+  const uint16_t *sB = pB.s + static_cast<size_t>(cB) * Gc;
+  const uint16_t *bB = pB.b + static_cast<size_t>(cB) * Gc;
+  uint32_t qa[PF][WB], qb[PF][WB];
+#pragma unroll
+  for (int j = 0; j < PF; ++j) {
+#pragma unroll
+    for (int wb = 0; wb < WB; ++wb) {
+      qa[j][wb] = ldg_u32(wA + j * WPG + wb * 4);
+      qb[j][wb] = ldg_u32(wB + j * WPG + wb * 4);
     }
-    // This warp's two MMA rows (clamped in range; rows past O are not stored).
-    const int o0 = cur.rt * ROWS + warp * RPW + r;
-    const int oA = o0;
-    const int oB = DUAL ? o0 : o0 + 8;
-    const int cA = min(oA, O - 1), cB = min(oB, O - 1);
-    const Ptrs &pA = cur.p[0];
-    const Ptrs &pB = DUAL ? cur.p[1] : cur.p[0];
-    const uint32_t *wA = pA.w + static_cast<size_t>(cA) * wpr + c;
-    const uint32_t *wB = pB.w + static_cast<size_t>(cB) * wpr + c;
-    const uint16_t *sA = pA.s + static_cast<size_t>(cA) * Gc;
-    const uint16_t *bA = pA.b + static_cast<size_t>(cA) * Gc;
-    const uint16_t *sB = pB.s + static_cast<size_t>(cB) * Gc;
-    const uint16_t *bB = pB.b + static_cast<size_t>(cB) * Gc;
-    uint32_t qa[PF][WB], qb[PF][WB];
+  }
+  Vec16<PF> vsA, vbA, vsB, vbB;
+  vsA.load(sA);
+  vbA.load(bA);
+  vsB.load(sB);
+  vbB.load(bB);
+  const uint8_t *xb = st + (r >> 1) * xs.Xrow + (r & 1) * (G * 2) + c * 16;
+  const float4 *mrow = reinterpret_cast<const float4 *>(st + xs.m_off + c * xs.Mp);
+  // Chain tree folded as chains complete: h0 = c0 (+ c2), h1 = c1 (+ c3).
+  float hA0[NT], hA1[NT], hB0[NT], hB1[NT];
 #pragma unroll
-    for (int j = 0; j < PF; ++j) {
+  for (int t = 0; t < NT; ++t) hA0[t] = hA1[t] = hB0[t] = hB1[t] = -0.0f;
+  for (int ch = 0; ch < P; ++ch) {
+    float accA[NT], accB[NT];
 #pragma unroll
-      for (int wb = 0; wb < WB; ++wb) {
-        qa[j][wb] = ldg_u32(wA + j * WPG + wb * 4);
-        qb[j][wb] = ldg_u32(wB + j * WPG + wb * 4);
-      }
-    }
-    Vec16<PF> vsA, vbA, vsB, vbB;
-    vsA.load(sA);
-    vbA.load(bA);
-    vsB.load(sB);
-    vbB.load(bB);
-    cp_async_wait1();
-    __syncthreads();  // activation stage of this item is visible
-    const uint8_t *xb = st + (r >> 1) * xs.Xrow + (r & 1) * (G * 2) + c * 16;
-    const float4 *mrow = reinterpret_cast<const float4 *>(st + xs.m_off + c * xs.Mp);
-    float chA[4] = {-0.0f, -0.0f, -0.0f, -0.0f}, chB[4] = {-0.0f, -0.0f, -0.0f, -0.0f};
-    for (int ch = 0; ch < P; ++ch) {
-      float accA = -0.0f, accB = -0.0f;
-      const int gend = chain_begin(ch + 1, P, Gc);
-      for (int g0 = chain_begin(ch, P, Gc); g0 < gend; g0 += PF) {
-        const int gn0 = (g0 + PF < Gc) ? g0 + PF : g0;  // next block (re-read the last one at the end)
-        Vec16<PF> nsA, nbA, nsB, nbB;
-        nsA.load(sA + gn0);
-        nbA.load(bA + gn0);
-        nsB.load(sB + gn0);
-        nbB.load(bB + gn0);
-        const uint32_t *nwA = wA + gn0 * WPG;
-        const uint32_t *nwB = wB + gn0 * WPG;
-        const uint8_t *xg = xb + g0 * (4 * G);
-        const float4 *mg = mrow + g0;
+    for (int t = 0; t < NT; ++t) accA[t] = accB[t] = -0.0f;
+    const int gend = chain_begin(ch + 1, P, Gc);
+    for (int g0 = chain_begin(ch, P, Gc); g0 < gend; g0 += PF) {
+      const int gn0 = (g0 + PF < Gc) ? g0 + PF : g0;  // next block (the last one is re-read)
+      Vec16<PF> nsA, nbA, nsB, nbB;
+      nsA.load(sA + gn0);
+      nbA.load(bA + gn0);
+      nsB.load(sB + gn0);
+      nbB.load(bB + gn0);
+      const uint32_t *nwA = wA + gn0 * WPG;
+      const uint32_t *nwB = wB + gn0 * WPG;
+      const uint8_t *xg = xb + g0 * (4 * G);
+      const float4 *mg = mrow + g0;
 #pragma unroll
-        for (int j = 0; j < PF; ++j) {
-          uint32_t w0[WB], w1[WB];
+      for (int j = 0; j < PF; ++j) {
+        uint32_t A0[WB][4], A1[WB][4];
 #pragma unroll
-          for (int wb = 0; wb < WB; ++wb) {
-            w0[wb] = qa[j][wb];
-            w1[wb] = qb[j][wb];
-            qa[j][wb] = ldg_u32(nwA + j * WPG + wb * 4);
-            qb[j][wb] = ldg_u32(nwB + j * WPG + wb * 4);
-          }
+        for (int wb = 0; wb < WB; ++wb) {
+          nibble_operands(qa[j][wb], qb[j][wb], A0[wb], A1[wb]);
+          qa[j][wb] = ldg_u32(nwA + j * WPG + wb * 4);
+          qb[j][wb] = ldg_u32(nwB + j * WPG + wb * 4);
+        }
+        const float s0 = vsA.get(j), b0 = vbA.get(j), s1 = vsB.get(j), b1 = vbB.get(j);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
           float C[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
           for (int wb = 0; wb < WB; ++wb) {
-            uint32_t pa[4], pb[4];
-            nibble_pairs4(w0[wb], pa);
-            nibble_pairs4(w1[wb], pb);
-            const uint4 v = *reinterpret_cast<const uint4 *>(xg + j * (4 * G) + wb * 64);
-            const uint32_t A0[4] = {pa[0], pb[0], pa[1], pb[1]};
-            const uint32_t A1[4] = {pa[2], pb[2], pa[3], pb[3]};
-            mma_16816(C, A0, v.x, v.y);
-            mma_16816(C, A1, v.z, v.w);
+            const uint4 v = *reinterpret_cast<const uint4 *>(xg + t * 4 * xs.Xrow + j * (4 * G) + wb * 64);
+            mma_16816(C, A0[wb], v.x, v.y);
+            mma_16816(C, A1[wb], v.z, v.w);
           }
-          const float4 m = mg[j];
-          accA = __fadd_rn(accA, group_term(C[0], C[1], vsA.get(j), vbA.get(j), m));
-          accB = __fadd_rn(accB, group_term(C[2], C[3], vsB.get(j), vbB.get(j), m));
+          const float4 m = *reinterpret_cast<const float4 *>(
+              reinterpret_cast<const uint8_t *>(mg + j) + t * 4 * xs.Mp);
+          accA[t] = group_fold(accA[t], C[0], C[1], s0, b0, m);
+          accB[t] = group_fold(accB[t], C[2], C[3], s1, b1, m);
         }
-        vsA = nsA;
-        vbA = nbA;
-        vsB = nsB;
-        vbB = nbB;
       }
-      if (ch == 0) { chA[0] = accA; chB[0] = accB; }
-      else if (ch == 1) { chA[1] = accA; chB[1] = accB; }
-      else if (ch == 2) { chA[2] = accA; chB[2] = accB; }
-      else { chA[3] = accA; chB[3] = accB; }
+      vsA = nsA;
+      vbA = nbA;
+      vsB = nsB;
+      vbB = nbB;
     }
-    if (c < cur.len) {
-      const int pair = c == 0 ? cur.pair[0] : c == 1 ? cur.pair[1] : c == 2 ? cur.pair[2] : cur.pair[3];
-      const float yA = chain_tree(chA, P);
-      const float yB = chain_tree(chB, P);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      if (ch == 0) { hA0[t] = accA[t]; hB0[t] = accB[t]; }
+      else if (ch == 1) { hA1[t] = accA[t]; hB1[t] = accB[t]; }
+      else if (ch == 2) { hA0[t] = __fadd_rn(hA0[t], accA[t]); hB0[t] = __fadd_rn(hB0[t], accB[t]); }
+      else { hA1[t] = __fadd_rn(hA1[t], accA[t]); hB1[t] = __fadd_rn(hB1[t], accB[t]); }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const int q = 4 * t + c;
+    if (q < cur.len) {
+      const int pair = item_pair(cur, t, c);
+      const float yA = P == 1 ? hA0[t] : __fadd_rn(hA0[t], hA1[t]);
+      const float yB = P == 1 ? hB0[t] : __fadd_rn(hB0[t], hB1[t]);
       if (DUAL) {
         if (oA < O) {
           const float gvv = round_bf16(yA), uvv = round_bf16(yB);
@@ -651,6 +644,46 @@ __global__ void __launch_bounds__(WARPS * 32) k_expert_rows(ExpertCallArgs a, Gr
         if (oA < O) out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(yA);
         if (oB < O) out[static_cast<size_t>(pair) * O + oB] = f32_to_bf16(yB);
       }
+    }
+  }
+}
+
+template <int G, int WARPS, bool DUAL, int PF>
+__global__ void __launch_bounds__(WARPS * 32) k_expert_rows(ExpertCallArgs a, GroupView gv,
+                                                            const uint16_t *__restrict__ xl,
+                                                            const float4 *__restrict__ xm,
+                                                            uint16_t *__restrict__ out,
+                                                            uint16_t *__restrict__ g_out,
+                                                            uint16_t *__restrict__ u_out, uint32_t *err) {
+  constexpr int RPW = DUAL ? 8 : 16;
+  constexpr int ROWS = RPW * WARPS;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int K = DUAL ? a.H : a.I;
+  const int O = DUAL ? a.I : a.H;
+  const XStage xs = xstage_geom(K, G);
+  const int row_tiles = (O + ROWS - 1) / ROWS;
+  const int n_items = gv.n_tiles[0] * row_tiles;
+
+  int item = blockIdx.x;
+  ItemInfo cur = item_info<DUAL>(a, load_desc(gv, item, n_items, row_tiles), item, n_items, row_tiles, O, K);
+  RawDesc raw_next = load_desc(gv, item + gridDim.x, n_items, row_tiles);
+  load_xstage(smem, xs, cur, xl, xm, a.n_pairs, a.slots, DUAL);
+  cp_async_commit();
+  for (int k = 0; cur.valid; ++k) {
+    const uint8_t *st = smem + (k & 1) * xs.bytes;
+    const int nitem = item + gridDim.x;
+    const ItemInfo nxt = item_info<DUAL>(a, raw_next, nitem, n_items, row_tiles, O, K);
+    raw_next = load_desc(gv, nitem + gridDim.x, n_items, row_tiles);
+    load_xstage(smem + ((k + 1) & 1) * xs.bytes, xs, nxt, xl, xm, a.n_pairs, a.slots, DUAL);
+    cp_async_commit();
+    cp_async_wait1();
+    __syncthreads();  // activation stage of this item is visible
+    if (!cur.ok) {
+      if (threadIdx.x == 0) set_error(err, kErrBadRoute);
+    } else if (cur.len > 4) {
+      run_item<G, WARPS, DUAL, PF, 2>(a, cur, st, xs, O, K, out, g_out, u_out);
+    } else {
+      run_item<G, WARPS, DUAL, PF, 1>(a, cur, st, xs, O, K, out, g_out, u_out);
     }
     __syncthreads();  // the stage is refilled two items later
     item = nitem;
@@ -718,12 +751,12 @@ cudaError_t launch_gate_up(const ExpertCallArgs &a, const GroupView &gv,
   const size_t smem = 2 * static_cast<size_t>(xs.bytes);
   if (smem > kSmemBudget) return cudaErrorInvalidValue;
   const bool wide = (a.n_pairs + a.tokens) >= 64;
-  const int pf = pick_pf(a.H, a.G);
+  const int pf = std::min(4, pick_pf(a.H, a.G));
   if (a.G == 32) {
-    if (wide) return launch_rows_pf<32, 8, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
+    if (wide) return launch_rows_pf<32, 16, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
     return launch_rows_pf<32, 4, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
   }
-  if (wide) return launch_rows_pf<64, 8, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
+  if (wide) return launch_rows_pf<64, 16, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
   return launch_rows_pf<64, 4, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
 }
 
@@ -736,10 +769,10 @@ cudaError_t launch_down(const ExpertCallArgs &a, const GroupView &gv,
   const bool wide = (a.n_pairs + a.tokens) >= 64;
   const int pf = pick_pf(a.I, a.G);
   if (a.G == 32) {
-    if (wide) return launch_rows_pf<32, 8, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
+    if (wide) return launch_rows_pf<32, 16, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
     return launch_rows_pf<32, 4, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
   }
-  if (wide) return launch_rows_pf<64, 8, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
+  if (wide) return launch_rows_pf<64, 16, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
   return launch_rows_pf<64, 4, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
 }
 

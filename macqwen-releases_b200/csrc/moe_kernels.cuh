@@ -8,8 +8,8 @@ namespace fnmoe {
 
 // Key assigned to the shared expert's bin in grouping.
 constexpr uint32_t kSharedKey = 0xFFFFFFFFu;
-// Pairs per grouped work item: one 4-token MMA tile (N = 4 tokens x 2 limbs).
-constexpr int kTokPerItem = 4;
+// Pairs per grouped work item: up to two 4-token MMA tiles (N = 4 tokens x 2 limbs).
+constexpr int kTokPerItem = 8;
 
 // Pointers of one Q4 projection family.
 struct ProjArrays {
@@ -32,7 +32,7 @@ struct GroupView {
   int32_t *counts;     // [n_bins]
   int32_t *offsets;    // [n_bins + 1]
   int32_t *order;      // [n_total]   pair ids sorted by bin
-  int4 *tiles;         // [2 * max_tiles] {route key, start, len, bin}, {pair ids}
+  int4 *tiles;         // [3 * max_tiles] {route key, start, len, bin}, {pair ids 0-3}, {pair ids 4-7}
   int32_t *n_tiles;    // [1]
   uint32_t *bin_key;   // [n_bins]    route key of each bin
   int n_bins;
@@ -49,7 +49,7 @@ cudaError_t ensure_exp_table(cudaStream_t stream);
 uint32_t *device_error_word();
 
 // Fixed-point limbs of bf16 rows: limbs [rows][groups][2][G] fp16 (fragment
-// order), meta [rows][groups] float4 {fl(SX), 2^k or 0, k (int bits), 0}.
+// order), meta [rows][groups] float4 {fl(SX), A, B, 0} with A*B = 2^k (see scale_pow2).
 cudaError_t launch_prep_rows(const uint16_t *rows, int n_rows, int K, int G,
                              uint16_t *limbs, float4 *meta, cudaStream_t s);
 

@@ -90,7 +90,7 @@ def group_tokens(routes, array_experts: int, table_records: int = 0):
     counts = torch.empty(keys, dtype=torch.int32, device="cuda")
     offsets = torch.empty(keys + 1, dtype=torch.int32, device="cuda")
     order = torch.empty(pairs, dtype=torch.int32, device="cuda")
-    ws = torch.empty((pairs + 2 * keys + 64) * 16 + 4096, dtype=torch.uint8, device="cuda")
+    ws = torch.empty((2 * pairs + 4 * keys + 64) * 16 + 4096, dtype=torch.uint8, device="cuda")
     _lib.check(lib.fnmoe_group_tokens(rt.data_ptr(), pairs, array_experts, table_records, counts.data_ptr(),
                                       offsets.data_ptr(), order.data_ptr(), ws.data_ptr(), ws.numel(),
                                       _stream()), "group_tokens")

@@ -26,12 +26,16 @@ one projection row with packed codes ``q`` and bfloat16 ``s``/``b`` per group:
    below 2**23 in magnitude; exact for every bfloat16 input within 2**-15 of
    the group maximum);
    ``S = sum_i X_i*q_i`` and ``SX = sum_i X_i`` (exact integers);
-   ``t = fl(fl(s*fl(S)) + fl(b*fl(SX)))``; ``term_g = fl(t * 2**(E-22))``.
-   ``fl`` is float32 round-to-nearest-even.  The group sums are exact, so they
-   do not depend on any summation order;
+   ``t = fma(s, fl(S), fl(b*fl(SX)))``; ``u = fl(t * A)`` with
+   ``A*B = 2**(E-22)``, ``A = 2**max(E-22, -126)`` (so ``B = 1`` unless the
+   group's largest activation is below 2**-104).  ``fl`` is float32
+   round-to-nearest-even and ``fma`` a float32 fused multiply-add (one
+   rounding).  The group sums are exact, so they do not depend on any
+   summation order;
 2. ``P = min(4, 2**floor(log2(K/G)))`` chains over contiguous blocks of
-   groups: chain j adds ``term_g`` for every g with ``(g*P) // (K/G) == j`` in
-   increasing g, starting from ``-0.0``;
+   groups: chain j starts at ``-0.0`` and, for every g with
+   ``(g*P) // (K/G) == j`` in increasing g, becomes ``fma(u_g, B_g, chain)``
+   (``= fl(chain + u_g)`` when ``B_g = 1``);
 3. ``y = (c0 + c2) + (c1 + c3)`` for P = 4, ``c0 + c1`` for P = 2, ``c0`` for P = 1.
 
 Router dot products (bfloat16 weights) are exact per product and summed in a
@@ -168,9 +172,45 @@ def limbs(X):
     return l0, l1
 
 
-def _scale_pow2(t, k):
-    """fl(t * 2**k) for float32 t and integer k (one correct rounding)."""
-    return (np.asarray(t, np.float64) * np.ldexp(1.0, k.astype(np.int32))).astype(np.float32)
+def fma32(a, b, c):
+    """float32 fused multiply-add ``fl(a*b + c)`` with a single rounding, exactly.
+
+    The product of two float32 values is exact in float64; the float64 sum's
+    rounding error is recovered with TwoSum, and the one case where float64
+    rounding can mislead the final float32 rounding -- a float64 sum that
+    lands exactly on a float32 midpoint -- is resolved by the error's sign.
+    """
+    a64 = np.asarray(a, np.float32).astype(np.float64)
+    b64 = np.asarray(b, np.float32).astype(np.float64)
+    c64 = np.asarray(c, np.float32).astype(np.float64)
+    with np.errstate(all="ignore"):
+        p = a64 * b64
+        s = p + c64
+        bv = s - p
+        e = (p - (s - bv)) + (c64 - bv)
+        r = s.astype(np.float32)
+        r64 = r.astype(np.float64)
+        up = np.nextafter(r, np.float32(np.inf)).astype(np.float64)
+        dn = np.nextafter(r, np.float32(-np.inf)).astype(np.float64)
+        d = s - r64
+        tie_up = (d > 0) & (d * 2 == up - r64)    # s halfway between r and the next float32 up
+        tie_dn = (d < 0) & (-d * 2 == r64 - dn)   # s halfway between r and the next float32 down
+        out = np.where(tie_up & (e > 0), up, np.where(tie_dn & (e < 0), dn, r64))
+        # halfway and the error points back: r (the even neighbour) already
+        # sits on the other side only if RN chose away from the true value.
+        out = np.where(tie_up & (e < 0), r64, out)
+        out = np.where(tie_dn & (e > 0), r64, out)
+    return out.astype(np.float32)
+
+
+def scale_factors(k):
+    """(A, B) float32 with A*B = 2**k: A = 2**max(k, -126), B = 2**(k - max(k, -126))."""
+    k = np.asarray(k).astype(np.int32)
+    ka = np.maximum(k, -126)
+    return np.ldexp(np.float32(1.0), ka).astype(np.float32), np.ldexp(np.float32(1.0), k - ka).astype(np.float32)
+
+
+
 
 
 def _tree(chains):
@@ -199,17 +239,21 @@ def qmv(x, codes, scales, biases, group_size: int = 32) -> np.ndarray:
     S = np.matmul(X.transpose(1, 0, 2), qf.transpose(1, 2, 0))
     fS = S.astype(np.float32).transpose(1, 2, 0)          # [N, O, Gc]
     fSX = X.sum(axis=-1).astype(np.float32)               # [N, Gc]
-    s = np.asarray(scales, np.float32)[None]              # [1, O, Gc]
+    s = np.broadcast_to(np.asarray(scales, np.float32)[None], fS.shape)   # [N, O, Gc]
     b = np.asarray(biases, np.float32)[None]
     with np.errstate(all="ignore"):
-        t = (s * fS) + (b * fSX[:, None, :])
-    term = _scale_pow2(t, (emax - 22)[:, None, :])
+        pb = (b * fSX[:, None, :]).astype(np.float32)
+    t = fma32(s, fS, pb)
+    A, B = scale_factors((emax - 22)[:, None, :])
+    with np.errstate(all="ignore"):
+        u = (t * A).astype(np.float32)
+    B = np.broadcast_to(B, u.shape)
     p = chain_count(gc)
     chains = [np.full((n, o), -0.0, dtype=np.float32) for _ in range(p)]
+    for g in range(gc):
+        j = (g * p) // gc
+        chains[j] = fma32(u[:, :, g], B[:, :, g], chains[j])
     with np.errstate(all="ignore"):
-        for g in range(gc):
-            j = (g * p) // gc
-            chains[j] = chains[j] + term[:, :, g]
         return _tree(chains).astype(np.float32)
 
 

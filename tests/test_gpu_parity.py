@@ -361,3 +361,23 @@ def test_paged_decode_matches_oracle_and_truth(cuda_lib, batch, hq, hkv, d, page
         v = vc[pages].reshape(-1, hkv, d)[:n]
         truth = attn.dense_truth(_np(P.q)[b], k, v, P.scale)
         assert np.abs(got[b] - truth).max() / np.abs(truth).max() < 1.5e-2
+
+
+def test_executor_tiny_and_subnormal_activations_bit_exact(cuda_lib):
+    """Groups whose largest activation is below 2^-104 take the two-step
+    power-of-two scaling; bfloat16 subnormals enter the fixed point exactly."""
+    import torch
+
+    from flashnext_b200 import MoEExecutor
+    bank, x, routes, scores = _executor_case(3, 4, 256, 128, 6, 32, seed=51)
+    x = x.clone()
+    x[0] = (x[0].float() * 2.0 ** -110).to(torch.bfloat16)      # tiny but normal
+    x[1, :64] = (x[1, :64].float() * 2.0 ** -128).to(torch.bfloat16)  # partly subnormal
+    x[2, 32:64] = 0                                              # an all-zero group
+    ex = MoEExecutor(6, 256, 4)
+    nb = _bank_np(bank)
+    g, u, d = ex.execute(x, torch.tensor(routes).cuda(), bank, return_all=True)
+    og, ou, od = moe.executor(_np(x), routes, nb["gate_proj"], nb["up_proj"], nb["down_proj"], return_all=True)
+    assert_bf16_equal(_np(g), og, "gate")
+    assert_bf16_equal(_np(u), ou, "up")
+    assert_bf16_equal(_np(d), od, "down")
