@@ -26,6 +26,9 @@
  *   fnmoe_dequantize         mx.dequantize affine Q4 (metal_runtime.py:751-758)
  *   fnmoe_swiglu             fused up-SwiGLU bfloat16 epilogue (metal_runtime.py:262-285)
  *   fnmoe_paged_decode       paged_attention decode (models/qwen27b/paged_kv.py:417-495)
+ *   fnmoe_tile_experts       no direct counterpart: the B200 analogue of packing
+ *       expert records once for fast reads (models/flashnext/slab_pack.py:96-153),
+ *       into a tile-major HBM layout the decode kernels stream with bulk copies
  */
 #ifndef FNMOE_H
 #define FNMOE_H
@@ -43,7 +46,7 @@ extern "C" {
 #define FNMOE_API
 #endif
 
-#define FNMOE_ABI_VERSION 1u
+#define FNMOE_ABI_VERSION 2u
 
 /* Status codes (negative = failure), mirroring the native bridge's
  * "0 ok / negative specific failure" convention. */
@@ -132,6 +135,21 @@ typedef struct FnMoEArgs {
   uint64_t workspace_bytes;
 } FnMoEArgs;
 
+/* Tiled expert tables: the routed experts' projections (and optionally the
+ * shared expert's, as the last record) repacked once by fnmoe_tile_experts
+ * into one 2560-byte chunk per (row group, 128-byte block) in MMA fragment
+ * order, scales and biases included.  Record r of gate_up holds expert r's
+ * gate and up rows (inter/8 groups of 8 + 8 rows), record r of down its down
+ * rows (hidden/16 groups of 16).  Sizes: fnmoe_tiled_record_bytes. */
+typedef struct FnTiledExperts {
+  const void *gate_up;         /* [records][gate_up_record_bytes], 16-byte aligned, or NULL */
+  const void *down;            /* [records][down_record_bytes], 16-byte aligned */
+  uint64_t gate_up_record_bytes;
+  uint64_t down_record_bytes;
+  uint32_t records;            /* expert_count, +1 when the shared expert is the last record */
+  uint32_t has_shared;         /* 1: the last record is the shared expert */
+} FnTiledExperts;
+
 /* A whole sparse-MoE block: router -> top-k -> renorm -> routed experts +
  * sigmoid-gated shared expert -> combine. */
 typedef struct FnMoELayerArgs {
@@ -161,7 +179,26 @@ typedef struct FnMoELayerArgs {
   void *scores_out;            /* optional [tokens, top_k] bf16 (renormalised) */
   void *workspace;
   uint64_t workspace_bytes;
+  /* When tiled.gate_up != NULL the routed (and, with has_shared, the shared)
+   * expert projections come from these tables; the *_weight arrays and
+   * `table` are then ignored / must be NULL respectively. */
+  FnTiledExperts tiled;
 } FnMoELayerArgs;
+
+/* Repack experts [0, experts) of reference-layout projection arrays into
+ * records [first_record, first_record + experts) of tiled tables. */
+typedef struct FnTileArgs {
+  uint32_t abi_version;
+  uint32_t experts;
+  uint32_t hidden_size;
+  uint32_t inter_size;         /* multiple of 8; hidden a multiple of 16 */
+  uint32_t group_size;         /* 32 or 64 */
+  uint32_t first_record;
+  const uint32_t *gate_weight; const void *gate_scales; const void *gate_biases;
+  const uint32_t *up_weight; const void *up_scales; const void *up_biases;
+  const uint32_t *down_weight; const void *down_scales; const void *down_biases;
+  FnTiledExperts tiled;        /* destination tables (records = capacity) */
+} FnTileArgs;
 
 /* Paged-KV decode attention (one query token per sequence). */
 typedef struct FnPagedArgs {
@@ -236,6 +273,12 @@ FNMOE_API int fnmoe_group_tokens(const uint32_t *routes, uint32_t pairs,
 
 FNMOE_API int fnmoe_moe_layer_workspace_size(const FnMoELayerArgs *args, uint64_t *bytes);
 FNMOE_API int fnmoe_moe_layer(const FnMoELayerArgs *args, void *stream);
+
+/* Bytes of one tiled record for these sizes (no device work). */
+FNMOE_API int fnmoe_tiled_record_bytes(uint32_t hidden_size, uint32_t inter_size, uint32_t group_size,
+                                       uint64_t *gate_up_record_bytes, uint64_t *down_record_bytes);
+/* Repack projections into tiled tables on `stream` (see FnTileArgs). */
+FNMOE_API int fnmoe_tile_experts(const FnTileArgs *args, void *stream);
 
 /* Affine Q4 dequantisation to bf16: out[r, k] = bf16(s*q + b), rounded once. */
 FNMOE_API int fnmoe_dequantize(const uint32_t *weight, const void *scales,

@@ -17,6 +17,7 @@
 
 #include "../../include/fnmoe.h"
 #include "attention.cuh"
+#include "common.cuh"
 #include "moe_kernels.cuh"
 
 using namespace fnmoe;
@@ -100,13 +101,13 @@ bool device_ok(std::string &why) {
 struct Layout {
   // activations
   uint16_t *xl;
-  float4 *xm;
+  float *xm;
   // grouping
   GroupView gv;
   // intermediates
   uint16_t *act;
   uint16_t *al;
-  float4 *am;
+  float *am;
   uint16_t *d;
 };
 
@@ -115,7 +116,7 @@ void carve_core(Carver &cv, Layout &L, int T, int H, int I, int G, int n_total, 
                 bool need_d) {
   const int Gh = H / G, Gi = I / G;
   L.xl = cv.take<uint16_t>(static_cast<uint64_t>(T) * Gh * 2 * G);
-  L.xm = cv.take<float4>(static_cast<uint64_t>(T) * Gh);
+  L.xm = cv.take<float>(static_cast<uint64_t>(T) * meta_pitch(Gh));
   L.gv.n_bins = n_bins;
   L.gv.max_tiles = n_total / kTokPerItem + (n_bins < n_total ? n_bins : n_total) + 1;
   L.gv.counts = cv.take<int32_t>(n_bins);
@@ -126,7 +127,7 @@ void carve_core(Carver &cv, Layout &L, int T, int H, int I, int G, int n_total, 
   L.gv.bin_key = cv.take<uint32_t>(n_bins);
   L.act = cv.take<uint16_t>(static_cast<uint64_t>(n_total) * I);
   L.al = cv.take<uint16_t>(static_cast<uint64_t>(n_total) * Gi * 2 * G);
-  L.am = cv.take<float4>(static_cast<uint64_t>(n_total) * Gi);
+  L.am = cv.take<float>(static_cast<uint64_t>(n_total) * meta_pitch(Gi));
   L.d = need_d ? cv.take<uint16_t>(static_cast<uint64_t>(n_total) * H) : nullptr;
 }
 
@@ -190,6 +191,45 @@ uint64_t moe_workspace(const FnMoEArgs *a) {
   const bool per_slot = (a->flags & (FNMOE_FLAG_RETURN_ALL | FNMOE_FLAG_NO_COMBINE)) || a->scores == nullptr;
   carve_core(cv, L, a->tokens, a->hidden_size, a->inter_size, a->group_size, n_total, n_bins, !per_slot);
   return cv.off + 256;
+}
+
+bool aligned(const void *p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) & (n - 1)) == 0; }
+
+// The expert kernels copy packed rows in 16-byte pieces and scale/bias rows
+// in 4-byte pieces.  Rows of K/8 words are 16-byte multiples (K is a multiple
+// of 32), so only the bases (and table offsets/strides) need checking; scale
+// and bias rows additionally need an even group count for 4-byte copies,
+// which the kernels check per projection.
+int check_expert_alignment(ExpertCallArgs &c) {
+  bool w_ok = true, sb_ok = true, sb16 = true;
+  auto arr = [&](const ProjArrays &pa) {
+    if (pa.w == nullptr) return;
+    w_ok = w_ok && aligned(pa.w, 16);
+    sb_ok = sb_ok && aligned(pa.s, 4) && aligned(pa.b, 4);
+    sb16 = sb16 && aligned(pa.s, 16) && aligned(pa.b, 16);
+  };
+  arr(c.gate);
+  arr(c.up);
+  arr(c.down);
+  arr(c.sh_gate);
+  arr(c.sh_up);
+  arr(c.sh_down);
+  for (const TableView *t : {&c.table, &c.stream}) {
+    if (t->base == nullptr) continue;
+    const uintptr_t b = reinterpret_cast<uintptr_t>(t->base) + t->header;
+    w_ok = w_ok && (t->stride % 16) == 0;
+    sb_ok = sb_ok && (t->stride % 4) == 0;
+    sb16 = sb16 && (t->stride % 16) == 0;
+    for (int part = 0; part < 3; ++part) {
+      w_ok = w_ok && ((b + t->off[3 * part]) % 16) == 0;
+      sb_ok = sb_ok && ((b + t->off[3 * part + 1]) % 4) == 0 && ((b + t->off[3 * part + 2]) % 4) == 0;
+      sb16 = sb16 && ((b + t->off[3 * part + 1]) % 16) == 0 && ((b + t->off[3 * part + 2]) % 16) == 0;
+    }
+  }
+  if (!w_ok) return fail(FNMOE_ERR_VALUE, "packed expert weights must start on 16-byte boundaries");
+  c.sb_async = sb_ok ? 1 : 0;
+  c.sb_bulk = (sb_ok && sb16) ? 1 : 0;
+  return FNMOE_OK;
 }
 
 ExpertCallArgs make_call(const FnMoEArgs *a) {
@@ -280,6 +320,7 @@ int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
   carve_core(cv, L, T, H, I, G, n_pairs, n_bins, !per_slot);
   uint16_t *d = per_slot ? static_cast<uint16_t *>(a->down_out) : L.d;
   ExpertCallArgs call = make_call(a);
+  if (int rc = check_expert_alignment(call)) return rc;
 
   {
     Prof p("prep_x", s);
@@ -412,13 +453,30 @@ int validate_layer(const FnMoELayerArgs *a) {
   if (a->expert_count == 0 || a->expert_count > 1024) return fail(FNMOE_ERR_SHAPE, "expert_count must be in 1..1024");
   if (a->top_k == 0 || a->top_k > kMaxTopK || a->top_k > a->expert_count) return fail(FNMOE_ERR_VALUE, "top_k out of range");
   const bool has_table = a->table.base != nullptr;
-  if (!has_table && (!a->gate_weight || !a->up_weight || !a->down_weight))
+  const bool has_tiled = a->tiled.gate_up != nullptr;
+  if (has_tiled) {
+    if (has_table) return fail(FNMOE_ERR_VALUE, "provide a slab table or tiled tables, not both");
+    if (a->tiled.down == nullptr) return fail(FNMOE_ERR_NULL, "tiled tables need both gate_up and down");
+    if (a->inter_size % 8 || a->hidden_size % 16)
+      return fail(FNMOE_ERR_SHAPE, "tiled tables need inter_size % 8 == 0 and hidden_size % 16 == 0");
+    const uint64_t gu = tiled_record_bytes(a->inter_size, a->hidden_size, true);
+    const uint64_t dn = tiled_record_bytes(a->hidden_size, a->inter_size, false);
+    if (a->tiled.gate_up_record_bytes != gu || a->tiled.down_record_bytes != dn)
+      return fail(FNMOE_ERR_SHAPE, "tiled record sizes do not match hidden/inter sizes");
+    const bool sh = a->shared_inter_size != 0;
+    if ((a->tiled.has_shared != 0) != sh)
+      return fail(FNMOE_ERR_VALUE, "tiled tables must hold the shared expert exactly when the layer has one");
+    if (a->tiled.records != a->expert_count + (sh ? 1u : 0u))
+      return fail(FNMOE_ERR_SHAPE, "tiled records must be expert_count (+1 for the shared expert)");
+  } else if (!has_table && (!a->gate_weight || !a->up_weight || !a->down_weight)) {
     return fail(FNMOE_ERR_NULL, "routed experts need gate, up and down projections or a table");
+  }
   if (a->shared_inter_size) {
     if (a->shared_inter_size != a->inter_size)
       return fail(FNMOE_ERR_UNSUPPORTED, "shared expert intermediate must equal the routed intermediate");
-    if (!a->shared_gate_weight || !a->shared_up_weight || !a->shared_down_weight || !a->shared_expert_gate)
-      return fail(FNMOE_ERR_NULL, "shared expert needs gate, up, down and its sigmoid gate weight");
+    if (!a->shared_expert_gate) return fail(FNMOE_ERR_NULL, "shared expert needs its sigmoid gate weight");
+    if (!has_tiled && (!a->shared_gate_weight || !a->shared_up_weight || !a->shared_down_weight))
+      return fail(FNMOE_ERR_NULL, "shared expert needs gate, up and down projections");
   }
   const uint64_t bins = (has_table ? a->table.records : a->expert_count) + 1ull;
   if (bins > kMaxBins) return fail(FNMOE_ERR_SHAPE, "too many experts/records");
@@ -503,6 +561,17 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
   call.I = I;
   call.I_shared = shared ? static_cast<int>(a->shared_inter_size) : I;
   call.G = G;
+  if (a->tiled.gate_up != nullptr) {
+    call.tiled.gate_up = static_cast<const uint8_t *>(a->tiled.gate_up);
+    call.tiled.down = static_cast<const uint8_t *>(a->tiled.down);
+    call.tiled.gate_up_record = a->tiled.gate_up_record_bytes;
+    call.tiled.down_record = a->tiled.down_record_bytes;
+    call.tiled.records = a->tiled.records;
+    call.tiled.has_shared = a->tiled.has_shared ? 1 : 0;
+    if (!aligned(call.tiled.gate_up, 16) || !aligned(call.tiled.down, 16))
+      return fail(FNMOE_ERR_VALUE, "tiled tables must start on 16-byte boundaries");
+  }
+  if (int rc = check_expert_alignment(call)) return rc;
 
   Layout &L = LL.core;
   uint16_t *logits = a->logits_out ? static_cast<uint16_t *>(a->logits_out) : LL.logits;
@@ -636,6 +705,53 @@ int fnmoe_paged_decode_workspace_size(const FnPagedArgs *args, uint64_t *bytes) 
 
 int fnmoe_paged_decode(const FnPagedArgs *args, void *stream) {
   return paged_decode(args, static_cast<cudaStream_t>(stream), g_last_error);
+}
+
+int fnmoe_tiled_record_bytes(uint32_t hidden_size, uint32_t inter_size, uint32_t group_size,
+                             uint64_t *gate_up_record_bytes, uint64_t *down_record_bytes) {
+  if (!gate_up_record_bytes || !down_record_bytes) return fail(FNMOE_ERR_NULL, "output pointers are required");
+  if (group_size != 32 && group_size != 64) return fail(FNMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64");
+  if (hidden_size == 0 || inter_size == 0 || hidden_size % group_size || inter_size % group_size)
+    return fail(FNMOE_ERR_SHAPE, "Q4 projection inputs must be group aligned");
+  if (inter_size % 8 || hidden_size % 16)
+    return fail(FNMOE_ERR_SHAPE, "tiled tables need inter_size % 8 == 0 and hidden_size % 16 == 0");
+  *gate_up_record_bytes = tiled_record_bytes(static_cast<int>(inter_size), static_cast<int>(hidden_size), true);
+  *down_record_bytes = tiled_record_bytes(static_cast<int>(hidden_size), static_cast<int>(inter_size), false);
+  return FNMOE_OK;
+}
+
+int fnmoe_tile_experts(const FnTileArgs *a, void *stream) {
+  if (a == nullptr) return fail(FNMOE_ERR_NULL, "args is NULL");
+  if (a->abi_version != FNMOE_ABI_VERSION) return fail(FNMOE_ERR_ABI, "abi_version mismatch");
+  uint64_t gu = 0, dn = 0;
+  if (int rc = fnmoe_tiled_record_bytes(a->hidden_size, a->inter_size, a->group_size, &gu, &dn)) return rc;
+  if (a->experts == 0) return FNMOE_OK;
+  if (!a->gate_weight || !a->gate_scales || !a->gate_biases || !a->up_weight || !a->up_scales || !a->up_biases ||
+      !a->down_weight || !a->down_scales || !a->down_biases)
+    return fail(FNMOE_ERR_NULL, "gate, up and down projections with scales and biases are required");
+  if (!a->tiled.gate_up || !a->tiled.down) return fail(FNMOE_ERR_NULL, "destination tables are required");
+  if (a->tiled.gate_up_record_bytes != gu || a->tiled.down_record_bytes != dn)
+    return fail(FNMOE_ERR_SHAPE, "destination record sizes do not match hidden/inter sizes");
+  if (static_cast<uint64_t>(a->first_record) + a->experts > a->tiled.records)
+    return fail(FNMOE_ERR_SHAPE, "records past the end of the destination tables");
+  std::string why;
+  if (!device_ok(why)) return fail(FNMOE_ERR_DEVICE, why);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int H = static_cast<int>(a->hidden_size), I = static_cast<int>(a->inter_size);
+  const int G = static_cast<int>(a->group_size), E = static_cast<int>(a->experts);
+  uint8_t *gdst = static_cast<uint8_t *>(const_cast<void *>(a->tiled.gate_up)) + gu * a->first_record;
+  uint8_t *ddst = static_cast<uint8_t *>(const_cast<void *>(a->tiled.down)) + dn * a->first_record;
+  cudaError_t e = launch_tile_experts(a->gate_weight, a->up_weight, static_cast<const uint16_t *>(a->gate_scales),
+                                      static_cast<const uint16_t *>(a->gate_biases),
+                                      static_cast<const uint16_t *>(a->up_scales),
+                                      static_cast<const uint16_t *>(a->up_biases), E, I, H, G, true, gdst, gu, s);
+  if (e != cudaSuccess) return cuda_fail(e, "tile gate/up");
+  e = launch_tile_experts(a->down_weight, a->down_weight, static_cast<const uint16_t *>(a->down_scales),
+                          static_cast<const uint16_t *>(a->down_biases),
+                          static_cast<const uint16_t *>(a->down_scales),
+                          static_cast<const uint16_t *>(a->down_biases), E, H, I, G, false, ddst, dn, s);
+  if (e != cudaSuccess) return cuda_fail(e, "tile down");
+  return FNMOE_OK;
 }
 
 }  // extern "C"

@@ -83,21 +83,22 @@ __device__ __forceinline__ float swiglu_bf16(const uint16_t *tab, float g, float
   return bmul(bmul(g, sigmoid_bf16(tab, g)), u);
 }
 
-// fl(fl(t * A) * B) with A * B = 2^k, A = 2^max(k, -126): a single exact
-// scaling (B = 1) unless the group's activations are all below 2^-104.
-__device__ __forceinline__ float scale_pow2(float t, float A, float B) {
-  return __fmul_rn(__fmul_rn(t, A), B);
-}
-
 // m16n8k16 fp16 MMA, fp32 accumulate (exact here: all operands are small
 // integers and every partial sum stays below 2^24).
 __device__ __forceinline__ void mma_16816(float c[4], const uint32_t a[4],
                                           uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// The same with a zero accumulator input.
+__device__ __forceinline__ void mma_16816_z(float c[4], const uint32_t a[4],
+                                            uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
 // Nibbles j and j+4 of a packed word as an fp16x2 pair (low half = nibble j).
@@ -163,19 +164,10 @@ __device__ __forceinline__ void set_error(uint32_t *err, uint32_t bit) {
   if (err) atomicOr(err, bit);
 }
 
-// Chains: P = min(4, 2^floor(log2 G)); chain of group g = (g*P)/G.
-__host__ __device__ __forceinline__ int chain_count(int groups) {
-  return groups >= 4 ? 4 : (groups >= 2 ? 2 : 1);
-}
-__host__ __device__ __forceinline__ int chain_begin(int chain, int P, int groups) {
-  // smallest g with (g*P)/groups >= chain  ->  ceil(chain*groups/P)
-  return (chain * groups + P - 1) / P;
-}
-
-__device__ __forceinline__ float chain_tree(const float c[4], int P) {
-  if (P == 4) return __fadd_rn(__fadd_rn(c[0], c[2]), __fadd_rn(c[1], c[3]));
-  if (P == 2) return __fadd_rn(c[0], c[1]);
-  return c[0];
-}
+// Metadata row of a fixed-point input row (floats): fl(SX) of each of the
+// Gc groups, zero padding to a multiple of 4, then {A, B, 0, 0} with
+// A * B = 2^(E-22), A = 2^max(E-22, -126).
+__host__ __device__ __forceinline__ int meta_a_index(int groups) { return ((groups + 3) / 4) * 4; }
+__host__ __device__ __forceinline__ int meta_pitch(int groups) { return meta_a_index(groups) + 4; }
 
 }  // namespace fnmoe

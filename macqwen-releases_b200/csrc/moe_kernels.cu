@@ -84,89 +84,104 @@ uint32_t *device_error_word() {
 // prep_rows: block fixed point of bf16 rows, fp16 limbs in fragment order
 // ---------------------------------------------------------------------------
 
-constexpr int kNoExp = -100000;
+// Fixed-point value of one bfloat16 input for the row exponent E:
+// trunc(x * 2^(22-E)); non-finite inputs give 0 (and are flagged).
+__device__ __forceinline__ int fixed_x(uint32_t h, int E) {
+  const uint32_t ef = (h >> 7) & 0xFFu, mf = h & 0x7Fu;
+  if ((h & 0x7FFFu) == 0 || ef == 255u) return 0;
+  const uint32_t M = ef ? (mf | 0x80u) : mf;
+  const int sh = ef ? (static_cast<int>(ef) - 112 - E) : (-111 - E);
+  const uint32_t mag = sh >= 0 ? (M << sh) : ((-sh >= 31) ? 0u : (M >> (-sh)));
+  return (h & 0x8000u) ? -static_cast<int>(mag) : static_cast<int>(mag);
+}
 
+__device__ __forceinline__ uint32_t half_pair(int lo, int hi) {
+  return static_cast<uint32_t>(__half_as_ushort(__int2half_rn(lo))) |
+         (static_cast<uint32_t>(__half_as_ushort(__int2half_rn(hi))) << 16);
+}
+
+// One warp per row.  Lane l handles the 8-input slices l, l+32, ... (slice i
+// covers inputs 8i..8i+7).  Pass 1 finds the row's largest finite magnitude
+// (bfloat16 magnitudes order like their bit patterns); pass 2 writes both
+// limbs of each slice as one 16-byte store in fragment order
+// [e0,e4,e1,e5,e2,e6,e3,e7] and the per-group sums fl(SX).
 template <int G>
-__global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *__restrict__ rows,
-                                                   int n_rows, int K,
-                                                   uint16_t *__restrict__ limbs,
-                                                   float4 *__restrict__ meta,
+__global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *__restrict__ rows, int n_rows, int K,
+                                                   uint16_t *__restrict__ limbs, float *__restrict__ meta,
                                                    uint32_t *err) {
-  constexpr int PER = G / 32;
+  constexpr int LPG = G / 8;  // lanes per group
   const int lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= n_rows) return;
   const int Gc = K / G;
-  if (gw >= n_rows * Gc) return;
-  const int row = gw / Gc;
-  const int g = gw - row * Gc;
-  const uint16_t *src = rows + static_cast<size_t>(row) * K + static_cast<size_t>(g) * G;
-  uint32_t xb[PER];
-  int ex[PER];
-  int emax = kNoExp;
+  const int slices = K / 8;
+  const int mp = meta_pitch(Gc);
+  const uint4 *src = reinterpret_cast<const uint4 *>(rows + static_cast<size_t>(row) * K);
+  uint32_t mx = 0;
   bool bad = false;
+  for (int i = lane; i < slices; i += 32) {
+    const uint4 v = __ldg(src + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-  for (int p = 0; p < PER; ++p) {
-    xb[p] = src[p * 32 + lane];
-    const uint32_t ef = (xb[p] >> 7) & 0xFFu;
-    const uint32_t mf = xb[p] & 0x7Fu;
-    int e;
-    if ((xb[p] & 0x7FFFu) == 0) {
-      e = kNoExp;
-    } else if (ef == 0) {
-      e = (31 - __clz(static_cast<int>(mf))) - 133;
-    } else if (ef == 255) {
-      e = 128;
-      bad = true;
-    } else {
-      e = static_cast<int>(ef) - 127;
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t m = (w[k >> 1] >> (16 * (k & 1))) & 0x7FFFu;
+      if (m >= 0x7F80u) bad = true;
+      else mx = max(mx, m);
     }
-    ex[p] = e;
-    emax = max(emax, e);
   }
 #pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) emax = max(emax, __shfl_xor_sync(0xFFFFFFFFu, emax, off));
-  if (emax == kNoExp) emax = 0;
-  if (bad) set_error(err, kErrNonFinite);
-  int sx = 0;
+  for (int off = 16; off >= 1; off >>= 1) mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) set_error(err, kErrNonFinite);
+  int E = 0;
+  if (mx != 0) E = (mx >> 7) ? static_cast<int>(mx >> 7) - 127 : (31 - __clz(static_cast<int>(mx))) - 133;
+  float *mrow = meta + static_cast<size_t>(row) * mp;
+  const int iters = (slices + 31) / 32;
+  for (int it = 0; it < iters; ++it) {
+    const int i = it * 32 + lane;
+    int sx = 0;
+    if (i < slices) {
+      const uint4 v = __ldg(src + i);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      int X[8];
 #pragma unroll
-  for (int p = 0; p < PER; ++p) {
-    int X = 0;
-    if (ex[p] != kNoExp && !(((xb[p] >> 7) & 0xFFu) == 255u)) {
-      const uint32_t ef = (xb[p] >> 7) & 0xFFu;
-      const uint32_t mf = xb[p] & 0x7Fu;
-      const uint32_t M = ef ? (mf | 0x80u) : mf;
-      const int sh = ef ? (static_cast<int>(ef) - 112 - emax) : (-111 - emax);
-      uint32_t mag;
-      if (sh >= 0) mag = M << sh;
-      else mag = (-sh >= 31) ? 0u : (M >> (-sh));
-      X = (xb[p] & 0x8000u) ? -static_cast<int>(mag) : static_cast<int>(mag);
+      for (int k = 0; k < 8; ++k) {
+        X[k] = fixed_x((w[k >> 1] >> (16 * (k & 1))) & 0xFFFFu, E);
+        sx += X[k];
+      }
+      int l0[8], l1[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        l1[k] = ((X[k] + 2048) & 4095) - 2048;
+        l0[k] = (X[k] - l1[k]) >> 12;
+      }
+      const int g = (8 * i) / G;
+      const int within = (8 * i) - g * G;
+      uint16_t *dst = limbs + (static_cast<size_t>(row) * Gc + g) * 2 * G + within;
+      *reinterpret_cast<uint4 *>(dst) = make_uint4(half_pair(l0[0], l0[4]), half_pair(l0[1], l0[5]),
+                                                   half_pair(l0[2], l0[6]), half_pair(l0[3], l0[7]));
+      *reinterpret_cast<uint4 *>(dst + G) = make_uint4(half_pair(l1[0], l1[4]), half_pair(l1[1], l1[5]),
+                                                       half_pair(l1[2], l1[6]), half_pair(l1[3], l1[7]));
     }
-    sx += X;
-    const int l1 = ((X + 2048) & 4095) - 2048;
-    const int l0 = (X - l1) >> 12;
-    const int i = p * 32 + lane;
-    const int i32 = i & 31;
-    const int pos = (i >> 5) * 32 + (i32 >> 3) * 8 + ((i32 & 7) & 3) * 2 + ((i32 & 7) >> 2);
-    const size_t base = (static_cast<size_t>(row) * Gc + g) * 2 * G;
-    limbs[base + pos] = __half_as_ushort(__int2half_rn(l0));
-    limbs[base + G + pos] = __half_as_ushort(__int2half_rn(l1));
-  }
 #pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) sx += __shfl_xor_sync(0xFFFFFFFFu, sx, off);
+    for (int off = 1; off < LPG; off <<= 1) sx += __shfl_xor_sync(0xFFFFFFFFu, sx, off);
+    if (i < slices && (lane & (LPG - 1)) == 0) mrow[(8 * i) / G] = __int2float_rn(sx);
+  }
   if (lane == 0) {
-    const int k = emax - 22;
+    const int ai = meta_a_index(Gc);
+    for (int g = Gc; g < ai; ++g) mrow[g] = 0.0f;
+    const int k = E - 22;
     const int ka = max(k, -126);
-    const float A = __int_as_float((ka + 127) << 23);       // 2^ka, normal
-    const float B = __int_as_float((k - ka + 127) << 23);   // 2^(k-ka) in [2^-29, 1]
-    meta[static_cast<size_t>(row) * Gc + g] = make_float4(__int2float_rn(sx), A, B, 0.0f);
+    mrow[ai] = __int_as_float((ka + 127) << 23);       // A = 2^ka, normal
+    mrow[ai + 1] = __int_as_float((k - ka + 127) << 23);  // B = 2^(k-ka) in [2^-29, 1]
+    mrow[ai + 2] = 0.0f;
+    mrow[ai + 3] = 0.0f;
   }
 }
 
 cudaError_t launch_prep_rows(const uint16_t *rows, int n_rows, int K, int G,
-                             uint16_t *limbs, float4 *meta, cudaStream_t s) {
-  const long long warps = static_cast<long long>(n_rows) * (K / G);
-  if (warps <= 0) return cudaSuccess;
-  const int blocks = static_cast<int>((warps + 7) / 8);
+                             uint16_t *limbs, float *meta, cudaStream_t s) {
+  if (n_rows <= 0) return cudaSuccess;
+  const int blocks = (n_rows + 7) / 8;
   uint32_t *err = device_error_word();
   if (G == 32)
     k_prep_rows<32><<<blocks, 256, 0, s>>>(rows, n_rows, K, limbs, meta, err);
@@ -373,23 +388,41 @@ __device__ __forceinline__ int token_of_pair(int pair, int n_pairs, int slots) {
 // ---------------------------------------------------------------------------
 // grouped Q4 expert projections (gate/up + SwiGLU, and down)
 // ---------------------------------------------------------------------------
-// Work item = (expert bin, WARPS x RPW output rows, up to kTokPerItem pairs).
-// Each warp owns RPW rows over the full contraction width and keeps all P
-// summation chains in registers, so no cross-warp reduction is needed.  The
-// packed rows and their scales/biases stream straight from HBM into
-// registers, PF groups ahead of use; the item's activation limbs and
-// fixed-point metadata (shared by every warp of the CTA) are staged in
-// shared memory with cp.async, double-buffered across items.
+// Work item = (expert bin tile of up to kTokPerItem pairs, ROWS output rows).
+// A CTA takes a contiguous range of items, so consecutive items usually share
+// their tile and its staged activations (limbs + metadata, one shared-memory
+// stage reloaded only when the tile changes).  Each warp owns RPW output rows
+// over the full contraction width, one float32 accumulator per (row, token),
+// and streams its packed rows, scales and biases through a private R-stage
+// shared-memory ring, up to R-1 blocks ahead and across item boundaries.  A
+// block is 128 bytes (256 inputs) of each of the warp's 16 MMA rows plus
+// their scales and biases.
+//
+// Two weight layouts feed the ring:
+//  * arrays / table records in the reference layout (packed rows
+//    [rows][K/8] uint32, scales/biases [rows][K/G] bf16): every lane copies
+//    its share with 16-byte cp.async (per-lane copy groups);
+//  * tiled tables (fnmoe_tile_experts): each (16-row group, block) is one
+//    contiguous 2560-byte chunk, already in fragment order, which lane 0
+//    moves with one bulk copy (cp.async.bulk, no multicast) completing on the
+//    stage's mbarrier.
 //
 // MMA row mapping: DUAL (gate/up) -- M rows 0-7 are 8 gate rows and M rows
 // 8-15 the same 8 up rows, so a thread ends with gate and up of the same
 // (row, token) and applies SwiGLU in registers.  Single (down) -- M rows
-// 0-7 and 8-15 are 16 consecutive hidden rows.
+// 0-7 and 8-15 are 16 consecutive output rows.  N = 4 tokens x 2 limbs.
+
+constexpr int kBlkBytes = 128;                // packed bytes per row per block
+constexpr int kRowPitch = kBlkBytes + 16;     // generic layout: padded rows, conflict-free reads
+constexpr int kSBOff = 16 * kRowPitch;        // generic layout: [16 rows][scales 16 B | biases 16 B]
+constexpr int kStageBytes = kSBOff + 16 * 32;
+constexpr uint32_t kSpinLimit = 1u << 20;     // mbarrier polls before a wait gives up
 
 struct XStage {
   int Gc;      // groups along the contraction width
   int Xrow;    // limb bytes per pair
-  int Mp;      // padded metadata pitch per pair
+  int Mp;      // metadata bytes per pair: fl(SX) per group, then {A, B}
+  int a_off;   // byte offset of {A, B} in a metadata row
   int m_off;   // metadata offset in the stage
   int bytes;   // stage size
 };
@@ -398,35 +431,76 @@ __host__ __device__ inline XStage xstage_geom(int K, int G) {
   XStage s{};
   s.Gc = K / G;
   s.Xrow = s.Gc * 4 * G;
-  s.Mp = s.Gc * 16 + 16;
+  s.Mp = meta_pitch(s.Gc) * 4;
+  s.a_off = meta_a_index(s.Gc) * 4;
   s.m_off = kTokPerItem * s.Xrow;
   s.bytes = ((s.m_off + kTokPerItem * s.Mp + 127) / 128) * 128;
   return s;
 }
 
+__device__ __forceinline__ unsigned smem_u32(const void *p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
-  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async8(void *smem, const void *gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(smem_u32(smem)), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem)), "l"(gmem));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+// Wait until at most n of this thread's most recent copy groups are pending.
+__device__ __forceinline__ void cp_async_wait_dyn(int n) {
+  switch (n) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    default: cp_async_wait<3>(); break;
+  }
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bulk global -> shared copy (no multicast) completing on mbarrier `bar`.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Order earlier generic shared-memory accesses before later async-proxy
+// (bulk copy) writes.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
 struct RawDesc {
   int4 d0, d1, d2;
 };
 
-struct ItemInfo {
-  bool valid;   // item index in range
-  bool ok;      // expert pointers resolved
-  int len, rt;
-  int pair[kTokPerItem];  // pair ids of the token slots (-1 beyond len)
-  Ptrs p[2];
-};
-
-__device__ __forceinline__ RawDesc load_desc(const GroupView &gv, int item, int n_items, int row_tiles) {
+__device__ __forceinline__ RawDesc load_desc(const GroupView &gv, int tile) {
   RawDesc r{};
-  if (item < n_items) {
-    const int tile = item / row_tiles;
+  if (tile >= 0) {
     r.d0 = gv.tiles[3 * tile];
     r.d1 = gv.tiles[3 * tile + 1];
     r.d2 = gv.tiles[3 * tile + 2];
@@ -434,203 +508,353 @@ __device__ __forceinline__ RawDesc load_desc(const GroupView &gv, int item, int 
   return r;
 }
 
-template <bool DUAL>
-__device__ __forceinline__ ItemInfo item_info(const ExpertCallArgs &a, const RawDesc &rd, int item,
-                                              int n_items, int row_tiles, int out_rows, int in_cols) {
+struct ItemInfo {
+  bool ok;      // expert data resolved and this warp's rows exist
+  int len, rt;  // pairs in the tile, row tile
+};
+
+// This lane's copy sources for one item.  Generic layout: the packed row of
+// MMA row lane % 16 and the scale (lanes 0-15) or bias (lanes 16-31) row of
+// MMA row lane % 16.  Tiled layout: w is the warp's first chunk.
+struct Src {
+  const uint8_t *w, *sb;
+};
+
+// Record of a tiled route key: routed experts map to their index, the shared
+// expert to the last record.
+__device__ __forceinline__ bool tiled_record(const ExpertCallArgs &a, uint32_t key, uint32_t &rec) {
+  if (key == kSharedKey) {
+    if (!a.tiled.has_shared) return false;
+    rec = a.tiled.records - 1;
+    return true;
+  }
+  if (key >= static_cast<uint32_t>(a.array_experts)) return false;
+  rec = key;
+  return true;
+}
+
+// Resolve item `item` (tile descriptor rd) into its info and this lane's
+// copy sources.
+template <bool DUAL, bool TILED>
+__device__ __forceinline__ ItemInfo item_setup(const ExpertCallArgs &a, const RawDesc &rd, int item, int row_tiles,
+                                               int rows_per_tile, int wbase, int O, int K, int Gc, int nblk,
+                                               int lane, Src &src) {
   ItemInfo it{};
-  it.valid = item < n_items;
-  if (!it.valid) return it;
+  src = Src{nullptr, nullptr};
   it.rt = item - (item / row_tiles) * row_tiles;
   it.len = rd.d0.z;
-  it.pair[0] = rd.d1.x;
-  it.pair[1] = rd.d1.y;
-  it.pair[2] = rd.d1.z;
-  it.pair[3] = rd.d1.w;
-  it.pair[4] = rd.d2.x;
-  it.pair[5] = rd.d2.y;
-  it.pair[6] = rd.d2.z;
-  it.pair[7] = rd.d2.w;
   const uint32_t key = static_cast<uint32_t>(rd.d0.x);
-  if (DUAL) {
-    it.ok = resolve(a, key, 0, out_rows, in_cols, it.p[0]) && resolve(a, key, 1, out_rows, in_cols, it.p[1]);
-  } else {
-    it.ok = resolve(a, key, 2, out_rows, in_cols, it.p[0]);
+  const int o_base = it.rt * rows_per_tile + wbase;
+  if (TILED) {
+    uint32_t rec = 0;
+    it.ok = tiled_record(a, key, rec);
+    if (!it.ok) return it;
+    const int rg = DUAL ? o_base / 8 : o_base / 16;
+    const uint8_t *base = DUAL ? a.tiled.gate_up + rec * a.tiled.gate_up_record
+                               : a.tiled.down + rec * a.tiled.down_record;
+    src.w = base + static_cast<size_t>(rg) * nblk * kTileChunk;
+    return it;
   }
+  Ptrs p[2];
+  if (DUAL) {
+    it.ok = resolve(a, key, 0, O, K, p[0]) && resolve(a, key, 1, O, K, p[1]);
+  } else {
+    it.ok = resolve(a, key, 2, O, K, p[0]);
+    p[1] = p[0];
+  }
+  if (!it.ok) return it;
+  const int mrow = lane & 15;
+  const int row = DUAL ? min(o_base + (mrow & 7), O - 1) : min(o_base + mrow, O - 1);
+  const Ptrs &pp = (DUAL && mrow >= 8) ? p[1] : p[0];
+  src.w = reinterpret_cast<const uint8_t *>(pp.w) + static_cast<size_t>(row) * (K / 2);
+  const uint16_t *base = (lane >> 4) ? pp.b : pp.s;
+  src.sb = reinterpret_cast<const uint8_t *>(base + static_cast<size_t>(row) * Gc);
   return it;
 }
 
-// Stage the activation limbs and metadata of an item's pairs (all threads).
-__device__ __forceinline__ void load_xstage(uint8_t *st, const XStage &xs, const ItemInfo &it,
-                                            const uint16_t *__restrict__ xl, const float4 *__restrict__ xm,
-                                            int n_pairs, int slots, bool by_token) {
-  if (!it.valid || !it.ok) return;
-  const int tid = threadIdx.x, nt = blockDim.x;
-  const int cpx = xs.Xrow / 16;
-#pragma unroll
-  for (int q = 0; q < kTokPerItem; ++q) {
-    uint8_t *dst = st + q * xs.Xrow;
-    uint8_t *mdst = st + xs.m_off + q * xs.Mp;
-    if (q < it.len) {
-      const int pair = it.pair[q];
-      const int row = by_token ? token_of_pair(pair, n_pairs, slots) : pair;
-      const uint8_t *src = reinterpret_cast<const uint8_t *>(xl) + static_cast<size_t>(row) * xs.Xrow;
-      for (int cc = tid; cc < cpx; cc += nt) cp_async16(dst + cc * 16, src + cc * 16);
-      const float4 *msrc = xm + static_cast<size_t>(row) * xs.Gc;
-      for (int g = tid; g < xs.Gc; g += nt) cp_async16(mdst + g * 16, msrc + g);
-    } else {
-      // empty slot: zero limbs (the MMA adds nothing) and a neutral scale
-      for (int cc = tid; cc < cpx; cc += nt) *reinterpret_cast<uint4 *>(dst + cc * 16) = make_uint4(0u, 0u, 0u, 0u);
-      for (int g = tid; g < xs.Gc; g += nt) *reinterpret_cast<float4 *>(mdst + g * 16) = make_float4(0.0f, 1.0f, 1.0f, 0.0f);
-    }
-  }
-}
-
-// Fold one group into a chain: fS = fl(S); t = fma(s, fS, fl(b*fl(SX)));
-// acc = fma(fl(t*A), B, acc).  m = {fl(SX), A, B, -}.
-__device__ __forceinline__ float group_fold(float acc, float c_hi, float c_lo, float s, float b, const float4 &m) {
-  const float S = __fmaf_rn(c_hi, 4096.0f, c_lo);
-  const float t = __fmaf_rn(s, S, __fmul_rn(b, m.x));
-  return __fmaf_rn(__fmul_rn(t, m.y), m.z, acc);
-}
-
-// PF consecutive bfloat16 scales (or biases) loaded as one vector.
-template <int PF>
-struct Vec16 {
-  uint32_t w[(PF + 1) / 2];
-  __device__ __forceinline__ void load(const uint16_t *p) {
-    if constexpr (PF == 8) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p));
-      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-    } else if constexpr (PF == 4) {
-      const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p));
-      w[0] = v.x; w[1] = v.y;
-    } else if constexpr (PF == 2) {
-      w[0] = __ldg(reinterpret_cast<const uint32_t *>(p));
-    } else {
-      w[0] = __ldg(p);
-    }
-  }
-  __device__ __forceinline__ float get(int j) const {  // j is a compile-time constant after unrolling
-    const uint32_t word = w[j >> 1];
-    return __uint_as_float((j & 1) ? (word & 0xFFFF0000u) : (word << 16));
-  }
+// Per-warp ring state.  Blocks are numbered in consumption order across
+// items; block n lives in stage n % R.
+struct Ring {
+  uint8_t *base;
+  uint64_t *bars;  // R mbarriers (tiled layout)
+  int fetched;     // blocks issued
+  int consumed;    // blocks computed
+  int f_next;      // 0: the fetch cursor is in the current item, 1: in the next
+  int f_blk;       // next block of that item to fetch
+  int f_stage;     // fetched % R
+  int c_stage;     // consumed % R
+  uint32_t phase;  // bit s: parity of stage s's next completion
+  bool dead;       // a wait gave up: skip waits, results are void
 };
 
-// Pair id of token slot 4t + c without dynamic register-array indexing.
-__device__ __forceinline__ int item_pair(const ItemInfo &it, int t, int c) {
-  if (t == 0) return c == 0 ? it.pair[0] : c == 1 ? it.pair[1] : c == 2 ? it.pair[2] : it.pair[3];
-  return c == 0 ? it.pair[4] : c == 1 ? it.pair[5] : c == 2 ? it.pair[6] : it.pair[7];
+// Scale/bias copy modes of the generic layout.
+enum SBMode { kSB16 = 0, kSB4 = 1, kSBSync = 2 };
+
+// Issue the copies of block fb of an item into stage st.
+template <int G, bool TILED>
+__device__ __forceinline__ void issue_block(uint8_t *st, uint64_t *bar, const Src &src, int fb, int lane,
+                                            int rowbytes, int Gc, int sb_mode) {
+  if (TILED) {
+    if (lane == 0) {
+      fence_proxy_async();
+      mbar_expect_tx(bar, kTileChunk);
+      bulk_g2s(st, src.w + static_cast<size_t>(fb) * kTileChunk, kTileChunk, bar);
+    }
+    return;
+  }
+  constexpr int GPB = 2 * kBlkBytes / G;
+  // packed rows: lane copies 64 bytes (half h) of MMA row lane % 16
+  const int row = lane & 15, h = lane >> 4;
+  const int off = fb * kBlkBytes + h * 64;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (off + 16 * i < rowbytes) cp_async16(st + row * kRowPitch + h * 64 + 16 * i, src.w + off + 16 * i);
+  uint8_t *d = st + kSBOff + row * 32 + h * 16;
+  const int g0 = fb * GPB;
+  if (sb_mode == kSB16) {
+    cp_async16(d, src.sb + 2 * g0);  // GPB == 8: one piece, always full
+  } else if (sb_mode == kSB4) {
+#pragma unroll
+    for (int p = 0; p < GPB / 2; ++p)
+      if (g0 + 2 * p < Gc) cp_async4(d + 4 * p, src.sb + 2 * (g0 + 2 * p));
+  } else {
+#pragma unroll
+    for (int j = 0; j < GPB; ++j)
+      if (g0 + j < Gc)
+        *reinterpret_cast<uint16_t *>(d + 2 * j) = ldg_u16(reinterpret_cast<const uint16_t *>(src.sb) + g0 + j);
+  }
+  cp_async_commit();
 }
 
-// Multiply one item's rows for NT token tiles (4 pairs each) and write the
-// results.  The packed words of the two MMA rows stream through a PF-deep
-// register ring; scales/biases arrive as PF-wide vectors one block ahead.
-template <int G, int WARPS, bool DUAL, int PF, int NT>
-__device__ __forceinline__ void run_item(const ExpertCallArgs &a, const ItemInfo &cur, const uint8_t *st,
-                                         const XStage &xs, int O, int K, uint16_t *__restrict__ out,
-                                         uint16_t *__restrict__ g_out, uint16_t *__restrict__ u_out) {
+// Keep up to R blocks (the one being computed included) in the ring.
+template <int G, int R, bool TILED>
+__device__ __forceinline__ void ring_fill(Ring &rg, const Src &sc, const Src &sn, int nb_cur, int nb_nxt,
+                                          int lane, int rowbytes, int Gc, int sb_mode) {
+  while (rg.fetched - rg.consumed < R) {
+    if (rg.f_next == 0 && rg.f_blk >= nb_cur) {
+      rg.f_next = 1;
+      rg.f_blk = 0;
+    }
+    if (rg.f_next == 1 && rg.f_blk >= nb_nxt) break;
+    issue_block<G, TILED>(rg.base + rg.f_stage * kStageBytes, rg.bars + rg.f_stage, rg.f_next ? sn : sc, rg.f_blk,
+                          lane, rowbytes, Gc, sb_mode);
+    ++rg.f_blk;
+    ++rg.fetched;
+    if (++rg.f_stage == R) rg.f_stage = 0;
+  }
+}
+
+// Wait for block rg.consumed (stage rg.c_stage).  A wait that gives up sets
+// the timeout flag and marks the warp dead: later waits return at once.
+template <bool TILED>
+__device__ __forceinline__ void ring_wait(Ring &rg, uint32_t *err) {
+  if (!TILED) {
+    cp_async_wait_dyn(rg.fetched - rg.consumed - 1);
+  } else if (!rg.dead) {
+    const unsigned parity = (rg.phase >> rg.c_stage) & 1u;
+    uint32_t spins = 0;
+    while (!mbar_try_wait(rg.bars + rg.c_stage, parity)) {
+      if (++spins >= kSpinLimit) {
+        rg.dead = true;
+        set_error(err, kErrTimeout);
+        break;
+      }
+    }
+    rg.phase ^= 1u << rg.c_stage;
+  }
+  __syncwarp();
+}
+
+// Stage the activation limbs and metadata of a tile's pairs (all threads) and
+// its pair ids.  Empty slots get zero limbs, zero sums and {A, B} = {1, 1}.
+__device__ __forceinline__ void load_xstage(uint8_t *st, int *s_pairs, const XStage &xs, const RawDesc &rd, bool ok,
+                                            const uint16_t *__restrict__ xl, const float *__restrict__ xm,
+                                            int n_pairs, int slots, bool by_token) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int cpx = xs.Xrow / 16, cpm = xs.Mp / 16, a_chunk = xs.a_off / 16;
+  const int len = rd.d0.z;
+  const int pairs[kTokPerItem] = {rd.d1.x, rd.d1.y, rd.d1.z, rd.d1.w, rd.d2.x, rd.d2.y, rd.d2.z, rd.d2.w};
+#pragma unroll
+  for (int q = 0; q < kTokPerItem; ++q) {
+    if (tid == q) s_pairs[q] = pairs[q];
+    uint8_t *dst = st + q * xs.Xrow;
+    uint8_t *mdst = st + xs.m_off + q * xs.Mp;
+    if (ok && q < len) {
+      const int pair = pairs[q];
+      const int row = by_token ? token_of_pair(pair, n_pairs, slots) : pair;
+      const uint8_t *src = reinterpret_cast<const uint8_t *>(xl) + static_cast<size_t>(row) * xs.Xrow;
+      const uint8_t *msrc = reinterpret_cast<const uint8_t *>(xm) + static_cast<size_t>(row) * xs.Mp;
+      for (int cc = tid; cc < cpx; cc += nt) cp_async16(dst + cc * 16, src + cc * 16);
+      for (int cc = tid; cc < cpm; cc += nt) cp_async16(mdst + cc * 16, msrc + cc * 16);
+    } else {
+      for (int cc = tid; cc < cpx; cc += nt) *reinterpret_cast<uint4 *>(dst + cc * 16) = make_uint4(0u, 0u, 0u, 0u);
+      for (int cc = tid; cc < cpm; cc += nt)
+        *reinterpret_cast<float4 *>(mdst + cc * 16) =
+            cc == a_chunk ? make_float4(1.0f, 1.0f, 0.0f, 0.0f) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+  }
+}
+
+// bfloat16 j (0-3) of two packed words as float32.
+__device__ __forceinline__ float bf16_at(const uint2 &v, int j) {
+  const uint32_t w = j < 2 ? v.x : v.y;
+  return __uint_as_float((j & 1) ? (w & 0xFFFF0000u) : (w << 16));
+}
+
+__device__ __forceinline__ uint32_t word_at(const uint4 &v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+__device__ __forceinline__ float f_at(const float4 &v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// One group against NT token tiles: MMA the two rows' nibbles with the
+// token limbs, fold S and SX into the accumulators.
+template <int G, int NT>
+__device__ __forceinline__ void group_step(const uint32_t (&qa)[G / 32], const uint32_t (&qb)[G / 32], float sA,
+                                           float bA, float sB, float bB, const uint8_t *xgj, int xstep,
+                                           const float (&fs)[NT], float (&accA)[NT], float (&accB)[NT]) {
   constexpr int WB = G / 32;
-  constexpr int WPG = G / 8;
+  uint32_t A0[WB][4], A1[WB][4];
+#pragma unroll
+  for (int wb = 0; wb < WB; ++wb) nibble_operands(qa[wb], qb[wb], A0[wb], A1[wb]);
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    float C[4];
+#pragma unroll
+    for (int wb = 0; wb < WB; ++wb) {
+      const uint4 v = *reinterpret_cast<const uint4 *>(xgj + t * xstep + wb * 64);
+      if (wb == 0) mma_16816_z(C, A0[wb], v.x, v.y);
+      else mma_16816(C, A0[wb], v.x, v.y);
+      mma_16816(C, A1[wb], v.z, v.w);
+    }
+    const float SA = __fmaf_rn(C[0], 4096.0f, C[1]);
+    const float SB = __fmaf_rn(C[2], 4096.0f, C[3]);
+    accA[t] = __fmaf_rn(bA, fs[t], __fmaf_rn(sA, SA, accA[t]));
+    accB[t] = __fmaf_rn(bB, fs[t], __fmaf_rn(sB, SB, accB[t]));
+  }
+}
+
+// One ring block: GPB groups of the warp's 16 MMA rows against NT token
+// tiles, in halves (scales, biases and group sums of one half live in
+// registers at a time).  TAIL blocks stop at the last group.
+template <int G, int NT, bool TAIL, bool TILED>
+__device__ __forceinline__ void compute_block(const uint8_t *st, const uint8_t *xg, const uint8_t *mg, int xstep,
+                                              int mstep, int g0, int Gc, int r, int c, float (&accA)[NT],
+                                              float (&accB)[NT]) {
+  constexpr int WB = G / 32;
+  constexpr int GPB = 2 * kBlkBytes / G;
+  constexpr int QG = GPB / 2;  // groups per half
+  const uint8_t *sbA = st + (TILED ? kTileW : kSBOff) + r * 32;
+  const uint8_t *sbB = sbA + 8 * 32;
+#pragma unroll 1
+  for (int h = 0; h < 2; ++h) {
+    const int gh = h * QG;
+    if (TAIL && g0 + gh >= Gc) break;
+    uint2 sA2, bA2, sB2, bB2;
+    if (QG == 4) {
+      sA2 = *reinterpret_cast<const uint2 *>(sbA + 2 * gh);
+      bA2 = *reinterpret_cast<const uint2 *>(sbA + 16 + 2 * gh);
+      sB2 = *reinterpret_cast<const uint2 *>(sbB + 2 * gh);
+      bB2 = *reinterpret_cast<const uint2 *>(sbB + 16 + 2 * gh);
+    } else {
+      sA2 = make_uint2(*reinterpret_cast<const uint32_t *>(sbA + 2 * gh), 0u);
+      bA2 = make_uint2(*reinterpret_cast<const uint32_t *>(sbA + 16 + 2 * gh), 0u);
+      sB2 = make_uint2(*reinterpret_cast<const uint32_t *>(sbB + 2 * gh), 0u);
+      bB2 = make_uint2(*reinterpret_cast<const uint32_t *>(sbB + 16 + 2 * gh), 0u);
+    }
+    float4 fsx[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      if (QG == 4) {
+        fsx[t] = *reinterpret_cast<const float4 *>(mg + t * mstep + 4 * gh);
+      } else {
+        const float2 f = *reinterpret_cast<const float2 *>(mg + t * mstep + 4 * gh);
+        fsx[t] = make_float4(f.x, f.y, 0.0f, 0.0f);
+      }
+    }
+    uint4 wA4, wB4;
+    if (TILED) {
+      // fragment-ordered chunk: [half][A/B][slot r*4+c][4 words]
+      wA4 = *reinterpret_cast<const uint4 *>(st + (2 * h) * 512 + (r * 4 + c) * 16);
+      wB4 = *reinterpret_cast<const uint4 *>(st + (2 * h + 1) * 512 + (r * 4 + c) * 16);
+    }
+#pragma unroll
+    for (int j = 0; j < QG; ++j) {
+      if (TAIL && g0 + gh + j >= Gc) break;
+      uint32_t qa[WB], qb[WB];
+#pragma unroll
+      for (int wb = 0; wb < WB; ++wb) {
+        if (TILED) {
+          qa[wb] = word_at(wA4, j * WB + wb);
+          qb[wb] = word_at(wB4, j * WB + wb);
+        } else {
+          const int off = (gh + j) * (G / 2) + wb * 16 + c * 4;
+          qa[wb] = *reinterpret_cast<const uint32_t *>(st + r * kRowPitch + off);
+          qb[wb] = *reinterpret_cast<const uint32_t *>(st + (r + 8) * kRowPitch + off);
+        }
+      }
+      float fs[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) fs[t] = f_at(fsx[t], j);
+      group_step<G, NT>(qa, qb, bf16_at(sA2, j), bf16_at(bA2, j), bf16_at(sB2, j), bf16_at(bB2, j),
+                        xg + (gh + j) * (4 * G), xstep, fs, accA, accB);
+    }
+  }
+}
+
+// Compute one item's rows for NT token tiles (4 pairs each) and write them.
+template <int G, int WARPS, bool DUAL, int R, bool TILED, int NT>
+__device__ __forceinline__ void run_item(const ExpertCallArgs &a, const ItemInfo &cur, const uint8_t *xst,
+                                         const int *s_pairs, const XStage &xs, int O, int K, int nblk, Ring &rg,
+                                         const Src &sc, const Src &sn, int nb_nxt, int sb_mode, uint32_t *err,
+                                         uint16_t *__restrict__ out, uint16_t *__restrict__ g_out,
+                                         uint16_t *__restrict__ u_out) {
+  constexpr int GPB = 2 * kBlkBytes / G;
   constexpr int RPW = DUAL ? 8 : 16;
   constexpr int ROWS = RPW * WARPS;
   const int Gc = xs.Gc;
-  const int P = chain_count(Gc);
+  const int rowbytes = K / 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
-  const int wpr = K / 8;
   const int o0 = cur.rt * ROWS + warp * RPW + r;
   const int oA = o0;
   const int oB = DUAL ? o0 : o0 + 8;
-  const int cA = min(oA, O - 1), cB = min(oB, O - 1);
-  const Ptrs &pA = cur.p[0];
-  const Ptrs &pB = DUAL ? cur.p[1] : cur.p[0];
-  const uint32_t *wA = pA.w + static_cast<size_t>(cA) * wpr + c;
-  const uint32_t *wB = pB.w + static_cast<size_t>(cB) * wpr + c;
-  const uint16_t *sA = pA.s + static_cast<size_t>(cA) * Gc;
-  const uint16_t *bA = pA.b + static_cast<size_t>(cA) * Gc;
-  const uint16_t *sB = pB.s + static_cast<size_t>(cB) * Gc;
-  const uint16_t *bB = pB.b + static_cast<size_t>(cB) * Gc;
-  uint32_t qa[PF][WB], qb[PF][WB];
+  const uint8_t *xb = xst + (r >> 1) * xs.Xrow + (r & 1) * (G * 2) + c * 16;
+  const uint8_t *mrow = xst + xs.m_off + c * xs.Mp;
+  const int xstep = 4 * xs.Xrow, mstep = 4 * xs.Mp;
+  const int full = Gc / GPB;  // blocks without a tail
+  float accA[NT], accB[NT];
 #pragma unroll
-  for (int j = 0; j < PF; ++j) {
-#pragma unroll
-    for (int wb = 0; wb < WB; ++wb) {
-      qa[j][wb] = ldg_u32(wA + j * WPG + wb * 4);
-      qb[j][wb] = ldg_u32(wB + j * WPG + wb * 4);
+  for (int t = 0; t < NT; ++t) accA[t] = accB[t] = -0.0f;
+#pragma unroll 1
+  for (int cb = 0; cb < nblk; ++cb) {
+    if (rg.fetched == rg.consumed) {  // nothing in flight (the previous item was skipped): fetch now
+      __syncwarp();
+      ring_fill<G, R, TILED>(rg, sc, sn, nblk, nb_nxt, lane, rowbytes, Gc, sb_mode);
     }
-  }
-  Vec16<PF> vsA, vbA, vsB, vbB;
-  vsA.load(sA);
-  vbA.load(bA);
-  vsB.load(sB);
-  vbB.load(bB);
-  const uint8_t *xb = st + (r >> 1) * xs.Xrow + (r & 1) * (G * 2) + c * 16;
-  const float4 *mrow = reinterpret_cast<const float4 *>(st + xs.m_off + c * xs.Mp);
-  // Chain tree folded as chains complete: h0 = c0 (+ c2), h1 = c1 (+ c3).
-  float hA0[NT], hA1[NT], hB0[NT], hB1[NT];
-#pragma unroll
-  for (int t = 0; t < NT; ++t) hA0[t] = hA1[t] = hB0[t] = hB1[t] = -0.0f;
-  for (int ch = 0; ch < P; ++ch) {
-    float accA[NT], accB[NT];
-#pragma unroll
-    for (int t = 0; t < NT; ++t) accA[t] = accB[t] = -0.0f;
-    const int gend = chain_begin(ch + 1, P, Gc);
-    for (int g0 = chain_begin(ch, P, Gc); g0 < gend; g0 += PF) {
-      const int gn0 = (g0 + PF < Gc) ? g0 + PF : g0;  // next block (the last one is re-read)
-      Vec16<PF> nsA, nbA, nsB, nbB;
-      nsA.load(sA + gn0);
-      nbA.load(bA + gn0);
-      nsB.load(sB + gn0);
-      nbB.load(bB + gn0);
-      const uint32_t *nwA = wA + gn0 * WPG;
-      const uint32_t *nwB = wB + gn0 * WPG;
-      const uint8_t *xg = xb + g0 * (4 * G);
-      const float4 *mg = mrow + g0;
-#pragma unroll
-      for (int j = 0; j < PF; ++j) {
-        uint32_t A0[WB][4], A1[WB][4];
-#pragma unroll
-        for (int wb = 0; wb < WB; ++wb) {
-          nibble_operands(qa[j][wb], qb[j][wb], A0[wb], A1[wb]);
-          qa[j][wb] = ldg_u32(nwA + j * WPG + wb * 4);
-          qb[j][wb] = ldg_u32(nwB + j * WPG + wb * 4);
-        }
-        const float s0 = vsA.get(j), b0 = vbA.get(j), s1 = vsB.get(j), b1 = vbB.get(j);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          float C[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-          for (int wb = 0; wb < WB; ++wb) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(xg + t * 4 * xs.Xrow + j * (4 * G) + wb * 64);
-            mma_16816(C, A0[wb], v.x, v.y);
-            mma_16816(C, A1[wb], v.z, v.w);
-          }
-          const float4 m = *reinterpret_cast<const float4 *>(
-              reinterpret_cast<const uint8_t *>(mg + j) + t * 4 * xs.Mp);
-          accA[t] = group_fold(accA[t], C[0], C[1], s0, b0, m);
-          accB[t] = group_fold(accB[t], C[2], C[3], s1, b1, m);
-        }
-      }
-      vsA = nsA;
-      vbA = nbA;
-      vsB = nsB;
-      vbB = nbB;
-    }
-#pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      if (ch == 0) { hA0[t] = accA[t]; hB0[t] = accB[t]; }
-      else if (ch == 1) { hA1[t] = accA[t]; hB1[t] = accB[t]; }
-      else if (ch == 2) { hA0[t] = __fadd_rn(hA0[t], accA[t]); hB0[t] = __fadd_rn(hB0[t], accB[t]); }
-      else { hA1[t] = __fadd_rn(hA1[t], accA[t]); hB1[t] = __fadd_rn(hB1[t], accB[t]); }
-    }
+    ring_wait<TILED>(rg, err);  // block rg.consumed landed; all lanes are done with the previous one
+    const uint8_t *st = rg.base + rg.c_stage * kStageBytes;
+    ring_fill<G, R, TILED>(rg, sc, sn, nblk, nb_nxt, lane, rowbytes, Gc, sb_mode);
+    const int g0 = cb * GPB;
+    if (cb < full)
+      compute_block<G, NT, false, TILED>(st, xb + g0 * (4 * G), mrow + g0 * 4, xstep, mstep, g0, Gc, r, c, accA,
+                                         accB);
+    else
+      compute_block<G, NT, true, TILED>(st, xb + g0 * (4 * G), mrow + g0 * 4, xstep, mstep, g0, Gc, r, c, accA,
+                                        accB);
+    ++rg.consumed;
+    if (++rg.c_stage == R) rg.c_stage = 0;
   }
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
     const int q = 4 * t + c;
     if (q < cur.len) {
-      const int pair = item_pair(cur, t, c);
-      const float yA = P == 1 ? hA0[t] : __fadd_rn(hA0[t], hA1[t]);
-      const float yB = P == 1 ? hB0[t] : __fadd_rn(hB0[t], hB1[t]);
+      const int pair = s_pairs[q];
+      const float2 ab = *reinterpret_cast<const float2 *>(mrow + t * mstep + xs.a_off);
+      const float yA = __fmul_rn(__fmul_rn(accA[t], ab.x), ab.y);
+      const float yB = __fmul_rn(__fmul_rn(accB[t], ab.x), ab.y);
       if (DUAL) {
         if (oA < O) {
           const float gvv = round_bf16(yA), uvv = round_bf16(yB);
@@ -648,13 +872,14 @@ __device__ __forceinline__ void run_item(const ExpertCallArgs &a, const ItemInfo
   }
 }
 
-template <int G, int WARPS, bool DUAL, int PF>
-__global__ void __launch_bounds__(WARPS * 32) k_expert_rows(ExpertCallArgs a, GroupView gv,
-                                                            const uint16_t *__restrict__ xl,
-                                                            const float4 *__restrict__ xm,
-                                                            uint16_t *__restrict__ out,
-                                                            uint16_t *__restrict__ g_out,
-                                                            uint16_t *__restrict__ u_out, uint32_t *err) {
+template <int G, int WARPS, bool DUAL, int R, bool TILED>
+__global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a, GroupView gv,
+                                                               const uint16_t *__restrict__ xl,
+                                                               const float *__restrict__ xm,
+                                                               uint16_t *__restrict__ out,
+                                                               uint16_t *__restrict__ g_out,
+                                                               uint16_t *__restrict__ u_out, int sb_mode,
+                                                               uint32_t *err) {
   constexpr int RPW = DUAL ? 8 : 16;
   constexpr int ROWS = RPW * WARPS;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -663,41 +888,105 @@ __global__ void __launch_bounds__(WARPS * 32) k_expert_rows(ExpertCallArgs a, Gr
   const XStage xs = xstage_geom(K, G);
   const int row_tiles = (O + ROWS - 1) / ROWS;
   const int n_items = gv.n_tiles[0] * row_tiles;
-
-  int item = blockIdx.x;
-  ItemInfo cur = item_info<DUAL>(a, load_desc(gv, item, n_items, row_tiles), item, n_items, row_tiles, O, K);
-  RawDesc raw_next = load_desc(gv, item + gridDim.x, n_items, row_tiles);
-  load_xstage(smem, xs, cur, xl, xm, a.n_pairs, a.slots, DUAL);
-  cp_async_commit();
-  for (int k = 0; cur.valid; ++k) {
-    const uint8_t *st = smem + (k & 1) * xs.bytes;
-    const int nitem = item + gridDim.x;
-    const ItemInfo nxt = item_info<DUAL>(a, raw_next, nitem, n_items, row_tiles, O, K);
-    raw_next = load_desc(gv, nitem + gridDim.x, n_items, row_tiles);
-    load_xstage(smem + ((k + 1) & 1) * xs.bytes, xs, nxt, xl, xm, a.n_pairs, a.slots, DUAL);
-    cp_async_commit();
-    cp_async_wait1();
-    __syncthreads();  // activation stage of this item is visible
-    if (!cur.ok) {
-      if (threadIdx.x == 0) set_error(err, kErrBadRoute);
-    } else if (cur.len > 4) {
-      run_item<G, WARPS, DUAL, PF, 2>(a, cur, st, xs, O, K, out, g_out, u_out);
-    } else {
-      run_item<G, WARPS, DUAL, PF, 1>(a, cur, st, xs, O, K, out, g_out, u_out);
+  const int i0 = static_cast<int>(static_cast<long long>(n_items) * blockIdx.x / gridDim.x);
+  const int i1 = static_cast<int>(static_cast<long long>(n_items) * (blockIdx.x + 1) / gridDim.x);
+  if (i0 >= i1) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rowbytes = K / 2;
+  const int nblk = (rowbytes + kBlkBytes - 1) / kBlkBytes;
+  const int wbase = warp * RPW;
+  uint8_t *ring_base = smem + xs.bytes + warp * R * kStageBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + xs.bytes + WARPS * R * kStageBytes) + warp * R;
+  int *s_pairs = reinterpret_cast<int *>(smem + xs.bytes + WARPS * R * (kStageBytes + 8));
+  if (TILED) {
+    if (lane == 0) {
+      for (int i = 0; i < R; ++i) mbar_init(bars + i, 1);
+      mbar_init_fence();
     }
-    __syncthreads();  // the stage is refilled two items later
-    item = nitem;
-    cur = nxt;
+    __syncwarp();
   }
-  asm volatile("cp.async.wait_all;\n" ::);
+  Ring rg{ring_base, bars, 0, 0, 0, 0, 0, 0, 0u, false};
+
+  // Tiled tables hold whole row groups only: a warp whose rows start past
+  // the last row has nothing to do (len -1 marks it: no bad-route error).
+  auto setup = [&](const RawDesc &rd, int item, Src &src) {
+    ItemInfo it = item_setup<DUAL, TILED>(a, rd, item, row_tiles, ROWS, wbase, O, K, xs.Gc, nblk, lane, src);
+    if (TILED && it.rt * ROWS + wbase >= O) {
+      it.ok = false;
+      it.len = -1;
+      src = Src{nullptr, nullptr};
+    }
+    return it;
+  };
+
+  Src sc, sn;
+  const RawDesc rd0 = load_desc(gv, i0 / row_tiles);
+  ItemInfo cur = setup(rd0, i0, sc);
+  RawDesc rd_nxt = load_desc(gv, i0 + 1 < i1 ? (i0 + 1) / row_tiles : -1);
+  int4 d0_nn = i0 + 2 < i1 ? gv.tiles[3 * ((i0 + 2) / row_tiles)] : make_int4(0, 0, 0, 0);
+  ItemInfo nxt{};
+  sn = Src{nullptr, nullptr};
+  if (i0 + 1 < i1) nxt = setup(rd_nxt, i0 + 1, sn);
+  int nb_cur = cur.ok ? nblk : 0;
+  int nb_nxt = nxt.ok ? nblk : 0;
+
+  load_xstage(smem, s_pairs, xs, rd0, rd0.d0.z > 0, xl, xm, a.n_pairs, a.slots, DUAL);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  ring_fill<G, R, TILED>(rg, sc, sn, nb_cur, nb_nxt, lane, rowbytes, xs.Gc, sb_mode);
+
+  for (int item = i0; item < i1; ++item) {
+    if (!cur.ok) {
+      if (cur.len >= 0 && lane == 0) set_error(err, kErrBadRoute);
+    } else if (cur.len > 4) {
+      run_item<G, WARPS, DUAL, R, TILED, 2>(a, cur, smem, s_pairs, xs, O, K, nblk, rg, sc, sn, nb_nxt, sb_mode, err,
+                                            out, g_out, u_out);
+    } else {
+      run_item<G, WARPS, DUAL, R, TILED, 1>(a, cur, smem, s_pairs, xs, O, K, nblk, rg, sc, sn, nb_nxt, sb_mode, err,
+                                            out, g_out, u_out);
+    }
+    const int ni = item + 1;
+    if (ni >= i1) break;
+    if (ni / row_tiles != item / row_tiles) {
+      __syncthreads();  // every warp is done with the staged activations and pair ids
+      load_xstage(smem, s_pairs, xs, rd_nxt, rd_nxt.d0.z > 0, xl, xm, a.n_pairs, a.slots, DUAL);
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
+    }
+    // rotate: the next item becomes current; the fetch cursor follows it
+    if (rg.f_next == 0) rg.f_blk = 0;
+    rg.f_next = 0;
+    cur = nxt;
+    sc = sn;
+    nb_cur = nb_nxt;
+    const int nn = ni + 1;
+    rd_nxt.d0 = d0_nn;  // prefetched one item ahead; the pair ids are needed only at a tile change
+    if (nn < i1) {
+      rd_nxt.d1 = gv.tiles[3 * (nn / row_tiles) + 1];
+      rd_nxt.d2 = gv.tiles[3 * (nn / row_tiles) + 2];
+    }
+    d0_nn = nn + 1 < i1 ? gv.tiles[3 * ((nn + 1) / row_tiles)] : make_int4(0, 0, 0, 0);
+    nxt = ItemInfo{};
+    sn = Src{nullptr, nullptr};
+    if (nn < i1) nxt = setup(rd_nxt, nn, sn);
+    nb_nxt = nxt.ok ? nblk : 0;
+  }
+  // Every issued block was consumed (items run to completion), so no copy is
+  // in flight; drain per-lane copy groups.
+  cp_async_wait<0>();
 }
 
 namespace {
 
-template <typename Kern>
-cudaError_t launch_rows(Kern kernel, int threads, size_t smem, const ExpertCallArgs &a, const GroupView &gv,
-                        const uint16_t *xl, const float4 *xm, uint16_t *out, uint16_t *g_out,
-                        uint16_t *u_out, cudaStream_t s) {
+constexpr size_t kSmemLimit = 227 * 1024;
+
+template <int G, int WARPS, bool DUAL, int R, bool TILED>
+cudaError_t launch_rows(const ExpertCallArgs &a, const GroupView &gv, const uint16_t *xl, const float *xm,
+                        uint16_t *out, uint16_t *g_out, uint16_t *u_out, int sb_mode, size_t smem, cudaStream_t s) {
+  auto kernel = k_expert_rows<G, WARPS, DUAL, R, TILED>;
+  const int threads = WARPS * 32;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
@@ -706,74 +995,162 @@ cudaError_t launch_rows(Kern kernel, int threads, size_t smem, const ExpertCallA
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm <= 0)
     per_sm = 1;
-  kernel<<<di.sms * per_sm, threads, smem, s>>>(a, gv, xl, xm, out, g_out, u_out, device_error_word());
+  kernel<<<di.sms * per_sm, threads, smem, s>>>(a, gv, xl, xm, out, g_out, u_out, sb_mode, device_error_word());
   return cudaGetLastError();
 }
 
-constexpr size_t kSmemBudget = 200 * 1024;
+size_t ring_smem(int xbytes, int warps, int r) {
+  return static_cast<size_t>(xbytes) + static_cast<size_t>(warps) * r * (kStageBytes + 8) + kTokPerItem * sizeof(int);
+}
+
+// Deepest ring (4, 3 or 2 stages) whose shared memory fits beside the
+// activation stage.
+template <int G, int WARPS, bool DUAL, bool TILED>
+cudaError_t launch_ring(const ExpertCallArgs &a, const GroupView &gv, int K, const uint16_t *xl, const float *xm,
+                        uint16_t *out, uint16_t *g_out, uint16_t *u_out, int sb_mode, cudaStream_t s) {
+  const int x = xstage_geom(K, G).bytes;
+  if (ring_smem(x, WARPS, 4) <= kSmemLimit)
+    return launch_rows<G, WARPS, DUAL, 4, TILED>(a, gv, xl, xm, out, g_out, u_out, sb_mode, ring_smem(x, WARPS, 4), s);
+  if (ring_smem(x, WARPS, 3) <= kSmemLimit)
+    return launch_rows<G, WARPS, DUAL, 3, TILED>(a, gv, xl, xm, out, g_out, u_out, sb_mode, ring_smem(x, WARPS, 3), s);
+  if (ring_smem(x, WARPS, 2) <= kSmemLimit)
+    return launch_rows<G, WARPS, DUAL, 2, TILED>(a, gv, xl, xm, out, g_out, u_out, sb_mode, ring_smem(x, WARPS, 2), s);
+  return cudaErrorInvalidValue;
+}
+
+template <int G, bool DUAL, bool TILED>
+cudaError_t launch_width(const ExpertCallArgs &a, const GroupView &gv, int K, const uint16_t *xl, const float *xm,
+                         uint16_t *out, uint16_t *g_out, uint16_t *u_out, int sb_mode, cudaStream_t s) {
+  // Many pairs -> 16-warp CTAs (one per SM); few pairs (batch-1 decode) ->
+  // 4-warp CTAs so that the handful of experts still spreads over every SM.
+  if ((a.n_pairs + a.tokens) >= 64)
+    return launch_ring<G, 16, DUAL, TILED>(a, gv, K, xl, xm, out, g_out, u_out, sb_mode, s);
+  return launch_ring<G, 4, DUAL, TILED>(a, gv, K, xl, xm, out, g_out, u_out, sb_mode, s);
+}
+
+template <bool DUAL>
+cudaError_t launch_family(const ExpertCallArgs &a, const GroupView &gv, int K, const uint16_t *xl,
+                          const float *xm, uint16_t *out, uint16_t *g_out, uint16_t *u_out, cudaStream_t s) {
+  const int Gc = K / a.G;
+  const bool tiled = DUAL ? a.tiled.gate_up != nullptr : a.tiled.down != nullptr;
+  if (tiled) {
+    if (a.G == 32) return launch_width<32, DUAL, true>(a, gv, K, xl, xm, out, g_out, u_out, kSB16, s);
+    return launch_width<64, DUAL, true>(a, gv, K, xl, xm, out, g_out, u_out, kSB16, s);
+  }
+  // Scale/bias rows move as one 16-byte piece per block when every row starts
+  // on a 16-byte boundary (group size 32, a multiple of 8 groups per row,
+  // aligned bases), as 4-byte pieces when rows are 4-byte aligned, else by
+  // plain loads.
+  const int sb_mode = (a.G == 32 && Gc % 8 == 0 && a.sb_bulk) ? kSB16 : (a.sb_async && Gc % 2 == 0) ? kSB4 : kSBSync;
+  if (a.G == 32) return launch_width<32, DUAL, false>(a, gv, K, xl, xm, out, g_out, u_out, sb_mode, s);
+  return launch_width<64, DUAL, false>(a, gv, K, xl, xm, out, g_out, u_out, sb_mode, s);
+}
 
 }  // namespace
 
-// Prefetch block: the largest of 8/4/2/1 that divides every chain length and
-// keeps the scales/biases vector loads aligned.
-int pick_pf(int K, int G) {
-  const int Gc = K / G;
-  const int P = chain_count(Gc);
-  for (int pf : {8, 4, 2}) {
-    bool ok = (Gc * 2) % (pf * 2) == 0;
-    for (int ch = 0; ch < P && ok; ++ch) ok = ((chain_begin(ch + 1, P, Gc) - chain_begin(ch, P, Gc)) % pf) == 0;
-    for (int ch = 0; ch < P && ok; ++ch) ok = (chain_begin(ch, P, Gc) % pf) == 0;
-    if (ok) return pf;
-  }
-  return 1;
-}
-
-template <int G, int WARPS, bool DUAL>
-cudaError_t launch_rows_pf(int pf, size_t smem, const ExpertCallArgs &a, const GroupView &gv, const uint16_t *xl,
-                           const float4 *xm, uint16_t *out, uint16_t *g_out, uint16_t *u_out, cudaStream_t s) {
-  const int threads = WARPS * 32;
-  switch (pf) {
-    case 8: return launch_rows(k_expert_rows<G, WARPS, DUAL, 8>, threads, smem, a, gv, xl, xm, out, g_out, u_out, s);
-    case 4: return launch_rows(k_expert_rows<G, WARPS, DUAL, 4>, threads, smem, a, gv, xl, xm, out, g_out, u_out, s);
-    case 2: return launch_rows(k_expert_rows<G, WARPS, DUAL, 2>, threads, smem, a, gv, xl, xm, out, g_out, u_out, s);
-    default: return launch_rows(k_expert_rows<G, WARPS, DUAL, 1>, threads, smem, a, gv, xl, xm, out, g_out, u_out, s);
-  }
-}
-
-// Expected pairs per launch decide the CTA width: many pairs -> 8 warps,
-// few pairs (batch-1 decode) -> 4 warps so that the handful of experts still
-// spreads over every SM.
 cudaError_t launch_gate_up(const ExpertCallArgs &a, const GroupView &gv,
-                           const uint16_t *x_limbs, const float4 *x_meta,
+                           const uint16_t *x_limbs, const float *x_meta,
                            uint16_t *act, uint16_t *g_out, uint16_t *u_out,
                            cudaStream_t s) {
-  const XStage xs = xstage_geom(a.H, a.G);
-  const size_t smem = 2 * static_cast<size_t>(xs.bytes);
-  if (smem > kSmemBudget) return cudaErrorInvalidValue;
-  const bool wide = (a.n_pairs + a.tokens) >= 64;
-  const int pf = std::min(4, pick_pf(a.H, a.G));
-  if (a.G == 32) {
-    if (wide) return launch_rows_pf<32, 16, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
-    return launch_rows_pf<32, 4, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
-  }
-  if (wide) return launch_rows_pf<64, 16, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
-  return launch_rows_pf<64, 4, true>(pf, smem, a, gv, x_limbs, x_meta, act, g_out, u_out, s);
+  return launch_family<true>(a, gv, a.H, x_limbs, x_meta, act, g_out, u_out, s);
 }
 
 cudaError_t launch_down(const ExpertCallArgs &a, const GroupView &gv,
-                        const uint16_t *act_limbs, const float4 *act_meta,
+                        const uint16_t *act_limbs, const float *act_meta,
                         uint16_t *d, cudaStream_t s) {
-  const XStage xs = xstage_geom(a.I, a.G);
-  const size_t smem = 2 * static_cast<size_t>(xs.bytes);
-  if (smem > kSmemBudget) return cudaErrorInvalidValue;
-  const bool wide = (a.n_pairs + a.tokens) >= 64;
-  const int pf = pick_pf(a.I, a.G);
-  if (a.G == 32) {
-    if (wide) return launch_rows_pf<32, 16, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
-    return launch_rows_pf<32, 4, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
+  return launch_family<false>(a, gv, a.I, act_limbs, act_meta, d, nullptr, nullptr, s);
+}
+
+// ---------------------------------------------------------------------------
+// tiled expert tables: one 2560-byte chunk per (row group, block)
+// ---------------------------------------------------------------------------
+// Chunk layout (bytes): [half h 0-1][side 0 = A rows, 1 = B rows][slot
+// r*4+c][4 words] (2048 bytes), then [16 MMA rows][scales 8 x bf16][biases
+// 8 x bf16] (512 bytes).  Slot (r, c) of half h holds the words thread
+// (r, c) feeds to the MMA for the groups of that half: G = 32 -- word c of
+// groups 4h..4h+3; G = 64 -- words c and c+4 of groups 2h and 2h+1.  Bytes
+// past the end of a row (tail block) are zero.  Gate/up chunks cover 8 gate
+// rows (A) and the same 8 up rows (B); down chunks cover 16 consecutive rows
+// (A = first 8).
+
+__global__ void k_tile_experts(const uint32_t *__restrict__ wA_base, const uint32_t *__restrict__ wB_base,
+                               const uint16_t *__restrict__ sA_base, const uint16_t *__restrict__ bA_base,
+                               const uint16_t *__restrict__ sB_base, const uint16_t *__restrict__ bB_base,
+                               int experts, int O, int K, int G, int dual, uint8_t *__restrict__ dst,
+                               uint64_t record_bytes) {
+  const int Gc = K / G;
+  const int nblk = (K / 2 + kBlkBytes - 1) / kBlkBytes;
+  const int rows_per_group = dual ? 8 : 16;
+  const int n_rg = O / rows_per_group;
+  const long long units = static_cast<long long>(experts) * n_rg * nblk * (kTileChunk / 16);
+  const int GPB = 2 * kBlkBytes / G;
+  for (long long u = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; u < units;
+       u += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int piece = static_cast<int>(u % (kTileChunk / 16));  // 16-byte piece of the chunk
+    long long rest = u / (kTileChunk / 16);
+    const int blk = static_cast<int>(rest % nblk);
+    rest /= nblk;
+    const int rg = static_cast<int>(rest % n_rg);
+    const int e = static_cast<int>(rest / n_rg);
+    uint32_t out[4] = {0u, 0u, 0u, 0u};
+    // MMA row m (0-15) of this chunk -> (matrix, row)
+    auto mat_row = [&](int m, bool &side_b) {
+      side_b = dual ? (m >= 8) : false;
+      return dual ? rg * 8 + (m & 7) : rg * 16 + m;
+    };
+    if (piece < 128) {
+      const int h = piece >> 6, side = (piece >> 5) & 1, slot = piece & 31;
+      const int r = slot >> 2, c = slot & 3;
+      bool sb;
+      const int row = mat_row(side * 8 + r, sb);
+      const uint32_t *w = (sb ? wB_base : wA_base) + (static_cast<size_t>(e) * O + row) * (K / 8);
+      for (int i = 0; i < 4; ++i) {
+        int word;
+        if (G == 32) {
+          const int g = blk * GPB + 4 * h + i;
+          word = 4 * g + c;
+        } else {
+          const int g = blk * GPB + 2 * h + (i >> 1);
+          word = 8 * g + c + 4 * (i & 1);
+        }
+        out[i] = word < K / 8 ? w[word] : 0u;
+      }
+    } else {
+      const int q = piece - 128;  // 0..31: MMA row q/2, scales (even) or biases (odd)
+      const int m = q >> 1, kind = q & 1;
+      bool sb;
+      const int row = mat_row(m, sb);
+      const uint16_t *src = kind ? (sb ? bB_base : bA_base) : (sb ? sB_base : sA_base);
+      src += (static_cast<size_t>(e) * O + row) * Gc;
+      uint16_t v[8];
+      for (int j = 0; j < 8; ++j) {
+        const int g = blk * GPB + j;
+        v[j] = (j < GPB && g < Gc) ? src[g] : static_cast<uint16_t>(0);
+      }
+      for (int i = 0; i < 4; ++i) out[i] = static_cast<uint32_t>(v[2 * i]) | (static_cast<uint32_t>(v[2 * i + 1]) << 16);
+    }
+    uint8_t *chunk = dst + static_cast<size_t>(e) * record_bytes + (static_cast<size_t>(rg) * nblk + blk) * kTileChunk;
+    *reinterpret_cast<uint4 *>(chunk + piece * 16) = make_uint4(out[0], out[1], out[2], out[3]);
   }
-  if (wide) return launch_rows_pf<64, 16, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
-  return launch_rows_pf<64, 4, false>(pf, smem, a, gv, act_limbs, act_meta, d, nullptr, nullptr, s);
+}
+
+cudaError_t launch_tile_experts(const uint32_t *wA, const uint32_t *wB, const uint16_t *sA, const uint16_t *bA,
+                                const uint16_t *sB, const uint16_t *bB, int experts, int O, int K, int G, bool dual,
+                                uint8_t *dst, uint64_t record_bytes, cudaStream_t s) {
+  const int nblk = (K / 2 + kBlkBytes - 1) / kBlkBytes;
+  const long long units = static_cast<long long>(experts) * (O / (dual ? 8 : 16)) * nblk * (kTileChunk / 16);
+  if (units <= 0) return cudaSuccess;
+  const int threads = 256;
+  const long long want = (units + threads - 1) / threads;
+  const int blocks = static_cast<int>(std::min<long long>(want, 148LL * 16));
+  k_tile_experts<<<blocks, threads, 0, s>>>(wA, wB, sA, bA, sB, bB, experts, O, K, G, dual ? 1 : 0, dst,
+                                            record_bytes);
+  return cudaGetLastError();
+}
+
+uint64_t tiled_record_bytes(int O, int K, bool dual) {
+  const int nblk = (K / 2 + kBlkBytes - 1) / kBlkBytes;
+  return static_cast<uint64_t>(O / (dual ? 8 : 16)) * nblk * kTileChunk;
 }
 
 // ---------------------------------------------------------------------------

@@ -48,15 +48,31 @@ DeviceInfo device_info();
 cudaError_t ensure_exp_table(cudaStream_t stream);
 uint32_t *device_error_word();
 
-// Fixed-point limbs of bf16 rows: limbs [rows][groups][2][G] fp16 (fragment
-// order), meta [rows][groups] float4 {fl(SX), A, B, 0} with A*B = 2^k (see scale_pow2).
+// Row fixed point of bf16 rows: limbs [rows][groups][2][G] fp16 (fragment
+// order), meta [rows][meta_pitch(groups)] float (fl(SX) per group, then
+// {A, B}; see meta_a_index).
 cudaError_t launch_prep_rows(const uint16_t *rows, int n_rows, int K, int G,
-                             uint16_t *limbs, float4 *meta, cudaStream_t s);
+                             uint16_t *limbs, float *meta, cudaStream_t s);
 
 // Stable counting-sort grouping of routes (+ optional shared bin).
 cudaError_t launch_group(const uint32_t *routes, int n_pairs, int shared_tokens,
                          int array_experts, int table_records, GroupView gv,
                          cudaStream_t s);
+
+// Tiled expert tables (fnmoe_tile_experts): one kTileChunk-byte chunk per
+// (row group, 128-byte block) -- 8 gate + 8 up rows for gate/up, 16 rows for
+// down -- in MMA fragment order, scales and biases included.
+constexpr int kTileChunk = 2560;
+constexpr int kTileW = 2048;  // packed-word bytes at the start of a chunk
+
+struct TiledView {
+  const uint8_t *gate_up;   // [records][I/8 row groups][blocks][kTileChunk], or null
+  const uint8_t *down;      // [records][H/16 row groups][blocks][kTileChunk], or null
+  uint64_t gate_up_record;  // bytes per record
+  uint64_t down_record;
+  uint32_t records;         // routed experts (+1 when has_shared: the last record)
+  int has_shared;
+};
 
 struct ExpertCallArgs {
   ProjArrays gate, up, down;          // routed arrays (may be null if table-only)
@@ -66,16 +82,19 @@ struct ExpertCallArgs {
   int array_experts;                  // valid non-slot route range
   int tokens, slots, n_pairs;         // n_pairs = tokens*slots (routed)
   int H, I, I_shared, G;
+  int sb_async;                       // scale/bias bases 4-byte aligned (rows too when the group count is even)
+  int sb_bulk;                        // scale/bias bases 16-byte aligned
+  TiledView tiled;                    // tiled tables replace the arrays when set
 };
 
 // gate/up + SwiGLU over all grouped tiles -> act [n_total, I] bf16.
 cudaError_t launch_gate_up(const ExpertCallArgs &a, const GroupView &gv,
-                           const uint16_t *x_limbs, const float4 *x_meta,
+                           const uint16_t *x_limbs, const float *x_meta,
                            uint16_t *act, uint16_t *g_out, uint16_t *u_out,
                            cudaStream_t s);
 // down projection -> d [n_total, H] bf16.
 cudaError_t launch_down(const ExpertCallArgs &a, const GroupView &gv,
-                        const uint16_t *act_limbs, const float4 *act_meta,
+                        const uint16_t *act_limbs, const float *act_meta,
                         uint16_t *d, cudaStream_t s);
 
 // Combine modes.
@@ -99,6 +118,13 @@ cudaError_t launch_softmax_topk(const uint16_t *logits, int T, int E, int k,
                                 uint16_t *scores, uint16_t *mass,
                                 const uint16_t *shared_logit,
                                 uint16_t *shared_gate, cudaStream_t s);
+
+// Repack `experts` experts' projections (reference layout) into tiled
+// records: dual = gate (A) + up (B) rows, else down rows.
+cudaError_t launch_tile_experts(const uint32_t *wA, const uint32_t *wB, const uint16_t *sA, const uint16_t *bA,
+                                const uint16_t *sB, const uint16_t *bB, int experts, int O, int K, int G, bool dual,
+                                uint8_t *dst, uint64_t record_bytes, cudaStream_t s);
+uint64_t tiled_record_bytes(int O, int K, bool dual);
 
 cudaError_t launch_dequant(const uint32_t *w, const uint16_t *sc,
                            const uint16_t *bi, uint16_t *out, uint64_t rows,

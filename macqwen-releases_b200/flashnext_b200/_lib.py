@@ -13,7 +13,7 @@ import threading
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libfnmoe.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 OK = 0
 ERR_NULL = -1
@@ -70,6 +70,14 @@ class FnMoEArgs(ctypes.Structure):
     ]
 
 
+class FnTiledExperts(ctypes.Structure):
+    _fields_ = [
+        ("gate_up", _vp), ("down", _vp),
+        ("gate_up_record_bytes", _u64), ("down_record_bytes", _u64),
+        ("records", _u32), ("has_shared", _u32),
+    ]
+
+
 class FnMoELayerArgs(ctypes.Structure):
     _fields_ = [
         ("abi_version", _u32), ("top_k", _u32),
@@ -88,6 +96,18 @@ class FnMoELayerArgs(ctypes.Structure):
         ("table_routes_of_expert", _vp),
         ("output", _vp), ("logits_out", _vp), ("inds_out", _vp), ("scores_out", _vp),
         ("workspace", _vp), ("workspace_bytes", _u64),
+        ("tiled", FnTiledExperts),
+    ]
+
+
+class FnTileArgs(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", _u32), ("experts", _u32), ("hidden_size", _u32), ("inter_size", _u32),
+        ("group_size", _u32), ("first_record", _u32),
+        ("gate_weight", _vp), ("gate_scales", _vp), ("gate_biases", _vp),
+        ("up_weight", _vp), ("up_scales", _vp), ("up_biases", _vp),
+        ("down_weight", _vp), ("down_scales", _vp), ("down_biases", _vp),
+        ("tiled", FnTiledExperts),
     ]
 
 
@@ -116,6 +136,8 @@ SIGNATURES = {
     "fnmoe_group_tokens": ([_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _u64, _vp], ctypes.c_int),
     "fnmoe_moe_layer_workspace_size": ([ctypes.POINTER(FnMoELayerArgs), ctypes.POINTER(_u64)], ctypes.c_int),
     "fnmoe_moe_layer": ([ctypes.POINTER(FnMoELayerArgs), _vp], ctypes.c_int),
+    "fnmoe_tiled_record_bytes": ([_u32, _u32, _u32, ctypes.POINTER(_u64), ctypes.POINTER(_u64)], ctypes.c_int),
+    "fnmoe_tile_experts": ([ctypes.POINTER(FnTileArgs), _vp], ctypes.c_int),
     "fnmoe_dequantize": ([_vp, _vp, _vp, _vp, _u64, _u32, _u32, _vp], ctypes.c_int),
     "fnmoe_swiglu": ([_vp, _vp, _vp, _u64, _vp], ctypes.c_int),
     "fnmoe_paged_decode_workspace_size": ([ctypes.POINTER(FnPagedArgs), ctypes.POINTER(_u64)], ctypes.c_int),

@@ -22,6 +22,7 @@ from typing import Any, Mapping
 from . import _lib
 from .cuda_runtime import _bf16, _dev, _stream, _Workspace
 from .expert_table import ExpertTable
+from .tiled import TiledExperts
 
 
 def _torch():
@@ -44,11 +45,15 @@ class SparseMoEBlock:
     :class:`ExpertTable` whose record ``e`` holds expert ``e`` (or
     ``route_map[e]`` when given).  ``shared`` is the same mapping for the
     shared expert ([O,K/8] etc. without the expert axis) or None.
+
+    With ``tiled`` (the default for array experts whose sizes allow it) the
+    experts are repacked once into :class:`TiledExperts` and the layer reads
+    only those; ``tiled=False`` keeps reading the reference-layout arrays.
     """
 
     def __init__(self, router_weight, experts: Any, *, top_k: int = 10, shared: Mapping | None = None,
                  shared_expert_gate=None, group_size: int = 32, renorm_blend: float = 1.0,
-                 route_map=None):
+                 route_map=None, tiled: bool = True):
         torch = _torch()
         self.router_weight = _bf16(router_weight, "router_weight")
         self.expert_count, self.hidden_size = (int(v) for v in self.router_weight.shape)
@@ -75,6 +80,10 @@ class SparseMoEBlock:
             if shared_expert_gate is None:
                 raise ValueError("shared expert needs its sigmoid gate weight")
             self.shared_expert_gate = _bf16(shared_expert_gate, "shared_expert_gate").reshape(-1)
+        self.tiled = None
+        if (tiled and self.experts is not None and self.inter_size % 8 == 0 and self.hidden_size % 16 == 0):
+            self.tiled = TiledExperts(self.experts, self.shared, group_size=self.group_size)
+            self.experts = None
         self._ws = _Workspace()
         self.last_inds = None
         self.last_scores = None
@@ -92,7 +101,9 @@ class SparseMoEBlock:
         a.inter_size = self.inter_size
         a.expert_count = self.expert_count
         a.group_size = self.group_size
-        if self.experts is not None:
+        if self.tiled is not None:
+            a.tiled = self.tiled.abi()
+        elif self.experts is not None:
             for name, key in (("gate_proj", "gate"), ("up_proj", "up"), ("down_proj", "down")):
                 w, s, b = self.experts[name]
                 setattr(a, f"{key}_weight", w.data_ptr())
@@ -105,6 +116,8 @@ class SparseMoEBlock:
         if self.shared is not None:
             a.shared_inter_size = int(self.shared["gate_proj"][0].shape[0])
             for name, key in (("gate_proj", "gate"), ("up_proj", "up"), ("down_proj", "down")):
+                if self.tiled is not None:
+                    break
                 w, s, b = self.shared[name]
                 setattr(a, f"shared_{key}_weight", w.data_ptr())
                 setattr(a, f"shared_{key}_scales", s.data_ptr())

@@ -19,24 +19,23 @@ Reference anchors (paths inside 1architect/macqwen-releases):
 Canonical arithmetic.  The reference delegates the projection reduction to
 MLX's ``qmv`` helpers, whose source is not present.  This oracle (and the CUDA
 kernels, which implement exactly the same definition) fixes it as follows, for
-one projection row with packed codes ``q`` and bfloat16 ``s``/``b`` per group:
+one input row ``x`` of K values and one projection row with packed codes
+``q`` and bfloat16 ``s``/``b`` per group of G inputs (G = 32 or 64):
 
-1. per group g of G inputs (G = 32 or 64):
-   ``E = floor(log2 max|x_i|)``; ``X_i = trunc(x_i * 2**(22-E))`` (integers
-   below 2**23 in magnitude; exact for every bfloat16 input within 2**-15 of
-   the group maximum);
-   ``S = sum_i X_i*q_i`` and ``SX = sum_i X_i`` (exact integers);
-   ``t = fma(s, fl(S), fl(b*fl(SX)))``; ``u = fl(t * A)`` with
-   ``A*B = 2**(E-22)``, ``A = 2**max(E-22, -126)`` (so ``B = 1`` unless the
-   group's largest activation is below 2**-104).  ``fl`` is float32
-   round-to-nearest-even and ``fma`` a float32 fused multiply-add (one
-   rounding).  The group sums are exact, so they do not depend on any
-   summation order;
-2. ``P = min(4, 2**floor(log2(K/G)))`` chains over contiguous blocks of
-   groups: chain j starts at ``-0.0`` and, for every g with
-   ``(g*P) // (K/G) == j`` in increasing g, becomes ``fma(u_g, B_g, chain)``
-   (``= fl(chain + u_g)`` when ``B_g = 1``);
-3. ``y = (c0 + c2) + (c1 + c3)`` for P = 4, ``c0 + c1`` for P = 2, ``c0`` for P = 1.
+1. row fixed point: ``E = floor(log2 max_i |x_i|)`` over the whole row (0 for
+   an all-zero row); ``X_i = trunc(x_i * 2**(22-E))`` (integers below 2**23
+   in magnitude; exact for every bfloat16 input within 2**-15 of the row
+   maximum);
+2. per group g: ``S_g = sum_i X_i*q_i`` and ``SX_g = sum_i X_i`` (exact
+   integers, so independent of any summation order);
+3. one chain from ``acc = -0.0``, groups in increasing order:
+   ``acc = fma(s_g, fl(S_g), acc)``; ``acc = fma(b_g, fl(SX_g), acc)``;
+4. ``y = fl(fl(acc * A) * B)`` with ``A*B = 2**(E-22)``,
+   ``A = 2**max(E-22, -126)`` (``B = 1`` unless the row's largest input is
+   below 2**-104).
+
+``fl`` is float32 round-to-nearest-even and ``fma`` a float32 fused
+multiply-add (one rounding).
 
 Router dot products (bfloat16 weights) are exact per product and summed in a
 fixed 32-lane order (see ``router_logits``).  ``exp`` is correctly rounded:
@@ -133,30 +132,20 @@ def swiglu_bf16(gate, up) -> np.ndarray:
 # --------------------------------------------------------------------------
 
 
-def chain_count(groups: int) -> int:
-    """Number of summation chains P for ``groups`` groups per row."""
-    p = 1
-    while p * 2 <= min(4, groups):
-        p *= 2
-    return p
+def fixed_point_rows(x):
+    """Row fixed point of the inputs.
 
-
-def fixed_point_groups(x, group_size: int):
-    """Block fixed point of each input group.
-
-    Returns ``(E, X)``: ``E`` [N, Gc] the floor(log2) of the largest magnitude
-    (0 for an all-zero group) and ``X`` [N, Gc, G] the integers
+    Returns ``(E, X)``: ``E`` [N] the floor(log2) of each row's largest
+    magnitude (0 for an all-zero row) and ``X`` [N, K] the integers
     ``trunc(x * 2**(22 - E))`` as float64 (exact, |X| < 2**23).
     """
     x = np.asarray(x, dtype=np.float64)
-    n, k = x.shape
-    xg = x.reshape(n, k // group_size, group_size)
-    nz = xg != 0
-    _, e = np.frexp(np.abs(xg))
+    nz = x != 0
+    _, e = np.frexp(np.abs(x))
     e = np.where(nz, e - 1, -(1 << 20))
     emax = e.max(axis=-1)
     emax = np.where(nz.any(axis=-1), emax, 0).astype(np.int64)
-    X = np.trunc(np.ldexp(xg, (22 - emax)[..., None].astype(np.int32)))
+    X = np.trunc(np.ldexp(x, (22 - emax)[..., None].astype(np.int32)))
     return emax, X
 
 
@@ -213,16 +202,8 @@ def scale_factors(k):
 
 
 
-def _tree(chains):
-    if len(chains) == 4:
-        return (chains[0] + chains[2]) + (chains[1] + chains[3])
-    if len(chains) == 2:
-        return chains[0] + chains[1]
-    return chains[0]
-
-
 def qmv(x, codes, scales, biases, group_size: int = 32) -> np.ndarray:
-    """Canonical Q4 projection rows.
+    """Canonical Q4 projection rows (steps 1-4 of the module docstring).
 
     x      [N, K] float32 (bfloat16 values)
     codes  [O, K] uint8 nibbles
@@ -233,28 +214,23 @@ def qmv(x, codes, scales, biases, group_size: int = 32) -> np.ndarray:
     n, k = x.shape
     o = codes.shape[0]
     gc = k // group_size
-    emax, X = fixed_point_groups(x, group_size)          # [N,Gc], [N,Gc,G]
+    emax, X = fixed_point_rows(x)                          # [N], [N,K]
+    Xg = X.reshape(n, gc, group_size)
     qf = np.asarray(codes, np.float64).reshape(o, gc, group_size)
     # S[g, n, o]: exact integer dot products (every partial sum < 2**53).
-    S = np.matmul(X.transpose(1, 0, 2), qf.transpose(1, 2, 0))
-    fS = S.astype(np.float32).transpose(1, 2, 0)          # [N, O, Gc]
-    fSX = X.sum(axis=-1).astype(np.float32)               # [N, Gc]
-    s = np.broadcast_to(np.asarray(scales, np.float32)[None], fS.shape)   # [N, O, Gc]
-    b = np.asarray(biases, np.float32)[None]
-    with np.errstate(all="ignore"):
-        pb = (b * fSX[:, None, :]).astype(np.float32)
-    t = fma32(s, fS, pb)
-    A, B = scale_factors((emax - 22)[:, None, :])
-    with np.errstate(all="ignore"):
-        u = (t * A).astype(np.float32)
-    B = np.broadcast_to(B, u.shape)
-    p = chain_count(gc)
-    chains = [np.full((n, o), -0.0, dtype=np.float32) for _ in range(p)]
+    S = np.matmul(Xg.transpose(1, 0, 2), qf.transpose(1, 2, 0))
+    fS = S.astype(np.float32)                              # [Gc, N, O]
+    fSX = Xg.sum(axis=-1).astype(np.float32)               # [N, Gc]
+    s = np.asarray(scales, np.float32)
+    b = np.asarray(biases, np.float32)
+    acc = np.full((n, o), -0.0, dtype=np.float32)
     for g in range(gc):
-        j = (g * p) // gc
-        chains[j] = fma32(u[:, :, g], B[:, :, g], chains[j])
+        acc = fma32(s[None, :, g], fS[g], acc)
+        acc = fma32(b[None, :, g], fSX[:, g:g + 1], acc)
+    A, B = scale_factors(emax - 22)
     with np.errstate(all="ignore"):
-        return _tree(chains).astype(np.float32)
+        u = (acc * A[:, None]).astype(np.float32)
+        return (u * B[:, None]).astype(np.float32)
 
 
 def expert_parts(words, scales, biases):

@@ -87,6 +87,10 @@ int main(void) {
   printf("FnMoELayerArgs %zu %zu %zu\n", sizeof(FnMoELayerArgs), offsetof(FnMoELayerArgs, table),
          offsetof(FnMoELayerArgs, workspace));
   printf("FnPagedArgs %zu %zu\n", sizeof(FnPagedArgs), offsetof(FnPagedArgs, q));
+  printf("FnTiledExperts %zu %zu\n", sizeof(FnTiledExperts), offsetof(FnTiledExperts, records));
+  printf("FnTileArgs %zu %zu %zu\n", sizeof(FnTileArgs), offsetof(FnTileArgs, gate_weight),
+         offsetof(FnTileArgs, tiled));
+  printf("LayerTiled %zu\n", offsetof(FnMoELayerArgs, tiled));
   return 0;
 }
 """
@@ -109,3 +113,22 @@ def test_struct_layout_matches_c_compiler(tmp_path):
     assert got == [s(_lib.FnMoELayerArgs), _lib.FnMoELayerArgs.table.offset, _lib.FnMoELayerArgs.workspace.offset]
     got = [int(v) for v in lines["FnPagedArgs"].split()]
     assert got == [s(_lib.FnPagedArgs), _lib.FnPagedArgs.q.offset]
+    got = [int(v) for v in lines["FnTiledExperts"].split()]
+    assert got == [s(_lib.FnTiledExperts), _lib.FnTiledExperts.records.offset]
+    got = [int(v) for v in lines["FnTileArgs"].split()]
+    assert got == [s(_lib.FnTileArgs), _lib.FnTileArgs.gate_weight.offset, _lib.FnTileArgs.tiled.offset]
+    assert int(lines["LayerTiled"]) == _lib.FnMoELayerArgs.tiled.offset
+
+
+def test_tiled_record_bytes_without_gpu():
+    """Record sizes of the tiled tables: one 2560-byte chunk per (row group,
+    128-byte block); gate/up groups hold 8 gate + 8 up rows, down groups 16 rows."""
+    lib = _lib.load()
+    gu, dn = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    assert lib.fnmoe_tiled_record_bytes(2048, 512, 32, ctypes.byref(gu), ctypes.byref(dn)) == _lib.OK
+    assert gu.value == (512 // 8) * (1024 // 128) * 2560 == 2 * (512 * 1024 + 2 * 512 * 64 * 2)
+    assert dn.value == (2048 // 16) * (256 // 128) * 2560 == 2048 * 256 + 2 * 2048 * 16 * 2
+    # H3072 / I640: the down rows (320 bytes) end in a partial block
+    assert lib.fnmoe_tiled_record_bytes(3072, 640, 32, ctypes.byref(gu), ctypes.byref(dn)) == _lib.OK
+    assert gu.value == 80 * 12 * 2560 and dn.value == 192 * 3 * 2560
+    assert lib.fnmoe_tiled_record_bytes(2048, 100, 32, ctypes.byref(gu), ctypes.byref(dn)) == _lib.ERR_SHAPE

@@ -331,6 +331,39 @@ def test_moe_layer_with_expert_table(cuda_lib):
     assert torch.equal(arrays.view(torch.int16), via.view(torch.int16))
 
 
+@pytest.mark.parametrize("tokens,hidden,inter,experts,group", [
+    (64, 2048, 512, 512, 32),   # headline layer, Zipf routing
+    (5, 2560, 640, 24, 32),     # down rows (320 bytes) end in a partial block; Gc = 20
+    (7, 1024, 256, 16, 64),     # group size 64
+    (3, 3072, 640, 12, 32),     # qwen4 full-depth layer shape
+])
+def test_tiled_layer_matches_arrays_and_oracle(cuda_lib, tokens, hidden, inter, experts, group):
+    """The tiled tables (one bulk-copied chunk per row group and block) give
+    the same bits as the reference-layout arrays, and both match the oracle."""
+    import torch
+
+    from flashnext_b200 import synthetic
+    from flashnext_b200.moe_block import SparseMoEBlock
+    k = min(10, experts)
+    L = synthetic.moe_layer(tokens, hidden, inter, experts, k, group, zipf=1.1 if tokens >= 64 else None,
+                            seed=tokens + hidden)
+    kw = dict(top_k=k, shared=L.shared, shared_expert_gate=L.shared_expert_gate, group_size=group)
+    tiled = SparseMoEBlock(L.router_weight, L.experts, **kw)
+    assert tiled.tiled is not None
+    arrays = SparseMoEBlock(L.router_weight, L.experts, tiled=False, **kw)
+    assert arrays.tiled is None
+    a = arrays(L.x).clone()
+    t = tiled(L.x)
+    assert torch.equal(a.view(torch.int16), t.view(torch.int16))
+    if tokens <= 7:
+        nb = _bank_np(L.experts)
+        sh = {n: (_np(w), _np(s), _np(b)) for n, (w, s, b) in L.shared.items()}
+        ref = moe.moe_block(_np(L.x), _np(L.router_weight), k, nb["gate_proj"], nb["up_proj"], nb["down_proj"],
+                            (sh["gate_proj"], sh["up_proj"], sh["down_proj"]), _np(L.shared_expert_gate),
+                            group_size=group)
+        assert_bf16_equal(_np(t), ref["out"], "tiled layer output")
+
+
 # --------------------------------------------------------------------------
 # paged attention
 # --------------------------------------------------------------------------

@@ -36,18 +36,20 @@ def test_dequantize_is_single_rounded_affine():
 def test_fixed_point_limbs_are_exact():
     rng = np.random.default_rng(3)
     x = _bf(rng, (5, 128))
-    x[0, :32] = 0.0                      # all-zero group
+    x[0, :] = 0.0                        # all-zero row
     x[1, 5] = np.float32(2.0 ** -130)    # subnormal-range value
-    emax, X = moe.fixed_point_groups(x, 32)
+    x[2, :] = x[2, :] * np.float32(2.0 ** -120)
+    emax, X = moe.fixed_point_rows(x)
     assert np.all(np.abs(X) < 2 ** 23)
+    assert emax[0] == 0 and not X[0].any()
     l0, l1 = moe.limbs(X)
     assert l1.min() >= -2048 and l1.max() <= 2047 and np.abs(l0).max() <= 2048
     np.testing.assert_array_equal(4096 * l0 + l1, X.astype(np.int64))
-    # every value within 2^-15 of its group maximum is represented exactly
-    xg = x.reshape(5, 4, 32).astype(np.float64)
-    back = np.ldexp(X, (emax - 22)[..., None].astype(np.int32))
-    big = np.abs(xg) >= np.ldexp(1.0, (emax - 15)[..., None].astype(np.int32))
-    np.testing.assert_array_equal(back[big], xg[big])
+    # every value within 2^-15 of its row maximum is represented exactly
+    xr = x.astype(np.float64)
+    back = np.ldexp(X, (emax - 22)[:, None].astype(np.int32))
+    big = np.abs(xr) >= np.ldexp(1.0, (emax - 15)[:, None].astype(np.int32))
+    np.testing.assert_array_equal(back[big], xr[big])
 
 
 @pytest.mark.parametrize("group,k", [(32, 2048), (32, 512), (64, 640), (32, 32), (64, 64), (32, 96)])
@@ -62,14 +64,6 @@ def test_qmv_matches_float64(group, k):
     dense = np.repeat(s, group, 1).astype(np.float64) * codes + np.repeat(b, group, 1)
     ref = x.astype(np.float64) @ dense.T
     np.testing.assert_allclose(y, ref, rtol=0, atol=1e-5 * np.abs(ref).max() + 1e-30)
-
-
-def test_chain_partition_covers_groups_once():
-    for gc in (1, 2, 3, 4, 5, 10, 16, 20, 64, 80):
-        p = moe.chain_count(gc)
-        owners = [(g * p) // gc for g in range(gc)]
-        assert sorted(set(owners)) == list(range(p))
-        assert owners == sorted(owners)
 
 
 def _ml_bf16_swiglu(g, u):
