@@ -123,7 +123,7 @@ void carve_core(Carver &cv, Layout &L, int T, int H, int I, int G, int n_total, 
   L.gv.offsets = cv.take<int32_t>(static_cast<uint64_t>(n_bins) + 1);
   L.gv.order = cv.take<int32_t>(n_total);
   L.gv.tiles = cv.take<int4>(3 * static_cast<uint64_t>(L.gv.max_tiles));
-  L.gv.n_tiles = cv.take<int32_t>(1);
+  L.gv.n_tiles = cv.take<int32_t>(4);
   L.gv.bin_key = cv.take<uint32_t>(n_bins);
   L.act = cv.take<uint16_t>(static_cast<uint64_t>(n_total) * I);
   L.al = cv.take<uint16_t>(static_cast<uint64_t>(n_total) * Gi * 2 * G);
@@ -427,7 +427,7 @@ int fnmoe_group_tokens(const uint32_t *routes, uint32_t pairs, uint32_t array_ex
   gv.max_tiles = static_cast<int>(pairs) / kTokPerItem + (n_bins < static_cast<int>(pairs) ? n_bins : static_cast<int>(pairs)) + 1;
   Carver cv(workspace);
   gv.tiles = cv.take<int4>(3 * static_cast<uint64_t>(gv.max_tiles));
-  gv.n_tiles = cv.take<int32_t>(1);
+  gv.n_tiles = cv.take<int32_t>(4);
   gv.bin_key = cv.take<uint32_t>(n_bins);
   if (workspace == nullptr || workspace_bytes < cv.off)
     return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(cv.off) + " bytes");

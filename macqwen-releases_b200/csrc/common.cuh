@@ -117,20 +117,32 @@ __device__ __forceinline__ uint32_t nibble_pair(uint32_t w, int j) {
 // nibbles (N, N+4) of word x (rows r and r+8 of the m16n8k16 fragment).
 // Even pairs use the 1024 + q encoding, odd pairs the unshifted 1024 + 16q.
 __device__ __forceinline__ void nibble_operands(uint32_t wa, uint32_t wb, uint32_t A0[4], uint32_t A1[4]) {
-  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
-  const __half2 k16th = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));
-  const __half2 km64 = __halves2half2(__ushort_as_half(0xD400), __ushort_as_half(0xD400));
-  const uint32_t wa8 = wa >> 8, wb8 = wb >> 8;
-  uint32_t t;
-  __half2 h;
-  t = (wa & 0x000F000Fu) | 0x64006400u; h = __hsub2(*reinterpret_cast<const __half2 *>(&t), k1024); A0[0] = *reinterpret_cast<uint32_t *>(&h);
-  t = (wb & 0x000F000Fu) | 0x64006400u; h = __hsub2(*reinterpret_cast<const __half2 *>(&t), k1024); A0[1] = *reinterpret_cast<uint32_t *>(&h);
-  t = (wa & 0x00F000F0u) | 0x64006400u; h = __hfma2(*reinterpret_cast<const __half2 *>(&t), k16th, km64); A0[2] = *reinterpret_cast<uint32_t *>(&h);
-  t = (wb & 0x00F000F0u) | 0x64006400u; h = __hfma2(*reinterpret_cast<const __half2 *>(&t), k16th, km64); A0[3] = *reinterpret_cast<uint32_t *>(&h);
-  t = (wa8 & 0x000F000Fu) | 0x64006400u; h = __hsub2(*reinterpret_cast<const __half2 *>(&t), k1024); A1[0] = *reinterpret_cast<uint32_t *>(&h);
-  t = (wb8 & 0x000F000Fu) | 0x64006400u; h = __hsub2(*reinterpret_cast<const __half2 *>(&t), k1024); A1[1] = *reinterpret_cast<uint32_t *>(&h);
-  t = (wa8 & 0x00F000F0u) | 0x64006400u; h = __hfma2(*reinterpret_cast<const __half2 *>(&t), k16th, km64); A1[2] = *reinterpret_cast<uint32_t *>(&h);
-  t = (wb8 & 0x00F000F0u) | 0x64006400u; h = __hfma2(*reinterpret_cast<const __half2 *>(&t), k16th, km64); A1[3] = *reinterpret_cast<uint32_t *>(&h);
+  // (w & mask) | 0x6400 per half is 1024 + q (mask 0x000F) or 1024 + 16q
+  // (mask 0x00F0); subtracting 1024, or scaling by 1/16 and adding -64,
+  // leaves q exactly.  lop3 LUT 0xEA = (a & b) | c.
+  asm("{\n"
+      ".reg .b32 t0, t1, t2, t3, t4, t5, t6, t7, a8, b8;\n"
+      "shr.b32 a8, %8, 8;\n"
+      "shr.b32 b8, %9, 8;\n"
+      "lop3.b32 t0, %8, 0x000F000F, 0x64006400, 0xEA;\n"
+      "lop3.b32 t1, %9, 0x000F000F, 0x64006400, 0xEA;\n"
+      "lop3.b32 t2, %8, 0x00F000F0, 0x64006400, 0xEA;\n"
+      "lop3.b32 t3, %9, 0x00F000F0, 0x64006400, 0xEA;\n"
+      "lop3.b32 t4, a8, 0x000F000F, 0x64006400, 0xEA;\n"
+      "lop3.b32 t5, b8, 0x000F000F, 0x64006400, 0xEA;\n"
+      "lop3.b32 t6, a8, 0x00F000F0, 0x64006400, 0xEA;\n"
+      "lop3.b32 t7, b8, 0x00F000F0, 0x64006400, 0xEA;\n"
+      "sub.f16x2 %0, t0, %10;\n"
+      "sub.f16x2 %1, t1, %10;\n"
+      "fma.rn.f16x2 %2, t2, %11, %12;\n"
+      "fma.rn.f16x2 %3, t3, %11, %12;\n"
+      "sub.f16x2 %4, t4, %10;\n"
+      "sub.f16x2 %5, t5, %10;\n"
+      "fma.rn.f16x2 %6, t6, %11, %12;\n"
+      "fma.rn.f16x2 %7, t7, %11, %12;\n"
+      "}\n"
+      : "=r"(A0[0]), "=r"(A0[1]), "=r"(A0[2]), "=r"(A0[3]), "=r"(A1[0]), "=r"(A1[1]), "=r"(A1[2]), "=r"(A1[3])
+      : "r"(wa), "r"(wb), "r"(0x64006400u), "r"(0x2C002C00u), "r"(0xD400D400u));
 }
 
 // All four nibble pairs (j, j+4), j = 0..3, of a packed word as fp16x2.

@@ -100,31 +100,44 @@ __device__ __forceinline__ uint32_t half_pair(int lo, int hi) {
          (static_cast<uint32_t>(__half_as_ushort(__int2half_rn(hi))) << 16);
 }
 
-// One warp per row.  Lane l handles the 8-input slices l, l+32, ... (slice i
-// covers inputs 8i..8i+7).  Pass 1 finds the row's largest finite magnitude
-// (bfloat16 magnitudes order like their bit patterns); pass 2 writes both
-// limbs of each slice as one 16-byte store in fragment order
-// [e0,e4,e1,e5,e2,e6,e3,e7] and the per-group sums fl(SX).
-template <int G>
-__global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *__restrict__ rows, int n_rows, int K,
+// TPR threads (a multiple of 32, <= 256) per row, RPC rows per CTA.  Thread
+// tr of a row handles the 8-input slices tr, tr + TPR, ... (SPT of them;
+// slice i covers inputs 8i..8i+7), all loaded up front.  The row's largest
+// finite magnitude (bfloat16 magnitudes order like their bit patterns) is
+// reduced over its warps through shared memory; then each slice's limbs go
+// out as one 16-byte store per limb in fragment order
+// [e0,e4,e1,e5,e2,e6,e3,e7], and each group's sum fl(SX) (G/8 consecutive
+// slices = consecutive lanes) from a shuffle reduction.
+template <int G, int SPT>
+__global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *__restrict__ rows, int n_rows, int K, int TPR,
                                                    uint16_t *__restrict__ limbs, float *__restrict__ meta,
                                                    uint32_t *err) {
   constexpr int LPG = G / 8;  // lanes per group
+  __shared__ uint32_t s_mx[8][8];
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= n_rows) return;
+  const int rl = threadIdx.x / TPR;  // row within the CTA
+  const int tr = threadIdx.x - rl * TPR;
+  const int wr = tr >> 5;            // warp within the row
+  const int row = blockIdx.x * (blockDim.x / TPR) + rl;
+  const bool live = row < n_rows;
   const int Gc = K / G;
   const int slices = K / 8;
   const int mp = meta_pitch(Gc);
-  const uint4 *src = reinterpret_cast<const uint4 *>(rows + static_cast<size_t>(row) * K);
+  const uint4 *src = reinterpret_cast<const uint4 *>(rows + static_cast<size_t>(live ? row : 0) * K);
+  uint4 v[SPT];
+#pragma unroll
+  for (int k = 0; k < SPT; ++k) {
+    const int i = tr + k * TPR;
+    v[k] = (live && i < slices) ? __ldg(src + i) : make_uint4(0u, 0u, 0u, 0u);
+  }
   uint32_t mx = 0;
   bool bad = false;
-  for (int i = lane; i < slices; i += 32) {
-    const uint4 v = __ldg(src + i);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint32_t m = (w[k >> 1] >> (16 * (k & 1))) & 0x7FFFu;
+  for (int k = 0; k < SPT; ++k) {
+    const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t m = (w[e >> 1] >> (16 * (e & 1))) & 0x7FFFu;
       if (m >= 0x7F80u) bad = true;
       else mx = max(mx, m);
     }
@@ -132,27 +145,32 @@ __global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *__restrict__ 
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
   if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) set_error(err, kErrNonFinite);
+  if (TPR > 32) {
+    if (lane == 0) s_mx[rl][wr] = mx;
+    __syncthreads();
+    for (int q = 0; q < TPR / 32; ++q) mx = max(mx, s_mx[rl][q]);
+  }
+  if (!live) return;
   int E = 0;
   if (mx != 0) E = (mx >> 7) ? static_cast<int>(mx >> 7) - 127 : (31 - __clz(static_cast<int>(mx))) - 133;
   float *mrow = meta + static_cast<size_t>(row) * mp;
-  const int iters = (slices + 31) / 32;
-  for (int it = 0; it < iters; ++it) {
-    const int i = it * 32 + lane;
+#pragma unroll
+  for (int k = 0; k < SPT; ++k) {
+    const int i = tr + k * TPR;
     int sx = 0;
     if (i < slices) {
-      const uint4 v = __ldg(src + i);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
       int X[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        X[k] = fixed_x((w[k >> 1] >> (16 * (k & 1))) & 0xFFFFu, E);
-        sx += X[k];
+      for (int e = 0; e < 8; ++e) {
+        X[e] = fixed_x((w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu, E);
+        sx += X[e];
       }
       int l0[8], l1[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        l1[k] = ((X[k] + 2048) & 4095) - 2048;
-        l0[k] = (X[k] - l1[k]) >> 12;
+      for (int e = 0; e < 8; ++e) {
+        l1[e] = ((X[e] + 2048) & 4095) - 2048;
+        l0[e] = (X[e] - l1[e]) >> 12;
       }
       const int g = (8 * i) / G;
       const int within = (8 * i) - g * G;
@@ -166,28 +184,39 @@ __global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *__restrict__ 
     for (int off = 1; off < LPG; off <<= 1) sx += __shfl_xor_sync(0xFFFFFFFFu, sx, off);
     if (i < slices && (lane & (LPG - 1)) == 0) mrow[(8 * i) / G] = __int2float_rn(sx);
   }
-  if (lane == 0) {
+  if (tr == 0) {
     const int ai = meta_a_index(Gc);
     for (int g = Gc; g < ai; ++g) mrow[g] = 0.0f;
     const int k = E - 22;
     const int ka = max(k, -126);
-    mrow[ai] = __int_as_float((ka + 127) << 23);       // A = 2^ka, normal
+    mrow[ai] = __int_as_float((ka + 127) << 23);          // A = 2^ka, normal
     mrow[ai + 1] = __int_as_float((k - ka + 127) << 23);  // B = 2^(k-ka) in [2^-29, 1]
     mrow[ai + 2] = 0.0f;
     mrow[ai + 3] = 0.0f;
   }
 }
 
+template <int G>
+cudaError_t launch_prep_g(const uint16_t *rows, int n_rows, int K, uint16_t *limbs, float *meta, cudaStream_t s) {
+  const int slices = K / 8;
+  const int tpr = std::min(256, ((slices + 31) / 32) * 32);
+  const int spt = (slices + tpr - 1) / tpr;
+  const int rpc = std::min(8, 256 / tpr);
+  const int blocks = (n_rows + rpc - 1) / rpc;
+  const int threads = rpc * tpr;
+  uint32_t *err = device_error_word();
+  if (spt == 1) k_prep_rows<G, 1><<<blocks, threads, 0, s>>>(rows, n_rows, K, tpr, limbs, meta, err);
+  else if (spt == 2) k_prep_rows<G, 2><<<blocks, threads, 0, s>>>(rows, n_rows, K, tpr, limbs, meta, err);
+  else if (spt <= 4) k_prep_rows<G, 4><<<blocks, threads, 0, s>>>(rows, n_rows, K, tpr, limbs, meta, err);
+  else if (spt <= 8) k_prep_rows<G, 8><<<blocks, threads, 0, s>>>(rows, n_rows, K, tpr, limbs, meta, err);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
 cudaError_t launch_prep_rows(const uint16_t *rows, int n_rows, int K, int G,
                              uint16_t *limbs, float *meta, cudaStream_t s) {
   if (n_rows <= 0) return cudaSuccess;
-  const int blocks = (n_rows + 7) / 8;
-  uint32_t *err = device_error_word();
-  if (G == 32)
-    k_prep_rows<32><<<blocks, 256, 0, s>>>(rows, n_rows, K, limbs, meta, err);
-  else
-    k_prep_rows<64><<<blocks, 256, 0, s>>>(rows, n_rows, K, limbs, meta, err);
-  return cudaGetLastError();
+  return G == 32 ? launch_prep_g<32>(rows, n_rows, K, limbs, meta, s) : launch_prep_g<64>(rows, n_rows, K, limbs, meta, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -281,6 +310,7 @@ __global__ void __launch_bounds__(1024) k_group(const uint32_t *__restrict__ rou
   if (tid == 0) {
     gv.offsets[n_bins] = total_pairs;
     gv.n_tiles[0] = min(total_tiles, gv.max_tiles);
+
   }
   // Stable scatter: warp 0 walks pairs in index order, 32 at a time.
   if (tid < 32) {
@@ -494,6 +524,24 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
 // (bulk copy) writes.
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
+// Shared-memory loads from 32-bit shared-window addresses.  volatile keeps
+// them after the ring's waits and barriers.
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(v) : "r"(a));
+  return v;
+}
+
 struct RawDesc {
   int4 d0, d1, d2;
 };
@@ -536,12 +584,11 @@ __device__ __forceinline__ bool tiled_record(const ExpertCallArgs &a, uint32_t k
 // Resolve item `item` (tile descriptor rd) into its info and this lane's
 // copy sources.
 template <bool DUAL, bool TILED>
-__device__ __forceinline__ ItemInfo item_setup(const ExpertCallArgs &a, const RawDesc &rd, int item, int row_tiles,
-                                               int rows_per_tile, int wbase, int O, int K, int Gc, int nblk,
-                                               int lane, Src &src) {
+__device__ __forceinline__ ItemInfo item_setup(const ExpertCallArgs &a, const RawDesc &rd, int rt, int rows_per_tile,
+                                               int wbase, int O, int K, int Gc, int nblk, int lane, Src &src) {
   ItemInfo it{};
   src = Src{nullptr, nullptr};
-  it.rt = item - (item / row_tiles) * row_tiles;
+  it.rt = rt;
   it.len = rd.d0.z;
   const uint32_t key = static_cast<uint32_t>(rd.d0.x);
   const int o_base = it.rt * rows_per_tile + wbase;
@@ -666,12 +713,13 @@ __device__ __forceinline__ void ring_wait(Ring &rg, uint32_t *err) {
 }
 
 // Stage the activation limbs and metadata of a tile's pairs (all threads) and
-// its pair ids.  Empty slots get zero limbs, zero sums and {A, B} = {1, 1}.
+// its pair ids.  Slots past the tile's length keep stale data: they only feed
+// MMA columns (and accumulators) whose results are never stored.
 __device__ __forceinline__ void load_xstage(uint8_t *st, int *s_pairs, const XStage &xs, const RawDesc &rd, bool ok,
                                             const uint16_t *__restrict__ xl, const float *__restrict__ xm,
                                             int n_pairs, int slots, bool by_token) {
   const int tid = threadIdx.x, nt = blockDim.x;
-  const int cpx = xs.Xrow / 16, cpm = xs.Mp / 16, a_chunk = xs.a_off / 16;
+  const int cpx = xs.Xrow / 16, cpm = xs.Mp / 16;
   const int len = rd.d0.z;
   const int pairs[kTokPerItem] = {rd.d1.x, rd.d1.y, rd.d1.z, rd.d1.w, rd.d2.x, rd.d2.y, rd.d2.z, rd.d2.w};
 #pragma unroll
@@ -686,11 +734,6 @@ __device__ __forceinline__ void load_xstage(uint8_t *st, int *s_pairs, const XSt
       const uint8_t *msrc = reinterpret_cast<const uint8_t *>(xm) + static_cast<size_t>(row) * xs.Mp;
       for (int cc = tid; cc < cpx; cc += nt) cp_async16(dst + cc * 16, src + cc * 16);
       for (int cc = tid; cc < cpm; cc += nt) cp_async16(mdst + cc * 16, msrc + cc * 16);
-    } else {
-      for (int cc = tid; cc < cpx; cc += nt) *reinterpret_cast<uint4 *>(dst + cc * 16) = make_uint4(0u, 0u, 0u, 0u);
-      for (int cc = tid; cc < cpm; cc += nt)
-        *reinterpret_cast<float4 *>(mdst + cc * 16) =
-            cc == a_chunk ? make_float4(1.0f, 1.0f, 0.0f, 0.0f) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
   }
 }
@@ -713,7 +756,7 @@ __device__ __forceinline__ float f_at(const float4 &v, int i) {
 // token limbs, fold S and SX into the accumulators.
 template <int G, int NT>
 __device__ __forceinline__ void group_step(const uint32_t (&qa)[G / 32], const uint32_t (&qb)[G / 32], float sA,
-                                           float bA, float sB, float bB, const uint8_t *xgj, int xstep,
+                                           float bA, float sB, float bB, uint32_t xgj, int xstep,
                                            const float (&fs)[NT], float (&accA)[NT], float (&accB)[NT]) {
   constexpr int WB = G / 32;
   uint32_t A0[WB][4], A1[WB][4];
@@ -724,7 +767,7 @@ __device__ __forceinline__ void group_step(const uint32_t (&qa)[G / 32], const u
     float C[4];
 #pragma unroll
     for (int wb = 0; wb < WB; ++wb) {
-      const uint4 v = *reinterpret_cast<const uint4 *>(xgj + t * xstep + wb * 64);
+      const uint4 v = lds128(xgj + t * xstep + wb * 64);
       if (wb == 0) mma_16816_z(C, A0[wb], v.x, v.y);
       else mma_16816(C, A0[wb], v.x, v.y);
       mma_16816(C, A1[wb], v.z, v.w);
@@ -740,45 +783,46 @@ __device__ __forceinline__ void group_step(const uint32_t (&qa)[G / 32], const u
 // tiles, in halves (scales, biases and group sums of one half live in
 // registers at a time).  TAIL blocks stop at the last group.
 template <int G, int NT, bool TAIL, bool TILED>
-__device__ __forceinline__ void compute_block(const uint8_t *st, const uint8_t *xg, const uint8_t *mg, int xstep,
-                                              int mstep, int g0, int Gc, int r, int c, float (&accA)[NT],
-                                              float (&accB)[NT]) {
+__device__ __forceinline__ void compute_block(uint32_t st, uint32_t xg, uint32_t mg, int xstep, int mstep, int g0,
+                                              int Gc, int r, int c, float (&accA)[NT], float (&accB)[NT]) {
   constexpr int WB = G / 32;
   constexpr int GPB = 2 * kBlkBytes / G;
   constexpr int QG = GPB / 2;  // groups per half
-  const uint8_t *sbA = st + (TILED ? kTileW : kSBOff) + r * 32;
-  const uint8_t *sbB = sbA + 8 * 32;
+  const uint32_t sbA = st + (TILED ? kTileW : kSBOff) + r * 32;
+  const uint32_t sbB = sbA + 8 * 32;
+  const uint32_t wq = TILED ? st + (r * 4 + c) * 16 : st + r * kRowPitch + c * 4;
 #pragma unroll 1
   for (int h = 0; h < 2; ++h) {
     const int gh = h * QG;
     if (TAIL && g0 + gh >= Gc) break;
     uint2 sA2, bA2, sB2, bB2;
     if (QG == 4) {
-      sA2 = *reinterpret_cast<const uint2 *>(sbA + 2 * gh);
-      bA2 = *reinterpret_cast<const uint2 *>(sbA + 16 + 2 * gh);
-      sB2 = *reinterpret_cast<const uint2 *>(sbB + 2 * gh);
-      bB2 = *reinterpret_cast<const uint2 *>(sbB + 16 + 2 * gh);
+      sA2 = lds64(sbA + 2 * gh);
+      bA2 = lds64(sbA + 16 + 2 * gh);
+      sB2 = lds64(sbB + 2 * gh);
+      bB2 = lds64(sbB + 16 + 2 * gh);
     } else {
-      sA2 = make_uint2(*reinterpret_cast<const uint32_t *>(sbA + 2 * gh), 0u);
-      bA2 = make_uint2(*reinterpret_cast<const uint32_t *>(sbA + 16 + 2 * gh), 0u);
-      sB2 = make_uint2(*reinterpret_cast<const uint32_t *>(sbB + 2 * gh), 0u);
-      bB2 = make_uint2(*reinterpret_cast<const uint32_t *>(sbB + 16 + 2 * gh), 0u);
+      sA2 = make_uint2(lds32(sbA + 2 * gh), 0u);
+      bA2 = make_uint2(lds32(sbA + 16 + 2 * gh), 0u);
+      sB2 = make_uint2(lds32(sbB + 2 * gh), 0u);
+      bB2 = make_uint2(lds32(sbB + 16 + 2 * gh), 0u);
     }
     float4 fsx[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       if (QG == 4) {
-        fsx[t] = *reinterpret_cast<const float4 *>(mg + t * mstep + 4 * gh);
+        const uint4 f = lds128(mg + t * mstep + 4 * gh);
+        fsx[t] = make_float4(__uint_as_float(f.x), __uint_as_float(f.y), __uint_as_float(f.z), __uint_as_float(f.w));
       } else {
-        const float2 f = *reinterpret_cast<const float2 *>(mg + t * mstep + 4 * gh);
-        fsx[t] = make_float4(f.x, f.y, 0.0f, 0.0f);
+        const uint2 f = lds64(mg + t * mstep + 4 * gh);
+        fsx[t] = make_float4(__uint_as_float(f.x), __uint_as_float(f.y), 0.0f, 0.0f);
       }
     }
-    uint4 wA4, wB4;
+    uint4 wA4 = make_uint4(0u, 0u, 0u, 0u), wB4 = make_uint4(0u, 0u, 0u, 0u);
     if (TILED) {
       // fragment-ordered chunk: [half][A/B][slot r*4+c][4 words]
-      wA4 = *reinterpret_cast<const uint4 *>(st + (2 * h) * 512 + (r * 4 + c) * 16);
-      wB4 = *reinterpret_cast<const uint4 *>(st + (2 * h + 1) * 512 + (r * 4 + c) * 16);
+      wA4 = lds128(wq + (2 * h) * 512);
+      wB4 = lds128(wq + (2 * h + 1) * 512);
     }
 #pragma unroll
     for (int j = 0; j < QG; ++j) {
@@ -790,9 +834,9 @@ __device__ __forceinline__ void compute_block(const uint8_t *st, const uint8_t *
           qa[wb] = word_at(wA4, j * WB + wb);
           qb[wb] = word_at(wB4, j * WB + wb);
         } else {
-          const int off = (gh + j) * (G / 2) + wb * 16 + c * 4;
-          qa[wb] = *reinterpret_cast<const uint32_t *>(st + r * kRowPitch + off);
-          qb[wb] = *reinterpret_cast<const uint32_t *>(st + (r + 8) * kRowPitch + off);
+          const int off = (gh + j) * (G / 2) + wb * 16;
+          qa[wb] = lds32(wq + off);
+          qb[wb] = lds32(wq + 8 * kRowPitch + off);
         }
       }
       float fs[NT];
@@ -821,8 +865,10 @@ __device__ __forceinline__ void run_item(const ExpertCallArgs &a, const ItemInfo
   const int o0 = cur.rt * ROWS + warp * RPW + r;
   const int oA = o0;
   const int oB = DUAL ? o0 : o0 + 8;
-  const uint8_t *xb = xst + (r >> 1) * xs.Xrow + (r & 1) * (G * 2) + c * 16;
-  const uint8_t *mrow = xst + xs.m_off + c * xs.Mp;
+  const uint32_t xs0 = smem_u32(xst);
+  const uint32_t xb = xs0 + (r >> 1) * xs.Xrow + (r & 1) * (G * 2) + c * 16;
+  const uint32_t mrow = xs0 + xs.m_off + c * xs.Mp;
+  const uint32_t ring0 = smem_u32(rg.base);
   const int xstep = 4 * xs.Xrow, mstep = 4 * xs.Mp;
   const int full = Gc / GPB;  // blocks without a tail
   float accA[NT], accB[NT];
@@ -835,7 +881,7 @@ __device__ __forceinline__ void run_item(const ExpertCallArgs &a, const ItemInfo
       ring_fill<G, R, TILED>(rg, sc, sn, nblk, nb_nxt, lane, rowbytes, Gc, sb_mode);
     }
     ring_wait<TILED>(rg, err);  // block rg.consumed landed; all lanes are done with the previous one
-    const uint8_t *st = rg.base + rg.c_stage * kStageBytes;
+    const uint32_t st = ring0 + rg.c_stage * kStageBytes;
     ring_fill<G, R, TILED>(rg, sc, sn, nblk, nb_nxt, lane, rowbytes, Gc, sb_mode);
     const int g0 = cb * GPB;
     if (cb < full)
@@ -852,7 +898,8 @@ __device__ __forceinline__ void run_item(const ExpertCallArgs &a, const ItemInfo
     const int q = 4 * t + c;
     if (q < cur.len) {
       const int pair = s_pairs[q];
-      const float2 ab = *reinterpret_cast<const float2 *>(mrow + t * mstep + xs.a_off);
+      const uint2 abw = lds64(mrow + t * mstep + xs.a_off);
+      const float2 ab = make_float2(__uint_as_float(abw.x), __uint_as_float(abw.y));
       const float yA = __fmul_rn(__fmul_rn(accA[t], ab.x), ab.y);
       const float yB = __fmul_rn(__fmul_rn(accB[t], ab.x), ab.y);
       if (DUAL) {
@@ -872,6 +919,19 @@ __device__ __forceinline__ void run_item(const ExpertCallArgs &a, const ItemInfo
   }
 }
 
+// Tiles are visited in the order t = (pos * P) mod n_tiles, P a prime not
+// dividing n_tiles (a bijection).  Bins come sorted by key with the shared
+// expert's tiles -- all of them full -- last, so walking them in plain order
+// would hand a few CTAs the heaviest items; the stride spreads them over the
+// contiguous item ranges.
+__device__ __forceinline__ int tile_stride(int n) {
+  const int primes[6] = {97, 89, 83, 79, 73, 71};
+#pragma unroll
+  for (int i = 0; i < 6; ++i)
+    if (n % primes[i] != 0) return primes[i] % max(n, 1);
+  return 1;
+}
+
 template <int G, int WARPS, bool DUAL, int R, bool TILED>
 __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a, GroupView gv,
                                                                const uint16_t *__restrict__ xl,
@@ -888,9 +948,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a,
   const XStage xs = xstage_geom(K, G);
   const int row_tiles = (O + ROWS - 1) / ROWS;
   const int n_items = gv.n_tiles[0] * row_tiles;
-  const int i0 = static_cast<int>(static_cast<long long>(n_items) * blockIdx.x / gridDim.x);
-  const int i1 = static_cast<int>(static_cast<long long>(n_items) * (blockIdx.x + 1) / gridDim.x);
-  if (i0 >= i1) return;
+  if (n_items == 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rowbytes = K / 2;
   const int nblk = (rowbytes + kBlkBytes - 1) / kBlkBytes;
@@ -909,8 +967,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a,
 
   // Tiled tables hold whole row groups only: a warp whose rows start past
   // the last row has nothing to do (len -1 marks it: no bad-route error).
-  auto setup = [&](const RawDesc &rd, int item, Src &src) {
-    ItemInfo it = item_setup<DUAL, TILED>(a, rd, item, row_tiles, ROWS, wbase, O, K, xs.Gc, nblk, lane, src);
+  auto setup = [&](const RawDesc &rd, int rt, Src &src) {
+    ItemInfo it = item_setup<DUAL, TILED>(a, rd, rt, ROWS, wbase, O, K, xs.Gc, nblk, lane, src);
     if (TILED && it.rt * ROWS + wbase >= O) {
       it.ok = false;
       it.len = -1;
@@ -919,14 +977,38 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a,
     return it;
   };
 
+  // Each CTA takes a contiguous range of items: consecutive items usually
+  // share a tile and its staged activations.  Item cursors (row tile, tile)
+  // advance incrementally; tiles follow the stride order of tile_stride.
+  const int i0 = static_cast<int>(static_cast<long long>(n_items) * blockIdx.x / gridDim.x);
+  const int i1 = static_cast<int>(static_cast<long long>(n_items) * (blockIdx.x + 1) / gridDim.x);
+  if (i0 >= i1) return;
+  const int n_tiles = gv.n_tiles[0];
+  const int stride = tile_stride(n_tiles);
+  struct Cursor {
+    int rt, tile;
+  };
+  auto advance = [&](Cursor c) {
+    if (++c.rt == row_tiles) {
+      c.rt = 0;
+      c.tile += stride;
+      if (c.tile >= n_tiles) c.tile -= n_tiles;
+    }
+    return c;
+  };
+  const int pos0 = i0 / row_tiles;
+  Cursor c_cur{i0 - pos0 * row_tiles, static_cast<int>((static_cast<long long>(pos0) * stride) % n_tiles)};
+  Cursor c_nxt = advance(c_cur);
+  Cursor c_nn = advance(c_nxt);
+
   Src sc, sn;
-  const RawDesc rd0 = load_desc(gv, i0 / row_tiles);
-  ItemInfo cur = setup(rd0, i0, sc);
-  RawDesc rd_nxt = load_desc(gv, i0 + 1 < i1 ? (i0 + 1) / row_tiles : -1);
-  int4 d0_nn = i0 + 2 < i1 ? gv.tiles[3 * ((i0 + 2) / row_tiles)] : make_int4(0, 0, 0, 0);
+  const RawDesc rd0 = load_desc(gv, c_cur.tile);
+  ItemInfo cur = setup(rd0, c_cur.rt, sc);
+  RawDesc rd_nxt = load_desc(gv, i0 + 1 < i1 ? c_nxt.tile : -1);
+  int4 d0_nn = i0 + 2 < i1 ? gv.tiles[3 * c_nn.tile] : make_int4(0, 0, 0, 0);
   ItemInfo nxt{};
   sn = Src{nullptr, nullptr};
-  if (i0 + 1 < i1) nxt = setup(rd_nxt, i0 + 1, sn);
+  if (i0 + 1 < i1) nxt = setup(rd_nxt, c_nxt.rt, sn);
   int nb_cur = cur.ok ? nblk : 0;
   int nb_nxt = nxt.ok ? nblk : 0;
 
@@ -948,8 +1030,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a,
     }
     const int ni = item + 1;
     if (ni >= i1) break;
-    if (ni / row_tiles != item / row_tiles) {
-      __syncthreads();  // every warp is done with the staged activations and pair ids
+    if (c_nxt.rt == 0) {  // the next item starts a new tile
+      __syncthreads();    // every warp is done with the staged activations and pair ids
       load_xstage(smem, s_pairs, xs, rd_nxt, rd_nxt.d0.z > 0, xl, xm, a.n_pairs, a.slots, DUAL);
       cp_async_commit();
       cp_async_wait<0>();
@@ -961,16 +1043,19 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a,
     cur = nxt;
     sc = sn;
     nb_cur = nb_nxt;
+    c_cur = c_nxt;
+    c_nxt = c_nn;
+    c_nn = advance(c_nn);
     const int nn = ni + 1;
     rd_nxt.d0 = d0_nn;  // prefetched one item ahead; the pair ids are needed only at a tile change
     if (nn < i1) {
-      rd_nxt.d1 = gv.tiles[3 * (nn / row_tiles) + 1];
-      rd_nxt.d2 = gv.tiles[3 * (nn / row_tiles) + 2];
+      rd_nxt.d1 = gv.tiles[3 * c_nxt.tile + 1];
+      rd_nxt.d2 = gv.tiles[3 * c_nxt.tile + 2];
     }
-    d0_nn = nn + 1 < i1 ? gv.tiles[3 * ((nn + 1) / row_tiles)] : make_int4(0, 0, 0, 0);
+    d0_nn = nn + 1 < i1 ? gv.tiles[3 * c_nn.tile] : make_int4(0, 0, 0, 0);
     nxt = ItemInfo{};
     sn = Src{nullptr, nullptr};
-    if (nn < i1) nxt = setup(rd_nxt, nn, sn);
+    if (nn < i1) nxt = setup(rd_nxt, c_nxt.rt, sn);
     nb_nxt = nxt.ok ? nblk : 0;
   }
   // Every issued block was consumed (items run to completion), so no copy is
@@ -1000,7 +1085,7 @@ cudaError_t launch_rows(const ExpertCallArgs &a, const GroupView &gv, const uint
 }
 
 size_t ring_smem(int xbytes, int warps, int r) {
-  return static_cast<size_t>(xbytes) + static_cast<size_t>(warps) * r * (kStageBytes + 8) + kTokPerItem * sizeof(int);
+  return static_cast<size_t>(xbytes) + static_cast<size_t>(warps) * r * (kStageBytes + 8) + (kTokPerItem + 4) * sizeof(int);
 }
 
 // Deepest ring (4, 3 or 2 stages) whose shared memory fits beside the
@@ -1157,11 +1242,84 @@ uint64_t tiled_record_bytes(int O, int K, bool dual) {
 // combine (metal_runtime.py:301-333)
 // ---------------------------------------------------------------------------
 
-__global__ void k_combine(const uint16_t *__restrict__ d, const uint32_t *__restrict__ routes,
-                          const void *__restrict__ scores, int sf32, int T, int S, int H,
-                          int mode, const uint16_t *__restrict__ sy,
-                          const uint16_t *__restrict__ sh, const uint16_t *__restrict__ sg,
-                          int E_arr, int records, uint16_t *__restrict__ out) {
+constexpr int kCombineMaxSlots = 16;
+
+__device__ __forceinline__ float bf16_lane(const uint4 &v, int e) {
+  const uint32_t w = e < 2 ? v.x : e < 4 ? v.y : e < 6 ? v.z : v.w;
+  return __uint_as_float((e & 1) ? (w & 0xFFFF0000u) : (w << 16));
+}
+
+// Thread = 8 consecutive hidden elements of one token.  Every slot's route,
+// score and 16-byte output slice is loaded before the slot-ordered float32
+// accumulation (no fused multiply-add), so the loads overlap.
+__global__ void __launch_bounds__(256) k_combine(const uint16_t *__restrict__ d, const uint32_t *__restrict__ routes,
+                                                 const void *__restrict__ scores, int sf32, int T, int S, int H,
+                                                 int mode, const uint16_t *__restrict__ sy,
+                                                 const uint16_t *__restrict__ sh, const uint16_t *__restrict__ sg,
+                                                 int E_arr, int records, uint16_t *__restrict__ out) {
+  const int t = blockIdx.y;
+  const int h8 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (8 * h8 >= H || t >= T) return;
+  float sc[kCombineMaxSlots];
+  uint4 dv[kCombineMaxSlots];
+#pragma unroll
+  for (int s = 0; s < kCombineMaxSlots; ++s) {
+    sc[s] = 0.0f;
+    dv[s] = make_uint4(0u, 0u, 0u, 0u);
+    if (s < S) {
+      const uint32_t r = routes[t * S + s];
+      const bool valid = (r & kSlotBit) ? ((r & 0x7FFFFFFFu) < static_cast<uint32_t>(records))
+                                        : (r < static_cast<uint32_t>(E_arr));
+      if (valid) {
+        sc[s] = sf32 ? static_cast<const float *>(scores)[t * S + s]
+                     : bf16_to_f32(static_cast<const uint16_t *>(scores)[t * S + s]);
+        dv[s] = ldg_u128(reinterpret_cast<const uint4 *>(d + (static_cast<size_t>(t) * S + s) * H + 8 * h8));
+      } else {
+        sc[s] = __int_as_float(0x7FC00000);  // marks an invalid slot (skipped below)
+      }
+    }
+  }
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+#pragma unroll
+  for (int s = 0; s < kCombineMaxSlots; ++s) {
+    if (s < S && !isnan(sc[s])) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], __fmul_rn(bf16_lane(dv[s], e), sc[s]));
+    }
+  }
+  const size_t base = static_cast<size_t>(t) * H + 8 * h8;
+  uint4 extra = make_uint4(0u, 0u, 0u, 0u);
+  float gate = 0.0f;
+  if (mode == kCombineSharedY) extra = ldg_u128(reinterpret_cast<const uint4 *>(sy + base));
+  if (mode == kCombineParts) {
+    extra = ldg_u128(reinterpret_cast<const uint4 *>(sh + base));
+    gate = bf16_to_f32(sg[t]);
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float r2[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int e = 2 * q + h;
+      const float routed = round_bf16(acc[e]);
+      float res = routed;
+      if (mode == kCombineSharedY) res = __fadd_rn(routed, bf16_lane(extra, e));
+      else if (mode == kCombineParts) res = __fadd_rn(routed, bmul(bf16_lane(extra, e), gate));
+      r2[h] = res;
+    }
+    o[q] = static_cast<uint32_t>(f32_to_bf16(r2[0])) | (static_cast<uint32_t>(f32_to_bf16(r2[1])) << 16);
+  }
+  *reinterpret_cast<uint4 *>(out + base) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Any slot count: one element per thread, loads in the slot loop.
+__global__ void k_combine_any(const uint16_t *__restrict__ d, const uint32_t *__restrict__ routes,
+                              const void *__restrict__ scores, int sf32, int T, int S, int H, int mode,
+                              const uint16_t *__restrict__ sy, const uint16_t *__restrict__ sh,
+                              const uint16_t *__restrict__ sg, int E_arr, int records, uint16_t *__restrict__ out) {
   const int t = blockIdx.y;
   const int h = blockIdx.x * blockDim.x + threadIdx.x;
   if (h >= H || t >= T) return;
@@ -1177,15 +1335,9 @@ __global__ void k_combine(const uint16_t *__restrict__ d, const uint32_t *__rest
     acc = __fadd_rn(acc, __fmul_rn(dv, sc));
   }
   const float routed = round_bf16(acc);
-  float res;
-  if (mode == kCombineSharedY) {
-    res = __fadd_rn(routed, bf16_to_f32(sy[static_cast<size_t>(t) * H + h]));
-  } else if (mode == kCombineParts) {
-    const float comp = bmul(bf16_to_f32(sh[static_cast<size_t>(t) * H + h]), bf16_to_f32(sg[t]));
-    res = __fadd_rn(routed, comp);
-  } else {
-    res = routed;
-  }
+  float res = routed;
+  if (mode == kCombineSharedY) res = __fadd_rn(routed, bf16_to_f32(sy[static_cast<size_t>(t) * H + h]));
+  else if (mode == kCombineParts) res = __fadd_rn(routed, bmul(bf16_to_f32(sh[static_cast<size_t>(t) * H + h]), bf16_to_f32(sg[t])));
   out[static_cast<size_t>(t) * H + h] = f32_to_bf16(res);
 }
 
@@ -1194,9 +1346,17 @@ cudaError_t launch_combine(const uint16_t *d, const uint32_t *routes, const void
                            const uint16_t *shared_y, const uint16_t *shared,
                            const uint16_t *shared_gate, int array_experts, int table_records,
                            uint16_t *out, cudaStream_t s) {
-  dim3 grid((H + 255) / 256, tokens);
-  k_combine<<<grid, 256, 0, s>>>(d, routes, scores, scores_f32, tokens, slots, H, mode, shared_y,
-                                 shared, shared_gate, array_experts, table_records, out);
+  if (slots > kCombineMaxSlots || H % 8) {
+    dim3 grid((H + 255) / 256, tokens);
+    k_combine_any<<<grid, 256, 0, s>>>(d, routes, scores, scores_f32, tokens, slots, H, mode, shared_y, shared,
+                                       shared_gate, array_experts, table_records, out);
+    return cudaGetLastError();
+  }
+  const int chunks = H / 8;
+  const int threads = chunks >= 256 ? 256 : ((chunks + 31) / 32) * 32;
+  dim3 grid((chunks + threads - 1) / threads, tokens);
+  k_combine<<<grid, threads, 0, s>>>(d, routes, scores, scores_f32, tokens, slots, H, mode, shared_y,
+                                     shared, shared_gate, array_experts, table_records, out);
   return cudaGetLastError();
 }
 
@@ -1204,107 +1364,134 @@ cudaError_t launch_combine(const uint16_t *d, const uint32_t *routes, const void
 // router logits: bf16 GEMV with the canonical 32-lane order
 // ---------------------------------------------------------------------------
 
-constexpr int kRouterWarps = 4;
-constexpr int kRouterTokBlock = 8;
+constexpr int kRouterWarps = 8;  // warps per CTA
 
-template <int CH>
+// Grid (row groups, token blocks).  Each warp keeps kRouterRW router rows in
+// registers (RW = 2 up to hidden 3072, else 1) for blocks of kRouterTok tokens.
+// Each warp keeps kRouterRW router rows in
+// registers (lane j owns 8-element chunks j, j+32, ... of each) and runs the
+// canonical per-lane chain for every (row, token) of the block, reading each
+// staged input element once for both rows; then the xor butterfly.
+template <int CH, int kRouterRW, int kRouterTok>
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
     const uint16_t *__restrict__ x, const uint16_t *__restrict__ W, int T, int H, int E,
     const uint16_t *__restrict__ wsg, uint16_t *__restrict__ logits,
     uint16_t *__restrict__ shared_logit) {
-  extern __shared__ __align__(16) float xs[];  // [kRouterTokBlock][H]
+  extern __shared__ __align__(16) float xs[];  // [kRouterTok][H] float32
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kRouterWarps + warp;
+  const int row0 = (blockIdx.x * kRouterWarps + warp) * kRouterRW;
   const int rows = E + (wsg != nullptr ? 1 : 0);
   const int nchunks = H / 8;
-  const uint16_t *wrow = nullptr;
-  if (row < E) wrow = W + static_cast<size_t>(row) * H;
-  else if (row < rows) wrow = wsg;
-  float w[CH * 8];
+  const int t0 = blockIdx.y * kRouterTok;
+  const int tb = min(kRouterTok, T - t0);
+  // stage the token block as float32 (8 bf16 per 16-byte load)
+  const uint4 *xsrc = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t0) * H);
+  float4 *xdst = reinterpret_cast<float4 *>(xs);
+  for (int idx = threadIdx.x; idx < tb * nchunks; idx += blockDim.x) {
+    const uint4 v = ldg_u128(xsrc + idx);
+    xdst[2 * idx] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                                __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+    xdst[2 * idx + 1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
+                                    __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
+  }
+  float w[kRouterRW][CH * 8];
+  bool live[kRouterRW];
+#pragma unroll
+  for (int q = 0; q < kRouterRW; ++q) {
+    const int row = row0 + q;
+    const uint16_t *wrow = row < E ? W + static_cast<size_t>(row) * H : (row < rows ? wsg : nullptr);
+    live[q] = wrow != nullptr;
+#pragma unroll
+    for (int m = 0; m < CH; ++m) {
+      const int cidx = lane + 32 * m;
+      if (wrow != nullptr && cidx < nchunks) {
+        const uint4 v = ldg_u128(reinterpret_cast<const uint4 *>(wrow + cidx * 8));
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          w[q][m * 8 + 2 * i] = __uint_as_float(u[i] << 16);
+          w[q][m * 8 + 2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[q][m * 8 + i] = 0.0f;
+      }
+    }
+  }
+  __syncthreads();
+  if (!live[0]) return;
+  float acc[kRouterRW][kRouterTok];
+#pragma unroll
+  for (int q = 0; q < kRouterRW; ++q)
+#pragma unroll
+    for (int tt = 0; tt < kRouterTok; ++tt) acc[q][tt] = -0.0f;
 #pragma unroll
   for (int m = 0; m < CH; ++m) {
     const int cidx = lane + 32 * m;
-    if (wrow != nullptr && cidx < nchunks) {
-      const uint4 v = ldg_u128(reinterpret_cast<const uint4 *>(wrow + cidx * 8));
-      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    if (cidx < nchunks) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        w[m * 8 + 2 * i] = __uint_as_float(u[i] << 16);
-        w[m * 8 + 2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
-      }
-    } else {
+      for (int tt = 0; tt < kRouterTok; ++tt) {
+        // rows past tb hold stale data; their results are never stored
+        const float4 *xp = reinterpret_cast<const float4 *>(xs + tt * H + cidx * 8);
+        const float4 p0 = xp[0], p1 = xp[1];
+        const float xv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w[m * 8 + i] = 0.0f;
-    }
-  }
-  for (int t0 = 0; t0 < T; t0 += kRouterTokBlock) {
-    const int tb = min(kRouterTokBlock, T - t0);
-    __syncthreads();
-    // 8 bf16 per 16-byte load -> two float4 stores (rows are contiguous)
-    const uint4 *xsrc = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t0) * H);
-    float4 *xdst = reinterpret_cast<float4 *>(xs);
-    for (int idx = threadIdx.x; idx < tb * H / 8; idx += blockDim.x) {
-      const uint4 v = ldg_u128(xsrc + idx);
-      xdst[2 * idx] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
-                                  __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
-      xdst[2 * idx + 1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
-                                      __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
-    }
-    __syncthreads();
-    if (wrow == nullptr) continue;
-    for (int tt = 0; tt < tb; ++tt) {
-      float acc = -0.0f;
+        for (int q = 0; q < kRouterRW; ++q) {
+          float a = acc[q][tt];
 #pragma unroll
-      for (int m = 0; m < CH; ++m) {
-        const int cidx = lane + 32 * m;
-        if (cidx < nchunks) {
-          const float4 *xp = reinterpret_cast<const float4 *>(xs + tt * H + cidx * 8);
-          const float4 p0 = xp[0], p1 = xp[1];
-          acc = __fmaf_rn(w[m * 8 + 0], p0.x, acc);
-          acc = __fmaf_rn(w[m * 8 + 1], p0.y, acc);
-          acc = __fmaf_rn(w[m * 8 + 2], p0.z, acc);
-          acc = __fmaf_rn(w[m * 8 + 3], p0.w, acc);
-          acc = __fmaf_rn(w[m * 8 + 4], p1.x, acc);
-          acc = __fmaf_rn(w[m * 8 + 5], p1.y, acc);
-          acc = __fmaf_rn(w[m * 8 + 6], p1.z, acc);
-          acc = __fmaf_rn(w[m * 8 + 7], p1.w, acc);
+          for (int i = 0; i < 8; ++i) a = __fmaf_rn(w[q][m * 8 + i], xv[i], a);
+          acc[q][tt] = a;
         }
       }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, off));
-      if (lane == 0) {
-        if (row < E) logits[static_cast<size_t>(t0 + tt) * E + row] = f32_to_bf16(acc);
-        else shared_logit[t0 + tt] = f32_to_bf16(acc);
-      }
     }
   }
+#pragma unroll
+  for (int q = 0; q < kRouterRW; ++q) {
+#pragma unroll
+    for (int tt = 0; tt < kRouterTok; ++tt) {
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1)
+        acc[q][tt] = __fadd_rn(acc[q][tt], __shfl_xor_sync(0xFFFFFFFFu, acc[q][tt], off));
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < kRouterRW; ++q) {
+    const int row = row0 + q;
+    if (!live[q] || lane >= tb) continue;
+    float v = acc[q][0];
+#pragma unroll
+    for (int tt = 1; tt < kRouterTok; ++tt)
+      if (lane == tt) v = acc[q][tt];
+    if (row < E) logits[static_cast<size_t>(t0 + lane) * E + row] = f32_to_bf16(v);
+    else shared_logit[t0 + lane] = f32_to_bf16(v);
+  }
+}
+
+template <int CH, int RW, int TOK>
+cudaError_t launch_router_cfg(const uint16_t *x, const uint16_t *W, int T, int H, int E,
+                              const uint16_t *w_shared_gate, uint16_t *logits, uint16_t *shared_logit,
+                              cudaStream_t s) {
+  const int rows = E + (w_shared_gate ? 1 : 0);
+  const int rows_per_cta = kRouterWarps * RW;
+  const dim3 grid((rows + rows_per_cta - 1) / rows_per_cta, (T + TOK - 1) / TOK);
+  const size_t smem = static_cast<size_t>(TOK) * H * sizeof(float);
+  auto kernel = k_router_logits<CH, RW, TOK>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  kernel<<<grid, kRouterWarps * 32, smem, s>>>(x, W, T, H, E, w_shared_gate, logits, shared_logit);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, int H, int E,
                                  const uint16_t *w_shared_gate, uint16_t *logits,
                                  uint16_t *shared_logit, cudaStream_t s) {
-  const int rows = E + (w_shared_gate ? 1 : 0);
-  const int blocks = (rows + kRouterWarps - 1) / kRouterWarps;
-  const size_t smem = static_cast<size_t>(kRouterTokBlock) * H * sizeof(float);
-  const int nchunks = H / 8;
-  const int ch = (nchunks + 31) / 32;
-#define FNMOE_ROUTER_CASE(N)                                                                 \
-  if (ch <= N) {                                                                            \
-    if (smem > 48 * 1024) {                                                                 \
-      cudaError_t e = cudaFuncSetAttribute(k_router_logits<N>,                              \
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,     \
-                                           static_cast<int>(smem));                         \
-      if (e != cudaSuccess) return e;                                                       \
-    }                                                                                       \
-    k_router_logits<N><<<blocks, kRouterWarps * 32, smem, s>>>(x, W, T, H, E, w_shared_gate, \
-                                                               logits, shared_logit);       \
-    return cudaGetLastError();                                                              \
-  }
-  FNMOE_ROUTER_CASE(4)
-  FNMOE_ROUTER_CASE(8)
-  FNMOE_ROUTER_CASE(12)
-  FNMOE_ROUTER_CASE(16)
-#undef FNMOE_ROUTER_CASE
+  const int ch = (H / 8 + 31) / 32;
+  if (ch <= 4) return launch_router_cfg<4, 2, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
+  if (ch <= 8) return launch_router_cfg<8, 2, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
+  if (ch <= 12) return launch_router_cfg<12, 2, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
+  if (ch <= 16) return launch_router_cfg<16, 1, 8>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
   return cudaErrorInvalidValue;
 }
 
@@ -1312,8 +1499,9 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
 // softmax (precise) + top-k + renorm, one warp per token
 // ---------------------------------------------------------------------------
 
-constexpr int kMaxPerLane = 32;  // experts <= 1024
+// Logits per lane (experts <= 32 * PER) is a template parameter: 16 at 512 experts.
 
+template <int kMaxPerLane>
 __global__ void __launch_bounds__(128) k_softmax_topk(
     const uint16_t *__restrict__ logits, int T, int E, int k, float blend,
     const uint32_t *__restrict__ route_map, int table_routes, uint32_t *__restrict__ inds,
@@ -1398,10 +1586,20 @@ cudaError_t launch_softmax_topk(const uint16_t *logits, int T, int E, int k, flo
                                 uint32_t *routes, uint16_t *raw_scores, uint16_t *scores,
                                 uint16_t *mass, const uint16_t *shared_logit,
                                 uint16_t *shared_gate, cudaStream_t s) {
-  k_softmax_topk<<<(T + 3) / 4, 128, 0, s>>>(logits, T, E, k, blend, route_map, table_routes,
-                                            inds, routes, raw_scores, scores, mass, shared_logit,
-                                            shared_gate);
-  return cudaGetLastError();
+  const int per = (E + 31) / 32;
+#define FNMOE_TOPK_CASE(P)                                                                           \
+  if (per <= P) {                                                                                   \
+    k_softmax_topk<P><<<(T + 3) / 4, 128, 0, s>>>(logits, T, E, k, blend, route_map, table_routes, \
+                                                  inds, routes, raw_scores, scores, mass,          \
+                                                  shared_logit, shared_gate);                      \
+    return cudaGetLastError();                                                                    \
+  }
+  FNMOE_TOPK_CASE(4)
+  FNMOE_TOPK_CASE(8)
+  FNMOE_TOPK_CASE(16)
+  FNMOE_TOPK_CASE(32)
+#undef FNMOE_TOPK_CASE
+  return cudaErrorInvalidValue;
 }
 
 // ---------------------------------------------------------------------------

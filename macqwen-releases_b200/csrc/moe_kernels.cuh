@@ -33,7 +33,7 @@ struct GroupView {
   int32_t *offsets;    // [n_bins + 1]
   int32_t *order;      // [n_total]   pair ids sorted by bin
   int4 *tiles;         // [3 * max_tiles] {route key, start, len, bin}, {pair ids 0-3}, {pair ids 4-7}
-  int32_t *n_tiles;    // [1]
+  int32_t *n_tiles;    // [4]: tile count (the rest is spare)
   uint32_t *bin_key;   // [n_bins]    route key of each bin
   int n_bins;
   int max_tiles;
