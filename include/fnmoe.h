@@ -48,6 +48,9 @@ extern "C" {
 
 #define FNMOE_ABI_VERSION 2u
 
+/* Size of the library-owned scratch used by fnmoe_moe_execute_static. */
+#define FNMOE_STATIC_SCRATCH_BYTES (16ull << 20)
+
 /* Status codes (negative = failure), mirroring the native bridge's
  * "0 ok / negative specific failure" convention. */
 #define FNMOE_OK 0
@@ -239,6 +242,22 @@ FNMOE_API int fnmoe_moe_workspace_size(const FnMoEArgs *args, uint64_t *bytes);
 /* Executor: replaces flashnext_native_moe_execute (metal_runtime_native.mm:258)
  * and MetalMoEExecutor.execute's packed path (metal_runtime.py:764-932). */
 FNMOE_API int fnmoe_moe_execute(const FnMoEArgs *args, void *stream);
+
+/* fnmoe_moe_execute without a caller workspace and without allocating: the
+ * scratch is a fixed 16 MiB device array inside the library
+ * (FNMOE_STATIC_SCRATCH_BYTES); args->workspace and args->workspace_bytes
+ * are ignored.  For callers that hold only device pointers and no device
+ * allocator (a C or ctypes bridge like the reference's native one, which
+ * keeps process-wide scratch instead of per-call buffers).  No reference
+ * counterpart: the reference's bridge allocates and caches its scratch.
+ * A call whose fnmoe_moe_workspace_size exceeds the static size fails with
+ * FNMOE_ERR_WORKSPACE.  The scratch is shared by every call on a device:
+ * calls that may overlap on the GPU (other streams, other threads) race and
+ * must be serialised by the caller.  Its contents persist between calls;
+ * nothing in it needs to start at zero (each call rewrites what it reads).
+ * The first call on a device resolves the array's address
+ * (cudaGetSymbolAddress); make that first call before any stream capture. */
+FNMOE_API int fnmoe_moe_execute_static(const FnMoEArgs *args, void *stream);
 
 /* Combine-only probe: out[t,h] = sum_s outputs[t,s,h]*scores[t,s] (float32),
  * or outputs[t, routes[t,s], h] when experts > 0 (metal_runtime.py:145-191). */

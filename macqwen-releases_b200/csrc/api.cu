@@ -262,6 +262,35 @@ ExpertCallArgs make_call(const FnMoEArgs *a) {
 
 }  // namespace
 
+// Library-owned scratch of fnmoe_moe_execute_static: file-scope device
+// storage, no runtime allocation.  Its address is looked up once per device.
+static __device__ __align__(256) uint8_t g_static_scratch[FNMOE_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+std::mutex g_static_mu;
+std::map<int, void *> g_static_ptr;  // device -> address of g_static_scratch
+
+int static_scratch(void **ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "static scratch: cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  auto it = g_static_ptr.find(dev);
+  if (it != g_static_ptr.end()) {
+    *ptr = it->second;
+    return FNMOE_OK;
+  }
+  void *p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_static_scratch);
+  if (e != cudaSuccess || p == nullptr) return cuda_fail(e, "static scratch: cudaGetSymbolAddress");
+  g_static_ptr[dev] = p;
+  *ptr = p;
+  return FNMOE_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int fnmoe_available(void) {
@@ -362,6 +391,25 @@ int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
   }
   if (e != cudaSuccess) return cuda_fail(e, "combine");
   return FNMOE_OK;
+}
+
+int fnmoe_moe_execute_static(const FnMoEArgs *a, void *stream) {
+  const int v = validate_moe(a);
+  if (v != FNMOE_OK) return v;
+  const uint64_t need = moe_workspace(a);
+  if (need > FNMOE_STATIC_SCRATCH_BYTES)
+    return fail(FNMOE_ERR_WORKSPACE, "this call needs " + std::to_string(need) +
+                                         " bytes of scratch; the static scratch holds " +
+                                         std::to_string(FNMOE_STATIC_SCRATCH_BYTES) +
+                                         " (use fnmoe_moe_execute with a workspace)");
+  std::string why;
+  if (!device_ok(why)) return fail(FNMOE_ERR_DEVICE, why);
+  void *scratch = nullptr;
+  if (int rc = static_scratch(&scratch)) return rc;
+  FnMoEArgs local = *a;
+  local.workspace = scratch;
+  local.workspace_bytes = FNMOE_STATIC_SCRATCH_BYTES;
+  return fnmoe_moe_execute(&local, stream);
 }
 
 int fnmoe_weighted_combine(const float *outputs, const int32_t *routes, const float *scores,

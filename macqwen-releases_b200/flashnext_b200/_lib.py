@@ -14,6 +14,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libfnmoe.so"
 ABI_VERSION = 2
+STATIC_SCRATCH_BYTES = 16 << 20
 
 OK = 0
 ERR_NULL = -1
@@ -129,6 +130,7 @@ SIGNATURES = {
     "fnmoe_abi_version": ([], _u32),
     "fnmoe_moe_workspace_size": ([ctypes.POINTER(FnMoEArgs), ctypes.POINTER(_u64)], ctypes.c_int),
     "fnmoe_moe_execute": ([ctypes.POINTER(FnMoEArgs), _vp], ctypes.c_int),
+    "fnmoe_moe_execute_static": ([ctypes.POINTER(FnMoEArgs), _vp], ctypes.c_int),
     "fnmoe_weighted_combine": ([_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp], ctypes.c_int),
     "fnmoe_router_topk": ([_vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_float, _vp, _vp, _vp, _vp, _vp],
                           ctypes.c_int),
