@@ -18,8 +18,13 @@ its weights from HBM.
 ``value`` = tokens/s of the whole job with inputs resident in HBM (device
 time, CUDA events, max over ranks).  ``e2e`` = the same through the public
 API with the batch copied from pinned host memory and the output copied back
-inside the timed region.  N > 1 runs one independent replica per GPU
-(weak scaling: 64 tokens per GPU).
+inside the timed region.  N > 1 (torchrun) runs the layer expert-parallel:
+512/N experts per GPU, router and shared expert replicated, each GPU routing
+its own 64 tokens (weak scaling) with NCCL all-to-all dispatch and return of
+the per-slot outputs; device time is the max over ranks.
+
+``--workload c3|c4|c5`` print one line each for the other benchmark configs
+(48-layer stack, 5k-token prefill, paged attention).
 
 ``--impl reference`` times the reference-semantics CPU implementation (the
 NumPy oracle port; MLX, the reference's own runtime, is not installable
@@ -428,6 +433,121 @@ def gpu_arm(args):
     return 0
 
 
+def ep_arm(args):
+    """N > 1: the C2 layer expert-parallel over N GPUs (experts 512/N per rank,
+    router and shared expert replicated, 64 tokens routed by each rank, NCCL
+    all-to-all dispatch and return of the per-slot outputs)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    from flashnext_b200 import _lib, synthetic
+    from flashnext_b200.expert_parallel import CudaBackend, ExpertParallelMoE
+
+    _lib.ensure_device()
+    tokens = 64
+    layers = max(1, args.layers)
+    per = EXPERTS // world
+    eps, xs = [], []
+    for i in range(layers):
+        L = synthetic.moe_layer(tokens * world, HIDDEN, INTER, EXPERTS, TOP_K, GROUP, zipf=1.1, seed=17 + 101 * i)
+        local_bank = {n: tuple(t[rank * per:(rank + 1) * per].contiguous() for t in v) for n, v in L.experts.items()}
+        backend = CudaBackend(L.router_weight, local_bank, L.shared, L.shared_expert_gate, top_k=TOP_K)
+        eps.append(ExpertParallelMoE(backend, expert_count=EXPERTS, hidden_size=HIDDEN, top_k=TOP_K))
+        xs.append(L.x[tokens * rank:tokens * (rank + 1)].contiguous())
+        del L, local_bank
+    torch.cuda.synchronize()
+
+    def step(i):
+        j = i % layers
+        return eps[j](xs[j])
+
+    warm = max(3, args.warmup, layers)
+    for i in range(warm):
+        step(i)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    _barrier(world)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(CUSHION_CYCLES)
+    start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    ms = _max_over_ranks(start.elapsed_time(end), world)
+    clocks = sampler.stop()
+    value = tokens * args.steps * world / (ms / 1000.0)
+
+    host_x = [x.cpu().pin_memory() for x in xs]
+    host_out = [torch.empty((tokens, HIDDEN), dtype=torch.bfloat16).pin_memory() for _ in range(layers)]
+    dev_x = [torch.empty_like(x) for x in xs]
+
+    def e2e_step(i):
+        j = i % layers
+        dev_x[j].copy_(host_x[j], non_blocking=True)
+        host_out[j].copy_(eps[j](dev_x[j]), non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_value = tokens * args.steps * world / (e2e_ms / 1000.0)
+
+    _lib.profile_enable(True)
+    _lib.profile_read(reset=True)
+    for i in range(args.steps):
+        step(i)
+    torch.cuda.synchronize()
+    prof = _lib.profile_read(reset=True)
+    _lib.profile_enable(False)
+    _barrier(world)
+    launches_per_step = sum(c for c, _ in prof.values()) / max(1, args.steps)
+    hbm_peak, peak_kind = _peaks()
+    gu_count, gu_ms = prof.get("gate_up", (0, 0.0))
+    gu_avg_s = (gu_ms / max(1, gu_count)) / 1000.0
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": warm, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C2 layer, expert-parallel: 64 Zipf(1.1)-routed tokens per GPU, "
+                                   f"512 experts sharded {per}/GPU, router + shared expert replicated",
+                       "tokens_per_gpu": tokens, "layers_rotated": layers,
+                       "l2": f"inputs larger than L2: {layers} distinct layers rotated per step",
+                       "parallelism": f"ep{world}"},
+            "roofline": {"bound": "hbm", "kernel": "gate_up", "avg_launch_us": gu_avg_s * 1e6,
+                         "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s", "achieved": None,
+                         "frac": None, "traffic": None,
+                         "note": "per-rank expert kernels; see the single-GPU line for the roofline"},
+            "kernels": {k: {"launches": c, "avg_us": 1000.0 * t / max(1, c)} for k, (c, t) in prof.items()},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": tokens * HIDDEN * 2,
+                    "d2h_bytes_per_step": tokens * HIDDEN * 2},
+            "gpu_launches": int(round(launches_per_step * args.steps)),
+            "clocks": clocks, "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def batch1_numbers(hbm_peak):
     """Batch-1 (config 1) tokens/s over 8 distinct layers via one CUDA graph."""
     import torch
@@ -464,19 +584,189 @@ def batch1_numbers(hbm_peak):
             "note": "8 distinct layers in one CUDA graph, 20 replays"}
 
 
+# --------------------------------------------------------------------------
+# Other benchmark configs (one JSON line each; the default line is C2)
+# --------------------------------------------------------------------------
+
+
+def _timed(fn, steps, cushion=True):
+    """Device time (ms) of `steps` calls of fn(i), events on the current stream."""
+    import torch
+
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if cushion:
+        torch.cuda._sleep(CUSHION_CYCLES)
+    a.record()
+    for i in range(steps):
+        fn(i)
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b)
+
+
+def _graph(fn):
+    """Capture fn() into a CUDA graph (after one eager call)."""
+    import torch
+
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    return g
+
+
+def c5_arm(args):
+    """Config 5: paged-KV decode attention, GQA 16/2, D 256, page 64, 16 sequences
+    with context ~ U[1k, 32k]; two KV pools (each > L2) alternate per step."""
+    import torch
+
+    from flashnext_b200 import _lib, synthetic
+    from flashnext_b200.paged_attention import paged_decode
+
+    _lib.ensure_device()
+    hbm_peak, peak_kind = _peaks()
+    sets = [synthetic.paged_decode_inputs(16, 16, 2, 256, 64, (1024, 32768), seed=500 + i) for i in range(2)]
+    outs = [torch.empty_like(P.q) for P in sets]
+
+    def step(i):
+        P = sets[i % 2]
+        paged_decode(P.q, P.k_cache, P.v_cache, P.block_table, P.context_lens, P.scale, out=outs[i % 2])
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    ms = _timed(step, args.steps) / args.steps
+    ctx = [int(P.context_lens.sum()) for P in sets]
+    kv_bytes = sum(ctx) / 2 * 2048  # K and V, 2 KV heads x 256 x 2 B per context token (mean of the two sets)
+    io = 2 * 16 * 16 * 256 * 2
+    gbs = (kv_bytes + io) / (ms / 1000.0) / 1e9
+    print(json.dumps({
+        "metric": "paged-KV decode attention GB/s (C5)", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "C5: 16 sequences, GQA 16/2, head_dim 256, page 64, ctx U[1k,32k]",
+                   "context_tokens": ctx, "l2": "two KV pools of ~0.5 GB alternate"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": gbs / hbm_peak},
+    }), flush=True)
+    return 0
+
+
+def c3_arm(args):
+    """Config 3: 48-layer stack, hidden 3072, 512 experts of intermediate 640 +
+    shared, top-10, Q4/G32; batch-1 and batch-64 decode through all 48 layers
+    (CUDA graph replays).  Each layer is generated, tiled and its arrays freed
+    before the next, so ~97 GB of tiled experts stay resident."""
+    import torch
+
+    from flashnext_b200 import _lib, synthetic
+    from flashnext_b200.moe_block import SparseMoEBlock
+
+    _lib.ensure_device()
+    hbm_peak, peak_kind = _peaks()
+    H, I, E, K, n_layers = 3072, 640, 512, 10, 48
+    blocks, routers = [], []
+    for l in range(n_layers):
+        L = synthetic.moe_layer(64, H, I, E, K, 32, zipf=1.1, seed=7000 + 31 * l)
+        blocks.append(SparseMoEBlock(L.router_weight, L.experts, top_k=K, shared=L.shared,
+                                     shared_expert_gate=L.shared_expert_gate))
+        routers.append(L.x)
+        del L
+        torch.cuda.synchronize()
+    expert_bytes = 3 * (I * H // 2 + 2 * I * (H // 32) * 2)
+    results = {}
+    for tokens in (1, 64):
+        xs = [routers[l][:tokens].contiguous() for l in range(n_layers)]
+        outs = [torch.empty((tokens, H), dtype=torch.bfloat16, device="cuda") for _ in range(n_layers)]
+
+        def stack():
+            for l in range(n_layers):
+                blocks[l](xs[l], out=outs[l])
+
+        g = _graph(stack)
+        for _ in range(3):
+            g.replay()
+        ms = _timed(lambda i: g.replay(), args.steps) / args.steps
+        used = [int(torch.unique(b.last_inds).numel()) for b in blocks]
+        step_bytes = sum((u + 1) * expert_bytes for u in used) + n_layers * (E * H * 2 + H * 2)
+        gbs = step_bytes / (ms / 1000.0) / 1e9
+        results[f"batch{tokens}"] = {"tokens_per_s": tokens / (ms / 1000.0), "ms_per_token_step": ms,
+                                     "hbm_gbs": gbs, "roofline_frac": gbs / hbm_peak,
+                                     "distinct_experts_per_layer": sum(used) / len(used)}
+        del g
+    print(json.dumps({
+        "metric": "48-layer MoE decode tokens/s (C3)", "value": results["batch64"]["tokens_per_s"],
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": 3, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "C3: 48 layers, H3072/I640/E512 top-10 Q4/G32 + shared, Zipf(1.1) routing; "
+                               "value = batch-64 tokens/s, batch1 below",
+                   "resident_tiled_gb": sum(b.tiled.gate_up.numel() + b.tiled.down.numel() for b in blocks) / 1e9},
+        "results": results, "peak": hbm_peak, "peak_kind": peak_kind,
+    }), flush=True)
+    return 0
+
+
+def c4_arm(args):
+    """Config 4: 5,000-token prefill chunk through one H2048/I512/E512 top-10
+    Q4/G32 layer (+ shared), uniform routing; reports TFLOP/s of the grouped
+    expert GEMMs (routed 2*50,000*3*2048*512 + shared) over the layer time."""
+    import torch
+
+    from flashnext_b200 import _lib, synthetic
+    from flashnext_b200.moe_block import SparseMoEBlock
+
+    _lib.ensure_device()
+    tokens = 5000
+    L = synthetic.moe_layer(tokens, HIDDEN, INTER, EXPERTS, TOP_K, GROUP, zipf=None, seed=4242)
+    block = SparseMoEBlock(L.router_weight, L.experts, top_k=TOP_K, shared=L.shared,
+                           shared_expert_gate=L.shared_expert_gate)
+    out = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device="cuda")
+    for _ in range(max(2, args.warmup)):
+        block(L.x, out=out)
+    steps = max(1, min(args.steps, 10))
+    ms = _timed(lambda i: block(L.x, out=out), steps) / steps
+    flops = 2.0 * tokens * (TOP_K + 1) * 3 * HIDDEN * INTER + 2.0 * tokens * (EXPERTS + 1) * HIDDEN
+    tflops = flops / (ms / 1000.0) / 1e12
+    d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(d.get("bf16_tflops", 1590.0))
+    print(json.dumps({
+        "metric": "prefill MoE layer TFLOP/s (C4)", "value": tflops, "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": steps, "warmup": max(2, args.warmup), "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "C4: 5,000 tokens, H2048/I512/E512 top-10 Q4/G32 + shared, uniform routing",
+                   "kernel": "grouped fixed-point MMA expert kernels (decode path)"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak},
+    }), flush=True)
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c1"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c1", "c3", "c4", "c5"], default="c2",
+                    help="c2 (default) is the headline line; c3/c4/c5 print their own lines")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS, help="distinct layers rotated per step")
     ap.add_argument("--no-batch1", action="store_true", help="skip the batch-1 CUDA-graph sub-measure")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return reference_arm(args)
+    if args.workload == "c5":
+        return c5_arm(args)
+    if args.workload == "c3":
+        return c3_arm(args)
+    if args.workload == "c4":
+        return c4_arm(args)
+    if _dist()[0] > 1:
+        return ep_arm(args)
     return gpu_arm(args)
 
 

@@ -46,7 +46,7 @@ extern "C" {
 #define FNMOE_API
 #endif
 
-#define FNMOE_ABI_VERSION 2u
+#define FNMOE_ABI_VERSION 3u
 
 /* Size of the library-owned scratch used by fnmoe_moe_execute_static. */
 #define FNMOE_STATIC_SCRATCH_BYTES (16ull << 20)
@@ -97,6 +97,21 @@ typedef struct FnExpertTable {
 
 /* One MoE executor call: gate -> up -> SwiGLU -> down -> combine.
  * The first 19 fields follow FlashNextMoEArgs' order. */
+/* Tiled expert tables: the routed experts' projections (and optionally the
+ * shared expert's, as the last record) repacked once by fnmoe_tile_experts
+ * into one 2560-byte chunk per (row group, 128-byte block) in MMA fragment
+ * order, scales and biases included.  Record r of gate_up holds expert r's
+ * gate and up rows (inter/8 groups of 8 + 8 rows), record r of down its down
+ * rows (hidden/16 groups of 16).  Sizes: fnmoe_tiled_record_bytes. */
+typedef struct FnTiledExperts {
+  const void *gate_up;         /* [records][gate_up_record_bytes], 16-byte aligned, or NULL */
+  const void *down;            /* [records][down_record_bytes], 16-byte aligned */
+  uint64_t gate_up_record_bytes;
+  uint64_t down_record_bytes;
+  uint32_t records;            /* expert_count, +1 when the shared expert is the last record */
+  uint32_t has_shared;         /* 1: the last record is the shared expert */
+} FnTiledExperts;
+
 typedef struct FnMoEArgs {
   uint32_t abi_version;        /* FNMOE_ABI_VERSION */
   uint32_t flags;              /* FNMOE_FLAG_* */
@@ -136,22 +151,12 @@ typedef struct FnMoEArgs {
   void *down_out;              /* RETURN_ALL / NO_COMBINE: [tokens, slots, hidden] bf16 */
   void *workspace;
   uint64_t workspace_bytes;
+  /* When tiled.gate_up != NULL, routes without bit 31 address records of these
+   * tiled tables (fnmoe_tile_experts) instead of the *_weight arrays. */
+  FnTiledExperts tiled;
 } FnMoEArgs;
 
-/* Tiled expert tables: the routed experts' projections (and optionally the
- * shared expert's, as the last record) repacked once by fnmoe_tile_experts
- * into one 2560-byte chunk per (row group, 128-byte block) in MMA fragment
- * order, scales and biases included.  Record r of gate_up holds expert r's
- * gate and up rows (inter/8 groups of 8 + 8 rows), record r of down its down
- * rows (hidden/16 groups of 16).  Sizes: fnmoe_tiled_record_bytes. */
-typedef struct FnTiledExperts {
-  const void *gate_up;         /* [records][gate_up_record_bytes], 16-byte aligned, or NULL */
-  const void *down;            /* [records][down_record_bytes], 16-byte aligned */
-  uint64_t gate_up_record_bytes;
-  uint64_t down_record_bytes;
-  uint32_t records;            /* expert_count, +1 when the shared expert is the last record */
-  uint32_t has_shared;         /* 1: the last record is the shared expert */
-} FnTiledExperts;
+
 
 /* A whole sparse-MoE block: router -> top-k -> renorm -> routed experts +
  * sigmoid-gated shared expert -> combine. */
@@ -273,6 +278,33 @@ FNMOE_API int fnmoe_router_topk(const void *x, const void *router_weight, uint32
                       uint32_t hidden, uint32_t experts, uint32_t top_k,
                       float renorm_blend, uint32_t *inds, void *scores,
                       void *mass, void *logits, void *stream);
+
+/* fnmoe_router_topk plus the shared expert's sigmoid gate (adaptive_topk.py:
+ * 263-264): shared_gate_weight [hidden] bf16 is run as one more router row;
+ * shared_logit [tokens] bf16 receives x.w_g, shared_gate [tokens] bf16
+ * sigmoid of it (bfloat16 op sequence).  Used by the expert-parallel layer,
+ * which computes the gate on the token's own rank. */
+FNMOE_API int fnmoe_router_topk_shared(const void *x, const void *router_weight,
+                                       const void *shared_gate_weight, uint32_t tokens,
+                                       uint32_t hidden, uint32_t experts, uint32_t top_k,
+                                       float renorm_blend, uint32_t *inds, void *scores,
+                                       void *mass, void *logits, void *shared_logit,
+                                       void *shared_gate, void *stream);
+
+/* Slot-ordered combine of per-slot expert outputs (metal_runtime.py:301-333):
+ * out[t] = bf16(sum_s float(slot_outputs[t,s]) * score[t,s]) in slot order
+ * (float32, no fused multiply-add; slots whose route is >= expert_count are
+ * skipped), then + shared_y, or + bf16(shared * shared_gate) when shared and
+ * shared_gate are given (one of the two or neither).  slot_outputs
+ * [tokens, slots, hidden] bf16, routes [tokens, slots], scores
+ * [tokens, slots] (scores_dtype), shared_y/shared [tokens, hidden] bf16,
+ * shared_gate [tokens] bf16, out [tokens, hidden] bf16.  The combine stage of
+ * fnmoe_moe_execute on its own, for callers whose slot outputs come from
+ * elsewhere (the expert-parallel layer). */
+FNMOE_API int fnmoe_combine(const void *slot_outputs, const uint32_t *routes, const void *scores,
+                            uint32_t scores_dtype, uint32_t tokens, uint32_t slots, uint32_t hidden,
+                            uint32_t expert_count, const void *shared_y, const void *shared,
+                            const void *shared_gate, void *out, void *stream);
 
 /* Softmax (precise) -> top-k -> renorm on given bf16 logits [tokens, experts]
  * (compiled.router + compiled.renorm, compiled.py:61-71,96-112).  raw_scores

@@ -136,7 +136,7 @@ constexpr int kMaxBins = 16384;
 // Range of route values without bit 31: stream-pack records or array experts.
 uint32_t non_slot_keys(const FnMoEArgs *a) {
   if (a->stream_table.base != nullptr) return a->stream_table.records;
-  return a->gate_weight != nullptr ? a->expert_count : 0u;
+  return (a->gate_weight != nullptr || a->tiled.gate_up != nullptr) ? a->expert_count : 0u;
 }
 constexpr uint32_t kMaxTopK = 16;
 
@@ -157,9 +157,21 @@ int validate_moe(const FnMoEArgs *a) {
   const bool has_table = a->table.base != nullptr;
   const bool has_stream = a->stream_table.base != nullptr;
   if (has_stream && !has_table) return fail(FNMOE_ERR_VALUE, "stream pack requires a resident slab pack");
-  if (!has_table && (a->gate_weight == nullptr || a->up_weight == nullptr || a->down_weight == nullptr))
+  const bool has_tiled = a->tiled.gate_up != nullptr;
+  if (has_tiled) {
+    if (has_table) return fail(FNMOE_ERR_VALUE, "provide a slab pack or tiled tables, not both");
+    if (a->tiled.down == nullptr) return fail(FNMOE_ERR_NULL, "tiled tables need both gate_up and down");
+    if (a->inter_size % 8 || a->hidden_size % 16)
+      return fail(FNMOE_ERR_SHAPE, "tiled tables need inter_size % 8 == 0 and hidden_size % 16 == 0");
+    if (a->tiled.gate_up_record_bytes != tiled_record_bytes(a->inter_size, a->hidden_size, true) ||
+        a->tiled.down_record_bytes != tiled_record_bytes(a->hidden_size, a->inter_size, false))
+      return fail(FNMOE_ERR_SHAPE, "tiled record sizes do not match hidden/inter sizes");
+    if (a->tiled.has_shared) return fail(FNMOE_ERR_VALUE, "executor tiled tables hold routed experts only");
+    if (a->tiled.records != a->expert_count) return fail(FNMOE_ERR_SHAPE, "tiled records must equal expert_count");
+  } else if (!has_table && (a->gate_weight == nullptr || a->up_weight == nullptr || a->down_weight == nullptr)) {
     return fail(FNMOE_ERR_NULL, "packed execution needs gate, up, and down projections");
-  if (a->gate_weight && (!a->gate_scales || !a->gate_biases || !a->up_scales || !a->up_biases ||
+  }
+  if (!has_tiled && a->gate_weight && (!a->gate_scales || !a->gate_biases || !a->up_scales || !a->up_biases ||
                          !a->down_scales || !a->down_biases))
     return fail(FNMOE_ERR_NULL, "Q4 projections need scales and biases");
   if ((a->shared == nullptr) != (a->shared_gate == nullptr))
@@ -226,6 +238,7 @@ int check_expert_alignment(ExpertCallArgs &c) {
       sb16 = sb16 && ((b + t->off[3 * part + 1]) % 16) == 0 && ((b + t->off[3 * part + 2]) % 16) == 0;
     }
   }
+  if (c.tiled.gate_up != nullptr) w_ok = w_ok && aligned(c.tiled.gate_up, 16) && aligned(c.tiled.down, 16);
   if (!w_ok) return fail(FNMOE_ERR_VALUE, "packed expert weights must start on 16-byte boundaries");
   c.sb_async = sb_ok ? 1 : 0;
   c.sb_bulk = (sb_ok && sb16) ? 1 : 0;
@@ -249,7 +262,16 @@ ExpertCallArgs make_call(const FnMoEArgs *a) {
   for (int i = 0; i < 9; ++i) c.stream.off[i] = a->stream_table.part_offset[i];
   c.stream.records = a->stream_table.base ? a->stream_table.records : 0;
   c.array_experts = a->stream_table.base ? static_cast<int>(a->stream_table.records)
-                    : (a->gate_weight ? static_cast<int>(a->expert_count) : 0);
+                    : ((a->gate_weight || a->tiled.gate_up) ? static_cast<int>(a->expert_count) : 0);
+  if (a->tiled.gate_up != nullptr) {
+    c.gate = c.up = c.down = {nullptr, nullptr, nullptr};
+    c.tiled.gate_up = static_cast<const uint8_t *>(a->tiled.gate_up);
+    c.tiled.down = static_cast<const uint8_t *>(a->tiled.down);
+    c.tiled.gate_up_record = a->tiled.gate_up_record_bytes;
+    c.tiled.down_record = a->tiled.down_record_bytes;
+    c.tiled.records = a->tiled.records;
+    c.tiled.has_shared = 0;
+  }
   c.tokens = static_cast<int>(a->tokens);
   c.slots = static_cast<int>(a->slots);
   c.n_pairs = c.tokens * c.slots;
@@ -443,6 +465,51 @@ int fnmoe_router_topk(const void *x, const void *router_weight, uint32_t tokens,
                           nullptr, 0, inds, inds, nullptr, static_cast<uint16_t *>(scores),
                           static_cast<uint16_t *>(mass), nullptr, nullptr, s);
   return e == cudaSuccess ? FNMOE_OK : cuda_fail(e, "softmax_topk");
+}
+
+int fnmoe_router_topk_shared(const void *x, const void *router_weight, const void *shared_gate_weight,
+                             uint32_t tokens, uint32_t hidden, uint32_t experts, uint32_t top_k,
+                             float renorm_blend, uint32_t *inds, void *scores, void *mass, void *logits,
+                             void *shared_logit, void *shared_gate, void *stream) {
+  if (!x || !router_weight || !shared_gate_weight || !inds || !scores || !logits || !shared_logit || !shared_gate)
+    return fail(FNMOE_ERR_NULL,
+                "x, router_weight, shared_gate_weight, inds, scores, logits, shared_logit and shared_gate are required");
+  if (tokens == 0 || hidden == 0 || hidden % 8) return fail(FNMOE_ERR_SHAPE, "hidden must be a positive multiple of 8");
+  if (hidden > 4096) return fail(FNMOE_ERR_SHAPE, "hidden must be <= 4096");
+  if (experts == 0 || experts > 1024) return fail(FNMOE_ERR_SHAPE, "experts must be in 1..1024");
+  if (top_k == 0 || top_k > kMaxTopK || top_k > experts) return fail(FNMOE_ERR_VALUE, "top_k out of range");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = ensure_exp_table(s);
+  if (e != cudaSuccess) return cuda_fail(e, "exp table");
+  e = launch_router_logits(static_cast<const uint16_t *>(x), static_cast<const uint16_t *>(router_weight), tokens,
+                           hidden, experts, static_cast<const uint16_t *>(shared_gate_weight),
+                           static_cast<uint16_t *>(logits), static_cast<uint16_t *>(shared_logit), s);
+  if (e != cudaSuccess) return cuda_fail(e, "router logits");
+  e = launch_softmax_topk(static_cast<const uint16_t *>(logits), tokens, experts, top_k, renorm_blend, nullptr, 0,
+                          inds, inds, nullptr, static_cast<uint16_t *>(scores), static_cast<uint16_t *>(mass),
+                          static_cast<const uint16_t *>(shared_logit), static_cast<uint16_t *>(shared_gate), s);
+  return e == cudaSuccess ? FNMOE_OK : cuda_fail(e, "softmax_topk");
+}
+
+int fnmoe_combine(const void *slot_outputs, const uint32_t *routes, const void *scores, uint32_t scores_dtype,
+                  uint32_t tokens, uint32_t slots, uint32_t hidden, uint32_t expert_count, const void *shared_y,
+                  const void *shared, const void *shared_gate, void *out, void *stream) {
+  if (!slot_outputs || !routes || !scores || !out)
+    return fail(FNMOE_ERR_NULL, "slot_outputs, routes, scores and out are required");
+  if (tokens == 0 || slots == 0 || hidden == 0) return fail(FNMOE_ERR_SHAPE, "tokens, slots and hidden must be positive");
+  if (scores_dtype != FNMOE_DTYPE_F32 && scores_dtype != FNMOE_DTYPE_BF16)
+    return fail(FNMOE_ERR_UNSUPPORTED, "scores must be float32 or bfloat16");
+  if ((shared == nullptr) != (shared_gate == nullptr))
+    return fail(FNMOE_ERR_VALUE, "shared and shared_gate must be provided together");
+  if (shared_y != nullptr && shared != nullptr) return fail(FNMOE_ERR_VALUE, "provide shared_y or shared parts, not both");
+  const int mode = shared_y ? kCombineSharedY : (shared ? kCombineParts : kCombineNone);
+  cudaError_t e = launch_combine(static_cast<const uint16_t *>(slot_outputs), routes, scores,
+                                 scores_dtype == FNMOE_DTYPE_F32, static_cast<int>(tokens), static_cast<int>(slots),
+                                 static_cast<int>(hidden), mode, static_cast<const uint16_t *>(shared_y),
+                                 static_cast<const uint16_t *>(shared), static_cast<const uint16_t *>(shared_gate),
+                                 static_cast<int>(expert_count), 0, static_cast<uint16_t *>(out),
+                                 static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FNMOE_OK : cuda_fail(e, "combine");
 }
 
 int fnmoe_softmax_topk(const void *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,

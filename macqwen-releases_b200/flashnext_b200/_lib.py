@@ -13,7 +13,7 @@ import threading
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libfnmoe.so"
-ABI_VERSION = 2
+ABI_VERSION = 3
 STATIC_SCRATCH_BYTES = 16 << 20
 
 OK = 0
@@ -51,6 +51,14 @@ class FnExpertTable(ctypes.Structure):
     ]
 
 
+class FnTiledExperts(ctypes.Structure):
+    _fields_ = [
+        ("gate_up", _vp), ("down", _vp),
+        ("gate_up_record_bytes", _u64), ("down_record_bytes", _u64),
+        ("records", _u32), ("has_shared", _u32),
+    ]
+
+
 class FnMoEArgs(ctypes.Structure):
     _fields_ = [
         ("abi_version", _u32), ("flags", _u32),
@@ -68,14 +76,7 @@ class FnMoEArgs(ctypes.Structure):
         ("stream_table", FnExpertTable),
         ("gate_out", _vp), ("up_out", _vp), ("down_out", _vp),
         ("workspace", _vp), ("workspace_bytes", _u64),
-    ]
-
-
-class FnTiledExperts(ctypes.Structure):
-    _fields_ = [
-        ("gate_up", _vp), ("down", _vp),
-        ("gate_up_record_bytes", _u64), ("down_record_bytes", _u64),
-        ("records", _u32), ("has_shared", _u32),
+        ("tiled", FnTiledExperts),
     ]
 
 
@@ -134,6 +135,9 @@ SIGNATURES = {
     "fnmoe_weighted_combine": ([_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp], ctypes.c_int),
     "fnmoe_router_topk": ([_vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_float, _vp, _vp, _vp, _vp, _vp],
                           ctypes.c_int),
+    "fnmoe_router_topk_shared": ([_vp, _vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_float, _vp, _vp, _vp, _vp, _vp,
+                                  _vp, _vp], ctypes.c_int),
+    "fnmoe_combine": ([_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "fnmoe_softmax_topk": ([_vp, _u32, _u32, _u32, ctypes.c_float, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "fnmoe_group_tokens": ([_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _u64, _vp], ctypes.c_int),
     "fnmoe_moe_layer_workspace_size": ([ctypes.POINTER(FnMoELayerArgs), ctypes.POINTER(_u64)], ctypes.c_int),

@@ -1,0 +1,190 @@
+"""Expert-parallel sparse-MoE layer over torch.distributed (one process per GPU).
+
+Rank r of W owns routed experts [r*E/W, (r+1)*E/W) (tiled tables on the GPU);
+the router and the shared expert are replicated, and each rank routes its own
+tokens (data parallel over tokens).  One layer step:
+
+1. route locally: logits -> softmax -> top-k -> renorm, plus the shared
+   expert's sigmoid gate (``fnmoe_router_topk_shared``; the reference computes
+   the same on one device, ``models/flashnext/adaptive_topk.py:53-64,263-264``);
+2. dispatch: the (token, slot) pairs are ordered by owner rank (stable in pair
+   order); pair counts are exchanged, then each pair's input row and the
+   owner-local expert id go to the owner (``all_to_all_single``);
+3. the owner runs its experts on the received rows, one slot per row
+   (``fnmoe_moe_execute`` with per-slot outputs);
+4. the bfloat16 outputs come back along the reverse all-to-all and land in
+   their (token, slot) places;
+5. the token's rank computes the shared expert and the slot-ordered combine
+   (``fnmoe_combine``, ``metal_runtime.py:301-333``).
+
+Every kernel gives a row's result independently of the rest of its batch, so
+the output is bit-identical to the single-device layer (``fnmoe_moe_layer``).
+The counts exchange is read on the host to size the payload all-to-all;
+rows travel as int32 words (pairs of bfloat16), which every backend carries.
+
+The compute steps go through a backend object: ``CudaBackend`` (the product)
+or, for multi-process tests of the dispatch/combine logic on CPU ranks, any
+object with the same four methods.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Mapping
+
+from . import _lib
+from .cuda_runtime import _bf16, _dev, _stream, _Workspace
+from .tiled import TiledExperts
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _triple(p):
+    if isinstance(p, Mapping):
+        return p["weight"], p["scales"], p["biases"]
+    return tuple(p)
+
+
+class CudaBackend:
+    """The sm_100a kernels behind the four compute steps."""
+
+    def __init__(self, router_weight, local_experts: Mapping, shared: Mapping, shared_expert_gate,
+                 *, top_k: int, group_size: int = 32, renorm_blend: float = 1.0):
+        self.router_weight = _bf16(router_weight, "router_weight")
+        self.expert_count, self.hidden_size = (int(v) for v in self.router_weight.shape)
+        self.top_k = int(top_k)
+        self.group_size = int(group_size)
+        self.renorm_blend = float(renorm_blend)
+        self.local = TiledExperts(local_experts, None, group_size=group_size)
+        self.local_count = self.local.expert_count
+        self.inter_size = self.local.inter_size
+        self.shared = {}
+        for name in ("gate_proj", "up_proj", "down_proj"):
+            w, s, b = _triple(shared[name])
+            self.shared[name] = (_dev(w).unsqueeze(0).contiguous(), _bf16(s, "shared scales").unsqueeze(0).contiguous(),
+                                 _bf16(b, "shared biases").unsqueeze(0).contiguous())
+        self.shared_gate_weight = _bf16(shared_expert_gate, "shared_expert_gate").reshape(-1)
+        self._ws = _Workspace()
+        self._ws2 = _Workspace()
+
+    def route(self, x):
+        torch = _torch()
+        lib = _lib.ensure_device()
+        T = x.shape[0]
+        inds = torch.empty((T, self.top_k), dtype=torch.int32, device="cuda")
+        scores = torch.empty((T, self.top_k), dtype=torch.bfloat16, device="cuda")
+        mass = torch.empty((T,), dtype=torch.bfloat16, device="cuda")
+        logits = torch.empty((T, self.expert_count), dtype=torch.bfloat16, device="cuda")
+        sl = torch.empty((T,), dtype=torch.bfloat16, device="cuda")
+        sg = torch.empty((T,), dtype=torch.bfloat16, device="cuda")
+        _lib.check(lib.fnmoe_router_topk_shared(
+            x.data_ptr(), self.router_weight.data_ptr(), self.shared_gate_weight.data_ptr(), T, self.hidden_size,
+            self.expert_count, self.top_k, self.renorm_blend, inds.data_ptr(), scores.data_ptr(), mass.data_ptr(),
+            logits.data_ptr(), sl.data_ptr(), sg.data_ptr(), _stream()), "router_topk_shared")
+        return inds, scores, sg
+
+    def _execute(self, x, routes, tiled, weights, expert_count, ws):
+        """Per-slot outputs [rows, H] of routes [rows, 1] (one slot per row)."""
+        torch = _torch()
+        lib = _lib.ensure_device()
+        rows = x.shape[0]
+        out = torch.empty((rows, self.hidden_size), dtype=torch.bfloat16, device="cuda")
+        if rows == 0:
+            return out
+        a = _lib.FnMoEArgs()
+        a.abi_version = _lib.ABI_VERSION
+        a.flags = _lib.FLAG_NO_COMBINE
+        a.x = x.data_ptr()
+        if tiled is not None:
+            a.tiled = tiled.abi()
+        else:
+            for name, key in (("gate_proj", "gate"), ("up_proj", "up"), ("down_proj", "down")):
+                w, s, b = weights[name]
+                setattr(a, f"{key}_weight", w.data_ptr())
+                setattr(a, f"{key}_scales", s.data_ptr())
+                setattr(a, f"{key}_biases", b.data_ptr())
+        a.routes = routes.data_ptr()
+        a.tokens, a.slots = rows, 1
+        a.hidden_size, a.inter_size, a.expert_count = self.hidden_size, self.inter_size, expert_count
+        a.group_size = self.group_size
+        a.x_dtype = _lib.DTYPE_BF16
+        a.down_out = out.data_ptr()
+        need = ctypes.c_uint64(0)
+        _lib.check(lib.fnmoe_moe_workspace_size(ctypes.byref(a), ctypes.byref(need)), "workspace_size")
+        w = ws.get(need.value)
+        a.workspace, a.workspace_bytes = w.data_ptr(), w.numel()
+        _lib.check(lib.fnmoe_moe_execute(ctypes.byref(a), _stream()), "moe_execute")
+        return out
+
+    def experts(self, rows, local_ids):
+        return self._execute(rows, local_ids.reshape(-1, 1).contiguous(), self.local, None, self.local_count, self._ws)
+
+    def shared_expert(self, x):
+        torch = _torch()
+        zeros = torch.zeros((x.shape[0], 1), dtype=torch.int32, device="cuda")
+        return self._execute(x, zeros, None, self.shared, 1, self._ws2)
+
+    def combine(self, d, inds, scores, shared, shared_gate):
+        torch = _torch()
+        lib = _lib.ensure_device()
+        T, S, H = d.shape
+        out = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
+        _lib.check(lib.fnmoe_combine(d.data_ptr(), inds.data_ptr(), scores.data_ptr(), _lib.DTYPE_BF16, T, S, H,
+                                     self.expert_count, None, shared.data_ptr(), shared_gate.data_ptr(),
+                                     out.data_ptr(), _stream()), "combine")
+        return out
+
+
+class ExpertParallelMoE:
+    """One sparse-MoE layer with experts sharded over the ranks of `group`."""
+
+    def __init__(self, backend, *, expert_count: int, hidden_size: int, top_k: int, group=None):
+        import torch.distributed as dist
+
+        self.backend = backend
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if expert_count % self.world:
+            raise ValueError("expert_count must be divisible by the number of ranks")
+        self.expert_count = expert_count
+        self.per_rank = expert_count // self.world
+        self.hidden_size = hidden_size
+        self.top_k = top_k
+
+    def _a2a(self, out, inp, out_splits, in_splits):
+        import torch.distributed as dist
+
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+        return out
+
+    def __call__(self, x):
+        torch = _torch()
+        T, H = x.shape
+        k = self.top_k
+        dev = x.device
+        inds, scores, sg = self.backend.route(x)
+        flat = inds.reshape(-1).to(torch.int64)
+        owner = torch.div(flat, self.per_rank, rounding_mode="floor")
+        order = torch.sort(owner, stable=True).indices  # pairs grouped by owner, pair order kept
+        send_counts = torch.bincount(owner, minlength=self.world).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        self._a2a(recv_counts, send_counts, [1] * self.world, [1] * self.world)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        n_recv = int(sum(rc))
+        send_rows = x[torch.div(order, k, rounding_mode="floor")].contiguous()
+        send_ids = (flat[order] - owner[order] * self.per_rank).to(torch.int32).contiguous()
+        recv_rows = torch.empty((n_recv, H), dtype=x.dtype, device=dev)
+        recv_ids = torch.empty((n_recv,), dtype=torch.int32, device=dev)
+        self._a2a(recv_rows.view(torch.int32), send_rows.view(torch.int32), rc, sc)
+        self._a2a(recv_ids, send_ids, rc, sc)
+        d_recv = self.backend.experts(recv_rows, recv_ids)
+        d_back = torch.empty((T * k, H), dtype=d_recv.dtype, device=dev)
+        self._a2a(d_back.view(torch.int32), d_recv.contiguous().view(torch.int32), sc, rc)
+        d = torch.empty_like(d_back)
+        d[order] = d_back
+        shared = self.backend.shared_expert(x)
+        return self.backend.combine(d.view(T, k, H), inds, scores, shared, sg)
