@@ -191,7 +191,19 @@ typedef struct FnMoELayerArgs {
    * expert projections come from these tables; the *_weight arrays and
    * `table` are then ignored / must be NULL respectively. */
   FnTiledExperts tiled;
+  uint32_t flags;              /* FNMOE_LAYER_* */
+  uint32_t reserved1;
 } FnMoELayerArgs;
+
+/* FnMoELayerArgs.flags: by default a layer with tiled tables (group size 32,
+ * hidden and inter multiples of 256) and at least FNMOE_PREFILL_PAIRS
+ * (token, slot) pairs runs its experts as tcgen05 GEMMs on dequantised bf16
+ * weights (float32 accumulation; results within float32 rounding of the
+ * decode kernels, not bit-identical); smaller batches run the exact decode
+ * kernels.  These flags force one path. */
+#define FNMOE_LAYER_FORCE_PREFILL 1u
+#define FNMOE_LAYER_FORCE_DECODE 2u
+#define FNMOE_PREFILL_PAIRS 4096u
 
 /* Repack experts [0, experts) of reference-layout projection arrays into
  * records [first_record, first_record + experts) of tiled tables. */

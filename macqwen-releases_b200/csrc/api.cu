@@ -602,6 +602,9 @@ struct LayerLayout {
   Layout core;
   uint16_t *logits, *shared_logit, *shared_gate, *scores, *mass;
   uint32_t *inds, *routes;
+  int4 *ptiles;        // 128-pair tiles of the prefill path
+  int32_t *n_ptiles;
+  int max_ptiles;
 };
 
 uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL) {
@@ -622,6 +625,9 @@ uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL) {
   LL.inds = cv.take<uint32_t>(static_cast<uint64_t>(T) * k);
   LL.routes = cv.take<uint32_t>(static_cast<uint64_t>(T) * k);
   carve_core(cv, LL.core, T, a->hidden_size, a->inter_size, a->group_size, n_total, n_bins, true);
+  LL.max_ptiles = prefill_max_tiles(n_total, n_bins);
+  LL.ptiles = cv.take<int4>(static_cast<uint64_t>(LL.max_ptiles));
+  LL.n_ptiles = cv.take<int32_t>(4);
   return cv.off + 256;
 }
 
@@ -688,12 +694,18 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
   }
   if (int rc = check_expert_alignment(call)) return rc;
 
+  const int n_total_pairs = n_pairs + (shared ? T : 0);
+  bool prefill = prefill_supported(call) && (a->flags & FNMOE_LAYER_FORCE_DECODE) == 0 &&
+                 ((a->flags & FNMOE_LAYER_FORCE_PREFILL) != 0 || n_total_pairs >= static_cast<int>(FNMOE_PREFILL_PAIRS));
+  if ((a->flags & FNMOE_LAYER_FORCE_PREFILL) && !prefill_supported(call))
+    return fail(FNMOE_ERR_UNSUPPORTED,
+                "the prefill path needs tiled tables, group size 32 and hidden/inter multiples of 256");
   Layout &L = LL.core;
   uint16_t *logits = a->logits_out ? static_cast<uint16_t *>(a->logits_out) : LL.logits;
   uint32_t *inds = a->inds_out ? a->inds_out : LL.inds;
   uint16_t *scores = a->scores_out ? static_cast<uint16_t *>(a->scores_out) : LL.scores;
 
-  {
+  if (!prefill) {
     Prof p("prep_x", s);
     e = launch_prep_rows(static_cast<const uint16_t *>(a->x), T, H, G, L.xl, L.xm, s);
   }
@@ -718,21 +730,40 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
                      static_cast<int>(call.table.records), L.gv, s);
   }
   if (e != cudaSuccess) return cuda_fail(e, "group");
-  {
-    Prof p("gate_up", s);
-    e = launch_gate_up(call, L.gv, L.xl, L.xm, L.act, nullptr, nullptr, s);
+  if (prefill) {
+    {
+      Prof p("prefill_tiles", s);
+      e = launch_prefill_tiles(L.gv, LL.ptiles, LL.n_ptiles, LL.max_ptiles, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "prefill tiles");
+    {
+      Prof p("gate_up", s);
+      e = launch_prefill_gemm(true, call, L.gv, LL.ptiles, LL.n_ptiles, LL.max_ptiles,
+                              static_cast<const uint16_t *>(a->x), L.act, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "prefill gate_up");
+    {
+      Prof p("down", s);
+      e = launch_prefill_gemm(false, call, L.gv, LL.ptiles, LL.n_ptiles, LL.max_ptiles, L.act, L.d, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "prefill down");
+  } else {
+    {
+      Prof p("gate_up", s);
+      e = launch_gate_up(call, L.gv, L.xl, L.xm, L.act, nullptr, nullptr, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "gate_up");
+    {
+      Prof p("prep_act", s);
+      e = launch_prep_rows(L.act, n_pairs + (shared ? T : 0), I, G, L.al, L.am, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "prep act");
+    {
+      Prof p("down", s);
+      e = launch_down(call, L.gv, L.al, L.am, L.d, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "down");
   }
-  if (e != cudaSuccess) return cuda_fail(e, "gate_up");
-  {
-    Prof p("prep_act", s);
-    e = launch_prep_rows(L.act, n_pairs + (shared ? T : 0), I, G, L.al, L.am, s);
-  }
-  if (e != cudaSuccess) return cuda_fail(e, "prep act");
-  {
-    Prof p("down", s);
-    e = launch_down(call, L.gv, L.al, L.am, L.d, s);
-  }
-  if (e != cudaSuccess) return cuda_fail(e, "down");
   {
     Prof p("combine", s);
     e = launch_combine(L.d, LL.routes, scores, 0, T, k, H, shared ? kCombineParts : kCombineNone, nullptr,

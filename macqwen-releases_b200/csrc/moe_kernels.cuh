@@ -46,6 +46,8 @@ struct DeviceInfo {
 
 DeviceInfo device_info();
 cudaError_t ensure_exp_table(cudaStream_t stream);
+// Device address of the bfloat16 exp table (initialised by ensure_exp_table).
+cudaError_t exp_table_address(const uint16_t **table);
 uint32_t *device_error_word();
 
 // Row fixed point of bf16 rows: limbs [rows][groups][2][G] fp16 (fragment
@@ -125,6 +127,16 @@ cudaError_t launch_tile_experts(const uint32_t *wA, const uint32_t *wB, const ui
                                 const uint16_t *sB, const uint16_t *bB, int experts, int O, int K, int G, bool dual,
                                 uint8_t *dst, uint64_t record_bytes, cudaStream_t s);
 uint64_t tiled_record_bytes(int O, int K, bool dual);
+
+// Prefill (tcgen05) path: 128-pair tiles per expert bin, then grouped GEMMs
+// on tiled tables with dequantised bf16 weights (G = 32, K % 256 == 0).
+bool prefill_supported(const ExpertCallArgs &a);
+int prefill_max_tiles(int n_total, int n_bins);
+cudaError_t launch_prefill_tiles(const GroupView &gv, int4 *ptiles, int32_t *n_ptiles, int max_tiles,
+                                 cudaStream_t s);
+cudaError_t launch_prefill_gemm(bool dual, const ExpertCallArgs &a, const GroupView &gv, const int4 *ptiles,
+                                const int32_t *n_ptiles, int max_tiles, const uint16_t *in, uint16_t *out,
+                                cudaStream_t s);
 
 cudaError_t launch_dequant(const uint32_t *w, const uint16_t *sc,
                            const uint16_t *bi, uint16_t *out, uint64_t rows,

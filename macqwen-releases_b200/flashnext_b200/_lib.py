@@ -99,7 +99,13 @@ class FnMoELayerArgs(ctypes.Structure):
         ("output", _vp), ("logits_out", _vp), ("inds_out", _vp), ("scores_out", _vp),
         ("workspace", _vp), ("workspace_bytes", _u64),
         ("tiled", FnTiledExperts),
+        ("flags", _u32), ("reserved1", _u32),
     ]
+
+
+LAYER_FORCE_PREFILL = 0x1
+LAYER_FORCE_DECODE = 0x2
+PREFILL_PAIRS = 4096
 
 
 class FnTileArgs(ctypes.Structure):

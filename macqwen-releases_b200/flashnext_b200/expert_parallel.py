@@ -10,11 +10,13 @@ tokens (data parallel over tokens).  One layer step:
 2. dispatch: the (token, slot) pairs are ordered by owner rank (stable in pair
    order); pair counts are exchanged, then each pair's input row and the
    owner-local expert id go to the owner (``all_to_all_single``);
-3. the owner runs its experts on the received rows, one slot per row
-   (``fnmoe_moe_execute`` with per-slot outputs);
+3. the owner runs its experts on the received rows, one slot per row,
+   together with the shared expert on its own tokens (the shared expert is
+   one more record of its tiled table; ``fnmoe_moe_execute`` with per-slot
+   outputs);
 4. the bfloat16 outputs come back along the reverse all-to-all and land in
    their (token, slot) places;
-5. the token's rank computes the shared expert and the slot-ordered combine
+5. the token's rank combines in slot order and adds the gated shared expert
    (``fnmoe_combine``, ``metal_runtime.py:301-333``).
 
 Every kernel gives a row's result independently of the rest of its batch, so
@@ -24,7 +26,7 @@ rows travel as int32 words (pairs of bfloat16), which every backend carries.
 
 The compute steps go through a backend object: ``CudaBackend`` (the product)
 or, for multi-process tests of the dispatch/combine logic on CPU ranks, any
-object with the same four methods.
+object with the same three methods (route, experts, combine).
 """
 from __future__ import annotations
 
@@ -58,17 +60,22 @@ class CudaBackend:
         self.top_k = int(top_k)
         self.group_size = int(group_size)
         self.renorm_blend = float(renorm_blend)
-        self.local = TiledExperts(local_experts, None, group_size=group_size)
-        self.local_count = self.local.expert_count
-        self.inter_size = self.local.inter_size
-        self.shared = {}
+        # Local records: this rank's routed experts, then the shared expert as
+        # one more record (an ordinary expert to the executor), so received
+        # pairs and this rank's shared-expert rows go through one call.
+        torch = _torch()
+        merged = {}
         for name in ("gate_proj", "up_proj", "down_proj"):
-            w, s, b = _triple(shared[name])
-            self.shared[name] = (_dev(w).unsqueeze(0).contiguous(), _bf16(s, "shared scales").unsqueeze(0).contiguous(),
-                                 _bf16(b, "shared biases").unsqueeze(0).contiguous())
+            lw, ls, lb = (t for t in _triple(local_experts[name]))
+            sw, ss, sb = _triple(shared[name])
+            merged[name] = (torch.cat([_dev(lw), _dev(sw).unsqueeze(0)]),
+                            torch.cat([_bf16(ls, "scales"), _bf16(ss, "shared scales").unsqueeze(0)]),
+                            torch.cat([_bf16(lb, "biases"), _bf16(sb, "shared biases").unsqueeze(0)]))
+        self.local = TiledExperts(merged, None, group_size=group_size)
+        self.local_count = self.local.expert_count - 1  # routed experts; the shared one is record local_count
+        self.inter_size = self.local.inter_size
         self.shared_gate_weight = _bf16(shared_expert_gate, "shared_expert_gate").reshape(-1)
         self._ws = _Workspace()
-        self._ws2 = _Workspace()
 
     def route(self, x):
         torch = _torch()
@@ -119,13 +126,16 @@ class CudaBackend:
         _lib.check(lib.fnmoe_moe_execute(ctypes.byref(a), _stream()), "moe_execute")
         return out
 
-    def experts(self, rows, local_ids):
-        return self._execute(rows, local_ids.reshape(-1, 1).contiguous(), self.local, None, self.local_count, self._ws)
-
-    def shared_expert(self, x):
+    def experts(self, rows, local_ids, x):
+        """Per-pair outputs of the received rows, and the shared expert on x."""
         torch = _torch()
-        zeros = torch.zeros((x.shape[0], 1), dtype=torch.int32, device="cuda")
-        return self._execute(x, zeros, None, self.shared, 1, self._ws2)
+        n = rows.shape[0]
+        all_rows = torch.cat([rows, x]).contiguous()
+        routes = torch.cat([local_ids.to(torch.int32),
+                            torch.full((x.shape[0],), self.local_count, dtype=torch.int32, device=x.device)])
+        out = self._execute(all_rows, routes.reshape(-1, 1).contiguous(), self.local, None, self.local_count + 1,
+                            self._ws)
+        return out[:n], out[n:]
 
     def combine(self, d, inds, scores, shared, shared_gate):
         torch = _torch()
@@ -175,16 +185,18 @@ class ExpertParallelMoE:
         self._a2a(recv_counts, send_counts, [1] * self.world, [1] * self.world)
         sc, rc = send_counts.tolist(), recv_counts.tolist()
         n_recv = int(sum(rc))
-        send_rows = x[torch.div(order, k, rounding_mode="floor")].contiguous()
-        send_ids = (flat[order] - owner[order] * self.per_rank).to(torch.int32).contiguous()
-        recv_rows = torch.empty((n_recv, H), dtype=x.dtype, device=dev)
-        recv_ids = torch.empty((n_recv,), dtype=torch.int32, device=dev)
-        self._a2a(recv_rows.view(torch.int32), send_rows.view(torch.int32), rc, sc)
-        self._a2a(recv_ids, send_ids, rc, sc)
-        d_recv = self.backend.experts(recv_rows, recv_ids)
+        # one payload row per pair: the input row as H/2 int32 words, then the
+        # owner-local expert id and three pad words
+        w = H // 2
+        send = torch.zeros((T * k, w + 4), dtype=torch.int32, device=dev)
+        send[:, :w] = x.view(torch.int32)[torch.div(order, k, rounding_mode="floor")]
+        send[:, w] = (flat[order] - owner[order] * self.per_rank).to(torch.int32)
+        recv = torch.empty((n_recv, w + 4), dtype=torch.int32, device=dev)
+        self._a2a(recv, send, rc, sc)
+        recv_rows = recv[:, :w].contiguous().view(x.dtype)
+        d_recv, shared = self.backend.experts(recv_rows, recv[:, w].contiguous(), x)
         d_back = torch.empty((T * k, H), dtype=d_recv.dtype, device=dev)
         self._a2a(d_back.view(torch.int32), d_recv.contiguous().view(torch.int32), sc, rc)
         d = torch.empty_like(d_back)
         d[order] = d_back
-        shared = self.backend.shared_expert(x)
         return self.backend.combine(d.view(T, k, H), inds, scores, shared, sg)

@@ -49,17 +49,23 @@ class SparseMoEBlock:
     With ``tiled`` (the default for array experts whose sizes allow it) the
     experts are repacked once into :class:`TiledExperts` and the layer reads
     only those; ``tiled=False`` keeps reading the reference-layout arrays.
+    ``path`` selects the expert kernels: "auto" (tcgen05 GEMMs on dequantised
+    bf16 weights for prefill-sized batches, the exact decode kernels
+    otherwise), "prefill" or "decode".
     """
 
     def __init__(self, router_weight, experts: Any, *, top_k: int = 10, shared: Mapping | None = None,
                  shared_expert_gate=None, group_size: int = 32, renorm_blend: float = 1.0,
-                 route_map=None, tiled: bool = True):
+                 route_map=None, tiled: bool = True, path: str = "auto"):
         torch = _torch()
         self.router_weight = _bf16(router_weight, "router_weight")
         self.expert_count, self.hidden_size = (int(v) for v in self.router_weight.shape)
         self.top_k = int(top_k)
         self.group_size = int(group_size)
         self.renorm_blend = float(renorm_blend)
+        if path not in ("auto", "prefill", "decode"):
+            raise ValueError("path must be 'auto', 'prefill' or 'decode'")
+        self.path = path
         self.table = experts if isinstance(experts, ExpertTable) else None
         self.route_map = None if route_map is None else _dev(route_map, torch.int32)
         if self.table is not None:
@@ -123,6 +129,7 @@ class SparseMoEBlock:
                 setattr(a, f"shared_{key}_scales", s.data_ptr())
                 setattr(a, f"shared_{key}_biases", b.data_ptr())
             a.shared_expert_gate = self.shared_expert_gate.data_ptr()
+        a.flags = {"auto": 0, "prefill": _lib.LAYER_FORCE_PREFILL, "decode": _lib.LAYER_FORCE_DECODE}[self.path]
         a.output = out.data_ptr()
         a.logits_out = logits.data_ptr()
         a.inds_out = inds.data_ptr()

@@ -42,7 +42,7 @@ def _tokens(rank):
 
 
 class OracleBackend:
-    """The four compute steps of the layer, by the NumPy oracle (torch CPU tensors in/out)."""
+    """The compute steps of the layer, by the NumPy oracle (torch CPU tensors in/out)."""
 
     def __init__(self, bank, shared, w, wg, lo, hi):
         self.bank = {k: tuple(a[lo:hi] for a in v) for k, v in bank.items()}
@@ -64,20 +64,17 @@ class OracleBackend:
         _, sg, _ = moe.shared_expert(xn, *self.shared, self.wg, G)
         return torch.from_numpy(inds.astype(np.int32)), self._bf(scores), self._bf(sg.reshape(-1))
 
-    def experts(self, rows, local_ids):
+    def experts(self, rows, local_ids, x):
         from oracle import moe
 
         if rows.shape[0] == 0:
-            return self._bf(np.zeros((0, H), np.float32))
-        d = moe.executor(rows.float().numpy(), local_ids.numpy().astype(np.int64).reshape(-1, 1),
-                         self.bank["gate_proj"], self.bank["up_proj"], self.bank["down_proj"], group_size=G)
-        return self._bf(d.reshape(-1, H))
-
-    def shared_expert(self, x):
-        from oracle import moe
-
+            d = np.zeros((0, H), np.float32)
+        else:
+            d = moe.executor(rows.float().numpy(), local_ids.numpy().astype(np.int64).reshape(-1, 1),
+                             self.bank["gate_proj"], self.bank["up_proj"], self.bank["down_proj"],
+                             group_size=G).reshape(-1, H)
         sh, _, _ = moe.shared_expert(x.float().numpy(), *self.shared, self.wg, G)
-        return self._bf(sh)
+        return self._bf(d), self._bf(sh)
 
     def combine(self, d, inds, scores, shared, shared_gate):
         from oracle import moe

@@ -364,6 +364,29 @@ def test_tiled_layer_matches_arrays_and_oracle(cuda_lib, tokens, hidden, inter, 
         assert_bf16_equal(_np(t), ref["out"], "tiled layer output")
 
 
+@pytest.mark.parametrize("tokens,experts,zipf", [(64, 64, None), (200, 32, 1.1), (13, 16, None)])
+def test_prefill_gemm_layer_within_tolerance(cuda_lib, tokens, experts, zipf):
+    """tcgen05 prefill path (dequantised bf16 weights, float32 tensor-core
+    accumulation) against the exact oracle layer and the exact decode path:
+    the north-star tolerance (max-abs 2e-2, mean-rel 5e-3), same routing."""
+    import torch
+
+    from flashnext_b200 import synthetic
+    from flashnext_b200.moe_block import SparseMoEBlock
+    L = synthetic.moe_layer(tokens, 2048, 512, experts, 10, 32, zipf=zipf, seed=tokens + 5)
+    kw = dict(top_k=10, shared=L.shared, shared_expert_gate=L.shared_expert_gate)
+    pre = SparseMoEBlock(L.router_weight, L.experts, path="prefill", **kw)
+    dec = SparseMoEBlock(L.router_weight, L.experts, path="decode", **kw)
+    out_p = pre(L.x).clone()
+    out_d = dec(L.x).clone()
+    assert torch.equal(pre.last_inds, dec.last_inds)
+    assert torch.isfinite(out_p.float()).all()
+    ref = _oracle_layer(L)
+    np.testing.assert_array_equal(_np(pre.last_inds), ref["inds"])
+    assert_north_star(_np(out_p), ref["out"])
+    assert_north_star(_np(out_p), _np(out_d))
+
+
 # --------------------------------------------------------------------------
 # paged attention
 # --------------------------------------------------------------------------
