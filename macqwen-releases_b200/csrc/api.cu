@@ -717,19 +717,30 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
                              logits, LL.shared_logit, s);
   }
   if (e != cudaSuccess) return cuda_fail(e, "router logits");
-  {
-    Prof p("softmax_topk", s);
-    e = launch_softmax_topk(logits, T, E, k, a->renorm_blend, a->table_routes_of_expert, has_table ? 1 : 0,
-                            inds, LL.routes, nullptr, scores, LL.mass, shared ? LL.shared_logit : nullptr,
-                            shared ? LL.shared_gate : nullptr, s);
+  e = cudaErrorNotSupported;
+  if (T <= 8) {
+    Prof p("route_group", s);
+    e = launch_route_small(logits, T, E, k, a->renorm_blend, a->table_routes_of_expert, has_table ? 1 : 0, inds,
+                           LL.routes, nullptr, scores, LL.mass, shared ? LL.shared_logit : nullptr,
+                           shared ? LL.shared_gate : nullptr, shared ? T : 0, call.array_experts,
+                           static_cast<int>(call.table.records), L.gv, s);
+    if (e != cudaSuccess && e != cudaErrorNotSupported) return cuda_fail(e, "route_group");
   }
-  if (e != cudaSuccess) return cuda_fail(e, "softmax_topk");
-  {
-    Prof p("group", s);
-    e = launch_group(LL.routes, n_pairs, shared ? T : 0, call.array_experts,
-                     static_cast<int>(call.table.records), L.gv, s);
+  if (e == cudaErrorNotSupported) {
+    {
+      Prof p("softmax_topk", s);
+      e = launch_softmax_topk(logits, T, E, k, a->renorm_blend, a->table_routes_of_expert, has_table ? 1 : 0,
+                              inds, LL.routes, nullptr, scores, LL.mass, shared ? LL.shared_logit : nullptr,
+                              shared ? LL.shared_gate : nullptr, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "softmax_topk");
+    {
+      Prof p("group", s);
+      e = launch_group(LL.routes, n_pairs, shared ? T : 0, call.array_experts,
+                       static_cast<int>(call.table.records), L.gv, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "group");
   }
-  if (e != cudaSuccess) return cuda_fail(e, "group");
   if (prefill) {
     {
       Prof p("prefill_tiles", s);

@@ -182,4 +182,33 @@ __device__ __forceinline__ void set_error(uint32_t *err, uint32_t bit) {
 __host__ __device__ __forceinline__ int meta_a_index(int groups) { return ((groups + 3) / 4) * 4; }
 __host__ __device__ __forceinline__ int meta_pitch(int groups) { return meta_a_index(groups) + 4; }
 
+// Programmatic dependent launch.  A kernel started by launch_pdl may begin
+// while the previous kernel of its stream is still running: pdl_wait()
+// blocks until that kernel has completed and its writes are visible.  Every
+// kernel launched this way calls pdl_wait() before it reads data written by
+// an earlier kernel and before its own global writes, so each kernel still
+// completes after all earlier ones.  pdl_trigger() lets the next kernel of
+// the stream start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+// false when FNMOE_NO_PDL is set in the environment (plain stream order).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 }  // namespace fnmoe

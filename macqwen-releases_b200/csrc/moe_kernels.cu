@@ -18,6 +18,7 @@
 
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <mutex>
 
 #include "async.cuh"
@@ -45,6 +46,11 @@ std::mutex g_init_mutex;
 bool g_exp_ready[64] = {false};
 int g_sms[64] = {0};
 }  // namespace
+
+bool pdl_enabled() {
+  static const bool on = std::getenv("FNMOE_NO_PDL") == nullptr;
+  return on;
+}
 
 DeviceInfo device_info() {
   int dev = 0;
@@ -120,6 +126,8 @@ template <int G, int SPT>
 __global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *__restrict__ rows, int n_rows, int K, int TPR,
                                                    uint16_t *__restrict__ limbs, float *__restrict__ meta,
                                                    uint32_t *err) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int LPG = G / 8;  // lanes per group
   __shared__ uint32_t s_mx[8][8];
   const int lane = threadIdx.x & 31;
@@ -213,11 +221,13 @@ cudaError_t launch_prep_g(const uint16_t *rows, int n_rows, int K, uint16_t *lim
   const int blocks = (n_rows + rpc - 1) / rpc;
   const int threads = rpc * tpr;
   uint32_t *err = device_error_word();
-  if (spt == 1) k_prep_rows<G, 1><<<blocks, threads, 0, s>>>(rows, n_rows, K, tpr, limbs, meta, err);
-  else if (spt == 2) k_prep_rows<G, 2><<<blocks, threads, 0, s>>>(rows, n_rows, K, tpr, limbs, meta, err);
-  else if (spt <= 4) k_prep_rows<G, 4><<<blocks, threads, 0, s>>>(rows, n_rows, K, tpr, limbs, meta, err);
-  else if (spt <= 8) k_prep_rows<G, 8><<<blocks, threads, 0, s>>>(rows, n_rows, K, tpr, limbs, meta, err);
+  cudaError_t e = cudaSuccess;
+  if (spt == 1) e = launch_pdl(k_prep_rows<G, 1>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err);
+  else if (spt == 2) e = launch_pdl(k_prep_rows<G, 2>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err);
+  else if (spt <= 4) e = launch_pdl(k_prep_rows<G, 4>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err);
+  else if (spt <= 8) e = launch_pdl(k_prep_rows<G, 8>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err);
   else return cudaErrorInvalidValue;
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -261,7 +271,7 @@ __device__ __forceinline__ int block_exclusive_scan_1024(int v, int *warp_sums, 
 __device__ __forceinline__ int bin_of_pair(const uint32_t *routes, int i, int n_pairs,
                                            int E_arr, int records, int n_bins) {
   if (i >= n_pairs) return n_bins - 1;  // shared expert bin
-  const uint32_t r = routes[i];
+  const uint32_t r = __ldcg(routes + i);  // L2 load: routes may come from this same kernel
   if (r & kSlotBit) {
     const uint32_t slot = r & 0x7FFFFFFFu;
     return slot < static_cast<uint32_t>(records) ? E_arr + static_cast<int>(slot) : -1;
@@ -269,108 +279,182 @@ __device__ __forceinline__ int bin_of_pair(const uint32_t *routes, int i, int n_
   return r < static_cast<uint32_t>(E_arr) ? static_cast<int>(r) : -1;
 }
 
-__global__ void __launch_bounds__(1024) k_group(const uint32_t *__restrict__ routes, int n_pairs,
-                                                int shared_tokens, int E_arr, int records,
-                                                GroupView gv, uint32_t *err) {
-  extern __shared__ int sm[];
-  int *cnt = sm;                 // [n_bins]
-  int *run = sm + gv.n_bins;     // [n_bins]
+// Stable counting sort of the pairs by bin in one CTA.  The first `seg_warps`
+// warps each own a contiguous segment of pair ids; a table of per-warp bin
+// counts ([seg_warps][n_bins] in shared memory) turns into each
+// warp's first write position inside every bin, so the segments scatter in
+// parallel and pair order inside a bin is kept.  The 8-pair decode tiles are
+// then written one per thread (bin found by binary search over the tile
+// prefix), so a large bin is not left to one thread.
+constexpr int kGroupUnroll = 4;
+
+// Lanes holding the same key (0 <= key < 2^nbits): a ballot per key bit.
+__device__ __forceinline__ unsigned match_key(int key, int nbits) {
+  unsigned m = 0xFFFFFFFFu;
+  for (int k = 0; k < nbits; ++k) {
+    const bool bit = (key >> k) & 1;
+    const unsigned bal = __ballot_sync(0xFFFFFFFFu, bit);
+    m &= bit ? bal : ~bal;
+  }
+  return m;
+}
+
+// One warp's segment [i0, i1): with order == nullptr, count pairs per bin into
+// `row`; otherwise scatter them stably, `row` holding the warp's next write
+// position inside each bin (relative to off[bin]).
+__device__ __forceinline__ void group_walk(const uint32_t *routes, int n_pairs, int E_arr,
+                                           int records, int n_bins, int i0, int i1, int *row,
+                                           const int *off, int32_t *order, uint32_t *err) {
+  const int lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  const int nbits = 32 - __clz(n_bins + 1);
+  for (int base = i0; base < i1; base += 32 * kGroupUnroll) {
+    int b[kGroupUnroll];
+#pragma unroll
+    for (int u = 0; u < kGroupUnroll; ++u) {
+      const int i = base + 32 * u + lane;
+      b[u] = i < i1 ? bin_of_pair(routes, i, n_pairs, E_arr, records, n_bins) : -2;
+    }
+    if (order == nullptr) {
+#pragma unroll
+      for (int u = 0; u < kGroupUnroll; ++u) {
+        if (b[u] >= 0) atomicAdd(&row[b[u]], 1);
+        else if (b[u] == -1) set_error(err, kErrBadRoute);
+      }
+      continue;
+    }
+#pragma unroll
+    for (int u = 0; u < kGroupUnroll; ++u) {
+      const unsigned m = match_key(b[u] + 2, nbits);
+      const bool leader = (m >> lane) == 1u;  // highest lane of its bin group
+      int pos = 0;
+      if (b[u] >= 0) pos = off[b[u]] + row[b[u]] + __popc(m & lt);
+      __syncwarp();
+      if (b[u] >= 0) {
+        order[pos] = base + 32 * u + lane;
+        if (leader) row[b[u]] += __popc(m);
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// Body of the grouping (1024 threads); `sm` is group_smem_bytes() of shared memory.
+__device__ __forceinline__ void group_body(const uint32_t *routes, int n_pairs,
+                                           int shared_tokens, int E_arr, int records,
+                                           const GroupView &gv, int seg_warps, uint32_t *err, int *sm) {
+  const int n_bins = gv.n_bins;
+  int *off = sm;                  // [n_bins + 1] first pair position of each bin
+  int *first = sm + n_bins + 1;   // [n_bins + 1] first decode tile of each bin
+  int *tbl = sm + 2 * (n_bins + 1);  // [seg_warps][n_bins]
   __shared__ int warp_sums[32];
   __shared__ int total_pairs, total_tiles;
-  const int tid = threadIdx.x;
-  const int n_bins = gv.n_bins;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int n_total = n_pairs + shared_tokens;
+  const int seg = ((n_total + seg_warps - 1) / seg_warps + 31) & ~31;
+  const int i0 = min(warp * seg, n_total), i1 = min(i0 + seg, n_total);
+  for (int j = tid; j < seg_warps * n_bins; j += blockDim.x) tbl[j] = 0;
+  __syncthreads();
+  if (warp < seg_warps)
+    group_walk(routes, n_pairs, E_arr, records, n_bins, i0, i1, tbl + warp * n_bins, nullptr, nullptr, err);
+  __syncthreads();
+  // per bin: total count, and each warp's exclusive prefix inside the bin
   for (int b = tid; b < n_bins; b += blockDim.x) {
-    cnt[b] = 0;
-    run[b] = 0;
+    int c = 0;
+    for (int w = 0; w < seg_warps; ++w) {
+      const int v = tbl[w * n_bins + b];
+      tbl[w * n_bins + b] = c;
+      c += v;
+    }
+    off[b] = c;  // count for now
   }
   __syncthreads();
-  for (int i = tid; i < n_total; i += blockDim.x) {
-    const int b = bin_of_pair(routes, i, n_pairs, E_arr, records, n_bins);
-    if (b >= 0) atomicAdd(&cnt[b], 1);
-    else set_error(err, kErrBadRoute);
-  }
-  __syncthreads();
-  // Exclusive scans of counts and tile counts over contiguous bin segments.
+  // exclusive scans of counts and decode-tile counts over contiguous bin segments
   const int per = (n_bins + 1023) / 1024;
   const int b0 = min(tid * per, n_bins), b1 = min(b0 + per, n_bins);
   int local_c = 0, local_t = 0;
   for (int b = b0; b < b1; ++b) {
-    local_c += cnt[b];
-    local_t += (cnt[b] + kTokPerItem - 1) / kTokPerItem;
+    local_c += off[b];
+    local_t += (off[b] + kTokPerItem - 1) / kTokPerItem;
   }
   int pre_c = block_exclusive_scan_1024(local_c, warp_sums, &total_pairs);
   int pre_t = block_exclusive_scan_1024(local_t, warp_sums, &total_tiles);
   for (int b = b0; b < b1; ++b) {
-    const int c = cnt[b];
+    const int c = off[b];
     gv.counts[b] = c;
     gv.offsets[b] = pre_c;
     gv.bin_key[b] = (b < E_arr) ? static_cast<uint32_t>(b)
                     : (b < E_arr + records) ? (kSlotBit | static_cast<uint32_t>(b - E_arr))
                                             : kSharedKey;
-    const int nt = (c + kTokPerItem - 1) / kTokPerItem;
-    cnt[b] = pre_t;  // first tile of the bin (counts now live in gv.counts)
-    run[b] = pre_c;  // running write position
+    off[b] = pre_c;
+    first[b] = pre_t;
     pre_c += c;
-    pre_t += nt;
+    pre_t += (c + kTokPerItem - 1) / kTokPerItem;
   }
-  __syncthreads();
   if (tid == 0) {
+    off[n_bins] = total_pairs;
+    first[n_bins] = total_tiles;
     gv.offsets[n_bins] = total_pairs;
     gv.n_tiles[0] = min(total_tiles, gv.max_tiles);
-
-  }
-  // Stable scatter: warp 0 walks pairs in index order, 32 at a time.
-  if (tid < 32) {
-    const int lane = tid;
-    const unsigned lt = (1u << lane) - 1u;
-    for (int base = 0; base < n_total; base += 32) {
-      const int i = base + lane;
-      const int b = (i < n_total) ? bin_of_pair(routes, i, n_pairs, E_arr, records, n_bins) : -2;
-      const unsigned m = __match_any_sync(0xFFFFFFFFu, b);
-      const int rank = __popc(m & lt);
-      int pos = 0;
-      if (b >= 0) pos = run[b] + rank;
-      __syncwarp();
-      if (b >= 0) {
-        gv.order[pos] = i;
-        if ((m >> lane) == 1u) run[b] += __popc(m);  // highest lane of the group
-      }
-      __syncwarp();
-    }
   }
   __syncthreads();
-  // Self-contained tile descriptors: {route key, start, len, bin} and the pair ids.
-  for (int b = b0; b < b1; ++b) {
-    const int c = gv.counts[b];
-    const int nt = (c + kTokPerItem - 1) / kTokPerItem;
-    const int first = cnt[b];
-    const int start_b = gv.offsets[b];
-    const uint32_t key = gv.bin_key[b];
-    for (int t = 0; t < nt && first + t < gv.max_tiles; ++t) {
-      const int st = start_b + t * kTokPerItem;
-      const int len = min(kTokPerItem, c - t * kTokPerItem);
-      int p[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) p[q] = q < len ? gv.order[st + q] : -1;
-      gv.tiles[3 * (first + t)] = make_int4(static_cast<int>(key), st, len, b);
-      gv.tiles[3 * (first + t) + 1] = make_int4(p[0], p[1], p[2], p[3]);
-      gv.tiles[3 * (first + t) + 2] = make_int4(p[4], p[5], p[6], p[7]);
+  if (warp < seg_warps)
+    group_walk(routes, n_pairs, E_arr, records, n_bins, i0, i1, tbl + warp * n_bins, off, gv.order, err);
+  __syncthreads();
+  // self-contained decode tile descriptors: {route key, start, len, bin} and the pair ids
+  const int n_tiles = min(total_tiles, gv.max_tiles);
+  for (int t = tid; t < n_tiles; t += blockDim.x) {
+    int lo = 0, hi = n_bins - 1;  // last bin with first[b] <= t (empty bins share their successor's start)
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (first[mid] <= t) lo = mid;
+      else hi = mid - 1;
     }
+    const int b = lo;
+    const int st = off[b] + (t - first[b]) * kTokPerItem;
+    const int len = min(kTokPerItem, off[b + 1] - st);
+    int p[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) p[q] = q < len ? gv.order[st + q] : -1;
+    gv.tiles[3 * t] = make_int4(static_cast<int>(gv.bin_key[b]), st, len, b);
+    gv.tiles[3 * t + 1] = make_int4(p[0], p[1], p[2], p[3]);
+    gv.tiles[3 * t + 2] = make_int4(p[4], p[5], p[6], p[7]);
   }
+}
+
+__global__ void __launch_bounds__(1024) k_group(const uint32_t *__restrict__ routes, int n_pairs,
+                                                int shared_tokens, int E_arr, int records,
+                                                GroupView gv, int seg_warps, uint32_t *err) {
+  extern __shared__ int sm[];
+  pdl_trigger();
+  pdl_wait();
+  group_body(routes, n_pairs, shared_tokens, E_arr, records, gv, seg_warps, err, sm);
+}
+
+// Segment warps and shared-memory bytes of the grouping for n_total pairs.
+size_t group_smem_bytes(int n_total, int n_bins, int *seg_warps_out) {
+  constexpr size_t kBudget = 200 * 1024;
+  const size_t fixed = static_cast<size_t>(n_bins + 1) * 2 * sizeof(int);
+  const size_t per_warp = static_cast<size_t>(n_bins) * sizeof(int);
+  int seg_warps = static_cast<int>(std::min<size_t>(32, (kBudget - std::min(fixed, kBudget)) / per_warp));
+  seg_warps = std::max(1, std::min(seg_warps, (n_total + 31) / 32));
+  *seg_warps_out = seg_warps;
+  return fixed + static_cast<size_t>(seg_warps) * per_warp;
 }
 
 cudaError_t launch_group(const uint32_t *routes, int n_pairs, int shared_tokens,
                          int array_experts, int table_records, GroupView gv,
                          cudaStream_t s) {
-  const size_t smem = static_cast<size_t>(gv.n_bins) * 2 * sizeof(int);
+  int seg_warps = 1;
+  const size_t smem = group_smem_bytes(n_pairs + shared_tokens, gv.n_bins, &seg_warps);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_group, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  k_group<<<1, 1024, smem, s>>>(routes, n_pairs, shared_tokens, array_experts, table_records,
-                                gv, device_error_word());
+  cudaError_t e = launch_pdl(k_group, 1, 1024, smem, s, routes, n_pairs, shared_tokens, array_experts,
+                             table_records, gv, seg_warps, device_error_word());
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -874,6 +958,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a,
                                                                uint16_t *__restrict__ g_out,
                                                                uint16_t *__restrict__ u_out, int sb_mode,
                                                                uint32_t *err) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int RPW = DUAL ? 8 : 16;
   constexpr int ROWS = RPW * WARPS;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1014,7 +1100,9 @@ cudaError_t launch_rows(const ExpertCallArgs &a, const GroupView &gv, const uint
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm <= 0)
     per_sm = 1;
-  kernel<<<di.sms * per_sm, threads, smem, s>>>(a, gv, xl, xm, out, g_out, u_out, sb_mode, device_error_word());
+  cudaError_t e = launch_pdl(kernel, di.sms * per_sm, threads, smem, s, a, gv, xl, xm, out, g_out, u_out, sb_mode,
+                             device_error_word());
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -1191,6 +1279,8 @@ __global__ void __launch_bounds__(256) k_combine(const uint16_t *__restrict__ d,
                                                  int mode, const uint16_t *__restrict__ sy,
                                                  const uint16_t *__restrict__ sh, const uint16_t *__restrict__ sg,
                                                  int E_arr, int records, uint16_t *__restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.y;
   const int h8 = blockIdx.x * blockDim.x + threadIdx.x;
   if (8 * h8 >= H || t >= T) return;
@@ -1254,6 +1344,8 @@ __global__ void k_combine_any(const uint16_t *__restrict__ d, const uint32_t *__
                               const void *__restrict__ scores, int sf32, int T, int S, int H, int mode,
                               const uint16_t *__restrict__ sy, const uint16_t *__restrict__ sh,
                               const uint16_t *__restrict__ sg, int E_arr, int records, uint16_t *__restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.y;
   const int h = blockIdx.x * blockDim.x + threadIdx.x;
   if (h >= H || t >= T) return;
@@ -1282,15 +1374,17 @@ cudaError_t launch_combine(const uint16_t *d, const uint32_t *routes, const void
                            uint16_t *out, cudaStream_t s) {
   if (slots > kCombineMaxSlots || H % 8) {
     dim3 grid((H + 255) / 256, tokens);
-    k_combine_any<<<grid, 256, 0, s>>>(d, routes, scores, scores_f32, tokens, slots, H, mode, shared_y, shared,
-                                       shared_gate, array_experts, table_records, out);
+    cudaError_t e = launch_pdl(k_combine_any, grid, 256, 0, s, d, routes, scores, scores_f32, tokens, slots, H, mode,
+                               shared_y, shared, shared_gate, array_experts, table_records, out);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }
   const int chunks = H / 8;
   const int threads = chunks >= 256 ? 256 : ((chunks + 31) / 32) * 32;
   dim3 grid((chunks + threads - 1) / threads, tokens);
-  k_combine<<<grid, threads, 0, s>>>(d, routes, scores, scores_f32, tokens, slots, H, mode, shared_y,
-                                     shared, shared_gate, array_experts, table_records, out);
+  cudaError_t e = launch_pdl(k_combine, grid, threads, 0, s, d, routes, scores, scores_f32, tokens, slots, H, mode, shared_y,
+                             shared, shared_gate, array_experts, table_records, out);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -1298,7 +1392,6 @@ cudaError_t launch_combine(const uint16_t *d, const uint32_t *routes, const void
 // router logits: bf16 GEMV with the canonical 32-lane order
 // ---------------------------------------------------------------------------
 
-constexpr int kRouterWarps = 8;  // warps per CTA
 
 // Grid (row groups, token blocks).  Each warp keeps kRouterRW router rows in
 // registers (RW = 2 up to hidden 3072, else 1) for blocks of kRouterTok tokens.
@@ -1306,7 +1399,7 @@ constexpr int kRouterWarps = 8;  // warps per CTA
 // registers (lane j owns 8-element chunks j, j+32, ... of each) and runs the
 // canonical per-lane chain for every (row, token) of the block, reading each
 // staged input element once for both rows; then the xor butterfly.
-template <int CH, int kRouterRW, int kRouterTok>
+template <int CH, int kRouterRW, int kRouterTok, int kRouterWarps>
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
     const uint16_t *__restrict__ x, const uint16_t *__restrict__ W, int T, int H, int E,
     const uint16_t *__restrict__ wsg, uint16_t *__restrict__ logits,
@@ -1318,16 +1411,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
   const int nchunks = H / 8;
   const int t0 = blockIdx.y * kRouterTok;
   const int tb = min(kRouterTok, T - t0);
-  // stage the token block as float32 (8 bf16 per 16-byte load)
-  const uint4 *xsrc = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t0) * H);
-  float4 *xdst = reinterpret_cast<float4 *>(xs);
-  for (int idx = threadIdx.x; idx < tb * nchunks; idx += blockDim.x) {
-    const uint4 v = ldg_u128(xsrc + idx);
-    xdst[2 * idx] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
-                                __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
-    xdst[2 * idx + 1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
-                                    __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
-  }
+  pdl_trigger();
   float w[kRouterRW][CH * 8];
   bool live[kRouterRW];
 #pragma unroll
@@ -1351,6 +1435,18 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
         for (int i = 0; i < 8; ++i) w[q][m * 8 + i] = 0.0f;
       }
     }
+  }
+  // the router rows are constant: their loads above overlap the previous kernel
+  pdl_wait();
+  // stage the token block as float32 (8 bf16 per 16-byte load)
+  const uint4 *xsrc = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t0) * H);
+  float4 *xdst = reinterpret_cast<float4 *>(xs);
+  for (int idx = threadIdx.x; idx < tb * nchunks; idx += blockDim.x) {
+    const uint4 v = ldg_u128(xsrc + idx);
+    xdst[2 * idx] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                                __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+    xdst[2 * idx + 1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
+                                    __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
   }
   __syncthreads();
   if (!live[0]) return;
@@ -1401,20 +1497,21 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
   }
 }
 
-template <int CH, int RW, int TOK>
+template <int CH, int RW, int TOK, int NW = 8>
 cudaError_t launch_router_cfg(const uint16_t *x, const uint16_t *W, int T, int H, int E,
                               const uint16_t *w_shared_gate, uint16_t *logits, uint16_t *shared_logit,
                               cudaStream_t s) {
   const int rows = E + (w_shared_gate ? 1 : 0);
-  const int rows_per_cta = kRouterWarps * RW;
+  const int rows_per_cta = NW * RW;
   const dim3 grid((rows + rows_per_cta - 1) / rows_per_cta, (T + TOK - 1) / TOK);
   const size_t smem = static_cast<size_t>(TOK) * H * sizeof(float);
-  auto kernel = k_router_logits<CH, RW, TOK>;
+  auto kernel = k_router_logits<CH, RW, TOK, NW>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  kernel<<<grid, kRouterWarps * 32, smem, s>>>(x, W, T, H, E, w_shared_gate, logits, shared_logit);
+  cudaError_t e = launch_pdl(kernel, grid, NW * 32, smem, s, x, W, T, H, E, w_shared_gate, logits, shared_logit);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -1422,6 +1519,15 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
                                  const uint16_t *w_shared_gate, uint16_t *logits,
                                  uint16_t *shared_logit, cudaStream_t s) {
   const int ch = (H / 8 + 31) / 32;
+  // Small batches: one router row per warp and 4-warp CTAs, so ~E/4 CTAs
+  // share the weight read instead of E/16.
+  if (T <= 4) {
+    if (ch <= 4) return launch_router_cfg<4, 1, 4, 4>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
+    if (ch <= 8) return launch_router_cfg<8, 1, 4, 4>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
+    if (ch <= 12) return launch_router_cfg<12, 1, 4, 4>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
+    if (ch <= 16) return launch_router_cfg<16, 1, 4, 4>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
+    return cudaErrorInvalidValue;
+  }
   if (ch <= 4) return launch_router_cfg<4, 2, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
   if (ch <= 8) return launch_router_cfg<8, 2, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
   if (ch <= 12) return launch_router_cfg<12, 2, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
@@ -1442,6 +1548,8 @@ __global__ void __launch_bounds__(128) k_softmax_topk(
     uint32_t *__restrict__ routes, uint16_t *__restrict__ raw_scores,
     uint16_t *__restrict__ scores, uint16_t *__restrict__ mass,
     const uint16_t *__restrict__ shl, uint16_t *__restrict__ shg) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 4 + warp;
   if (t >= T) return;
@@ -1515,6 +1623,146 @@ __global__ void __launch_bounds__(128) k_softmax_topk(
   }
 }
 
+// Softmax, top-k and renorm for up to kRouteSmallTokens tokens, then the
+// grouping, in one 1024-thread CTA (small decode batches: one launch instead
+// of two, and the exps of a token spread over 32/Tp warps, Tp = T rounded up
+// to a power of two).  Max, exps, the canonical 32-lane sum, the key order
+// and the renorm are those of k_softmax_topk, so results are identical.
+constexpr int kRouteSmallTokens = 8;
+
+template <int PER>
+__global__ void __launch_bounds__(1024) k_route_small(
+    const uint16_t *__restrict__ logits, int T, int E, int k, float blend,
+    const uint32_t *__restrict__ route_map, int table_routes, uint32_t *inds, uint32_t *routes,
+    uint16_t *raw_scores, uint16_t *scores, uint16_t *mass, const uint16_t *__restrict__ shl,
+    uint16_t *shg, int shared_tokens, int E_arr, int records, GroupView gv, int seg_warps, uint32_t *err) {
+  extern __shared__ int sm[];
+  pdl_trigger();
+  pdl_wait();
+  float *ev = reinterpret_cast<float *>(sm);  // [T][E]: exps, then keys
+  uint32_t *kv = reinterpret_cast<uint32_t *>(sm);
+  __shared__ float s_max[kRouteSmallTokens][32];
+  __shared__ float s_sum[kRouteSmallTokens];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tp = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
+  const int wpt = 32 / tp;
+  const int t = warp / wpt, wl = warp - t * wpt;
+  const int per = (E + 31) / 32;
+  const bool tok = t < T;
+  const uint16_t *lrow = logits + static_cast<size_t>(tok ? t : 0) * E;
+  float mx = -INFINITY;
+  if (tok)
+    for (int m = wl; m < per; m += wpt)
+      if (lane + 32 * m < E) mx = fmaxf(mx, bf16_to_f32(lrow[lane + 32 * m]));
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+  if (tok && lane == 0) s_max[t][wl] = mx;
+  __syncthreads();
+  if (tok) {
+    float M = -INFINITY;
+    for (int w = 0; w < wpt; ++w) M = fmaxf(M, s_max[t][w]);
+    for (int m = wl; m < per; m += wpt) {
+      const int i = lane + 32 * m;
+      if (i < E) ev[t * E + i] = __double2float_rn(exp(static_cast<double>(__fsub_rn(bf16_to_f32(lrow[i]), M))));
+    }
+  }
+  __syncthreads();
+  if (tok && wl == 0) {
+    float sum = -0.0f;
+#pragma unroll
+    for (int m = 0; m < PER; ++m)
+      if (m < per && lane + 32 * m < E) sum = __fadd_rn(sum, ev[t * E + lane + 32 * m]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xFFFFFFFFu, sum, off));
+    if (lane == 0) s_sum[t] = sum;
+  }
+  __syncthreads();
+  if (tok) {
+    const float sum = s_sum[t];
+    for (int m = wl; m < per; m += wpt) {
+      const int i = lane + 32 * m;
+      if (i < E) {
+        const uint32_t pb = f32_to_bf16(__fdiv_rn(ev[t * E + i], sum));
+        kv[t * E + i] = (pb << 16) | (0xFFFFu - static_cast<uint32_t>(i));
+      }
+    }
+  }
+  __syncthreads();
+  if (tok && wl == 0) {
+    uint32_t key[PER];
+#pragma unroll
+    for (int m = 0; m < PER; ++m) key[m] = (m < per && lane + 32 * m < E) ? kv[t * E + lane + 32 * m] : 0u;
+    float acc = 0.0f;
+    float sel = 0.0f;
+    uint32_t idx = 0;
+    for (int q = 0; q < k; ++q) {
+      uint32_t best = 0u;
+#pragma unroll
+      for (int m = 0; m < PER; ++m) best = max(best, key[m]);
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, off));
+#pragma unroll
+      for (int m = 0; m < PER; ++m)
+        if (key[m] == best) key[m] = 0u;
+      const float p = bf16_to_f32(static_cast<uint16_t>(best >> 16));
+      if (lane == q) {
+        sel = p;
+        idx = 0xFFFFu - (best & 0xFFFFu);
+      }
+      acc = __fadd_rn(acc, p);
+    }
+    const float topm = round_bf16(acc);
+    const float bl = round_bf16(blend);
+    const float normalizer = badd(topm, bmul(bl, bsub(topm, topm)));
+    if (lane < k) {
+      const size_t o = static_cast<size_t>(t) * k + lane;
+      inds[o] = idx;
+      routes[o] = route_map ? route_map[idx] : (table_routes ? (kSlotBit | idx) : idx);
+      if (raw_scores) raw_scores[o] = f32_to_bf16(sel);
+      if (scores) scores[o] = f32_to_bf16(__fdiv_rn(sel, normalizer));
+    }
+    if (lane == 0) {
+      if (mass) mass[t] = f32_to_bf16(topm);
+      if (shl && shg) shg[t] = f32_to_bf16(sigmoid_bf16(g_exp_bf16, bf16_to_f32(shl[t])));
+    }
+  }
+  __syncthreads();
+  group_body(routes, T * k, shared_tokens, E_arr, records, gv, seg_warps, err, sm);
+}
+
+cudaError_t launch_route_small(const uint16_t *logits, int T, int E, int k, float blend,
+                               const uint32_t *route_map, int table_routes, uint32_t *inds,
+                               uint32_t *routes, uint16_t *raw_scores, uint16_t *scores,
+                               uint16_t *mass, const uint16_t *shared_logit, uint16_t *shared_gate,
+                               int shared_tokens, int array_experts, int table_records, GroupView gv,
+                               cudaStream_t s) {
+  const int per = (E + 31) / 32;
+  if (T > kRouteSmallTokens || per > 32 || k > 32) return cudaErrorNotSupported;
+  int seg_warps = 1;
+  const size_t gsm = group_smem_bytes(T * k + shared_tokens, gv.n_bins, &seg_warps);
+  const size_t smem = std::max(gsm, static_cast<size_t>(T) * E * sizeof(float));
+#define FNMOE_ROUTE_CASE(P)                                                                            \
+  if (per <= P) {                                                                                      \
+    if (smem > 48 * 1024) {                                                                            \
+      cudaError_t e = cudaFuncSetAttribute(k_route_small<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                           static_cast<int>(smem));                                    \
+      if (e != cudaSuccess) return e;                                                                  \
+    }                                                                                                  \
+    cudaError_t e = launch_pdl(k_route_small<P>, 1, 1024, smem, s, logits, T, E, k, blend, route_map,     \
+                               table_routes, inds, routes, raw_scores, scores, mass, shared_logit,      \
+                               shared_gate, shared_tokens, array_experts, table_records, gv, seg_warps, \
+                               device_error_word());                                                    \
+    if (e != cudaSuccess) return e;                                                                    \
+    return cudaGetLastError();                                                                         \
+  }
+  FNMOE_ROUTE_CASE(4)
+  FNMOE_ROUTE_CASE(8)
+  FNMOE_ROUTE_CASE(16)
+  FNMOE_ROUTE_CASE(32)
+#undef FNMOE_ROUTE_CASE
+  return cudaErrorNotSupported;
+}
+
 cudaError_t launch_softmax_topk(const uint16_t *logits, int T, int E, int k, float blend,
                                 const uint32_t *route_map, int table_routes, uint32_t *inds,
                                 uint32_t *routes, uint16_t *raw_scores, uint16_t *scores,
@@ -1523,9 +1771,10 @@ cudaError_t launch_softmax_topk(const uint16_t *logits, int T, int E, int k, flo
   const int per = (E + 31) / 32;
 #define FNMOE_TOPK_CASE(P)                                                                           \
   if (per <= P) {                                                                                   \
-    k_softmax_topk<P><<<(T + 3) / 4, 128, 0, s>>>(logits, T, E, k, blend, route_map, table_routes, \
-                                                  inds, routes, raw_scores, scores, mass,          \
-                                                  shared_logit, shared_gate);                      \
+    cudaError_t e = launch_pdl(k_softmax_topk<P>, (T + 3) / 4, 128, 0, s, logits, T, E, k, blend,       \
+                               route_map, table_routes, inds, routes, raw_scores, scores, mass,        \
+                               shared_logit, shared_gate);                                              \
+    if (e != cudaSuccess) return e;                                                                    \
     return cudaGetLastError();                                                                    \
   }
   FNMOE_TOPK_CASE(4)

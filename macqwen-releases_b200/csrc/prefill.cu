@@ -175,6 +175,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
   const int nblk = K / 256;
   const uint64_t rec_bytes = DUAL ? a.tiled.gate_up_record : a.tiled.down_record;
   const uint8_t *tbase = DUAL ? a.tiled.gate_up : a.tiled.down;
+  pdl_trigger();
+  pdl_wait();
   const int n_items = n_ptiles[0] * NT;
   if (static_cast<int>(blockIdx.x) >= n_items) return;
 
@@ -329,6 +331,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
 // 128-pair tiles of every bin from the grouping counts and offsets (one CTA).
 __global__ void __launch_bounds__(1024) k_prefill_tiles(GroupView gv, int4 *ptiles, int32_t *n_ptiles,
                                                         int max_tiles) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int warp_sums[32];
   __shared__ int total;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -376,7 +380,8 @@ int prefill_max_tiles(int n_total, int n_bins) { return n_total / kPM + n_bins +
 
 cudaError_t launch_prefill_tiles(const GroupView &gv, int4 *ptiles, int32_t *n_ptiles, int max_tiles,
                                  cudaStream_t s) {
-  k_prefill_tiles<<<1, 1024, 0, s>>>(gv, ptiles, n_ptiles, max_tiles);
+  cudaError_t e = launch_pdl(k_prefill_tiles, 1, 1024, 0, s, gv, ptiles, n_ptiles, max_tiles);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -392,12 +397,15 @@ cudaError_t launch_prefill_gemm(bool dual, const ExpertCallArgs &a, const GroupV
   if (dual) {
     e = cudaFuncSetAttribute(k_prefill_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
     if (e != cudaSuccess) return e;
-    k_prefill_gemm<true><<<grid, kPThreads, kPSmem, s>>>(a, gv, ptiles, n_ptiles, in, out, tab, device_error_word());
+    e = launch_pdl(k_prefill_gemm<true>, grid, kPThreads, kPSmem, s, a, gv, ptiles, n_ptiles, in, out, tab,
+                   device_error_word());
+    if (e != cudaSuccess) return e;
   } else {
     e = cudaFuncSetAttribute(k_prefill_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
     if (e != cudaSuccess) return e;
-    k_prefill_gemm<false><<<grid, kPThreads, kPSmem, s>>>(a, gv, ptiles, n_ptiles, in, out, tab,
-                                                          device_error_word());
+    e = launch_pdl(k_prefill_gemm<false>, grid, kPThreads, kPSmem, s, a, gv, ptiles, n_ptiles, in, out, tab,
+                   device_error_word());
+    if (e != cudaSuccess) return e;
   }
   return cudaGetLastError();
 }
