@@ -750,12 +750,13 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
     {
       Prof p("gate_up", s);
       e = launch_prefill_gemm(true, call, L.gv, LL.ptiles, LL.n_ptiles, LL.max_ptiles,
-                              static_cast<const uint16_t *>(a->x), L.act, s);
+                              static_cast<const uint16_t *>(a->x), T, L.act, s);
     }
     if (e != cudaSuccess) return cuda_fail(e, "prefill gate_up");
     {
       Prof p("down", s);
-      e = launch_prefill_gemm(false, call, L.gv, LL.ptiles, LL.n_ptiles, LL.max_ptiles, L.act, L.d, s);
+      e = launch_prefill_gemm(false, call, L.gv, LL.ptiles, LL.n_ptiles, LL.max_ptiles, L.act, n_total_pairs,
+                              L.d, s);
     }
     if (e != cudaSuccess) return cuda_fail(e, "prefill down");
   } else {

@@ -22,6 +22,7 @@ constexpr int kWarp = 32;
 constexpr uint32_t kErrBadRoute = 1u;
 constexpr uint32_t kErrNonFinite = 2u;
 constexpr uint32_t kErrTimeout = 4u;
+constexpr uint32_t kErrBadTile = 8u;  // a prefill tile descriptor out of range (skipped)
 
 __device__ __forceinline__ float bf16_to_f32(uint16_t b) {
   return __uint_as_float(static_cast<uint32_t>(b) << 16);
@@ -188,7 +189,10 @@ __host__ __device__ __forceinline__ int meta_pitch(int groups) { return meta_a_i
 // kernel launched this way calls pdl_wait() before it reads data written by
 // an earlier kernel and before its own global writes, so each kernel still
 // completes after all earlier ones.  pdl_trigger() lets the next kernel of
-// the stream start launching.
+// the stream start launching.  Since such a kernel is alive while its
+// predecessor writes, data produced by earlier kernels is never read through
+// the non-coherent path (no __ldg, no const __restrict__ pointers): that
+// path assumes data read-only for the kernel's whole lifetime.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 

@@ -28,6 +28,7 @@
 namespace fnmoe {
 
 __device__ uint16_t g_exp_bf16[65536];
+__device__ uint16_t g_silu_bf16[65536];  // bf16 bits of bmul(g, sigmoid_bf16(g)) for every bf16 g
 __device__ uint32_t g_device_errors;
 
 // ---------------------------------------------------------------------------
@@ -39,6 +40,15 @@ __global__ void k_init_exp_table() {
   if (i >= 65536) return;
   const float v = bf16_to_f32(static_cast<uint16_t>(i));
   g_exp_bf16[i] = f64_to_bf16_once(exp(static_cast<double>(v)));
+}
+
+// g * sigmoid(g) with the SwiGLU's own bf16 operations (swiglu_bf16 without
+// the final multiply by u), so a lookup gives bit-identical activations.
+__global__ void k_init_silu_table() {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= 65536) return;
+  const float g = bf16_to_f32(static_cast<uint16_t>(i));
+  g_silu_bf16[i] = f32_to_bf16(bmul(g, sigmoid_bf16(g_exp_bf16, g)));
 }
 
 namespace {
@@ -72,6 +82,13 @@ cudaError_t exp_table_address(const uint16_t **table) {
   return e;
 }
 
+cudaError_t silu_table_address(const uint16_t **table) {
+  void *p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_silu_bf16);
+  *table = static_cast<const uint16_t *>(p);
+  return e;
+}
+
 cudaError_t ensure_exp_table(cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -80,6 +97,9 @@ cudaError_t ensure_exp_table(cudaStream_t stream) {
   std::lock_guard<std::mutex> lock(g_init_mutex);
   if (g_exp_ready[dev]) return cudaSuccess;
   k_init_exp_table<<<256, 256, 0, stream>>>();
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  k_init_silu_table<<<256, 256, 0, stream>>>();
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   e = cudaStreamSynchronize(stream);
@@ -123,11 +143,11 @@ __device__ __forceinline__ uint32_t half_pair(int lo, int hi) {
 // [e0,e4,e1,e5,e2,e6,e3,e7], and each group's sum fl(SX) (G/8 consecutive
 // slices = consecutive lanes) from a shuffle reduction.
 template <int G, int SPT>
-__global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *__restrict__ rows, int n_rows, int K, int TPR,
+__global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *rows, int n_rows, int K, int TPR,
                                                    uint16_t *__restrict__ limbs, float *__restrict__ meta,
                                                    uint32_t *err) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   constexpr int LPG = G / 8;  // lanes per group
   __shared__ uint32_t s_mx[8][8];
   const int lane = threadIdx.x & 31;
@@ -144,7 +164,7 @@ __global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *__restrict__ 
 #pragma unroll
   for (int k = 0; k < SPT; ++k) {
     const int i = tr + k * TPR;
-    v[k] = (live && i < slices) ? __ldg(src + i) : make_uint4(0u, 0u, 0u, 0u);
+    v[k] = (live && i < slices) ? src[i] : make_uint4(0u, 0u, 0u, 0u);
   }
   uint32_t mx = 0;
   bool bad = false;
@@ -422,12 +442,12 @@ __device__ __forceinline__ void group_body(const uint32_t *routes, int n_pairs,
   }
 }
 
-__global__ void __launch_bounds__(1024) k_group(const uint32_t *__restrict__ routes, int n_pairs,
+__global__ void __launch_bounds__(1024) k_group(const uint32_t *routes, int n_pairs,
                                                 int shared_tokens, int E_arr, int records,
                                                 GroupView gv, int seg_warps, uint32_t *err) {
   extern __shared__ int sm[];
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   group_body(routes, n_pairs, shared_tokens, E_arr, records, gv, seg_warps, err, sm);
 }
 
@@ -734,7 +754,7 @@ __device__ __forceinline__ void ring_wait(Ring &rg, uint32_t *err) {
 // its pair ids.  Slots past the tile's length keep stale data: they only feed
 // MMA columns (and accumulators) whose results are never stored.
 __device__ __forceinline__ void load_xstage(uint8_t *st, int *s_pairs, const XStage &xs, const RawDesc &rd, bool ok,
-                                            const uint16_t *__restrict__ xl, const float *__restrict__ xm,
+                                            const uint16_t *xl, const float *xm,
                                             int n_pairs, int slots, bool by_token) {
   const int tid = threadIdx.x, nt = blockDim.x;
   const int cpx = xs.Xrow / 16, cpm = xs.Mp / 16;
@@ -952,14 +972,14 @@ __device__ __forceinline__ int tile_stride(int n) {
 
 template <int G, int WARPS, bool DUAL, int R, bool TILED>
 __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a, GroupView gv,
-                                                               const uint16_t *__restrict__ xl,
-                                                               const float *__restrict__ xm,
+                                                               const uint16_t *xl,
+                                                               const float *xm,
                                                                uint16_t *__restrict__ out,
                                                                uint16_t *__restrict__ g_out,
                                                                uint16_t *__restrict__ u_out, int sb_mode,
                                                                uint32_t *err) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   constexpr int RPW = DUAL ? 8 : 16;
   constexpr int ROWS = RPW * WARPS;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1274,13 +1294,13 @@ __device__ __forceinline__ float bf16_lane(const uint4 &v, int e) {
 // Thread = 8 consecutive hidden elements of one token.  Every slot's route,
 // score and 16-byte output slice is loaded before the slot-ordered float32
 // accumulation (no fused multiply-add), so the loads overlap.
-__global__ void __launch_bounds__(256) k_combine(const uint16_t *__restrict__ d, const uint32_t *__restrict__ routes,
-                                                 const void *__restrict__ scores, int sf32, int T, int S, int H,
-                                                 int mode, const uint16_t *__restrict__ sy,
-                                                 const uint16_t *__restrict__ sh, const uint16_t *__restrict__ sg,
+__global__ void __launch_bounds__(256) k_combine(const uint16_t *d, const uint32_t *routes,
+                                                 const void *scores, int sf32, int T, int S, int H,
+                                                 int mode, const uint16_t *sy,
+                                                 const uint16_t *sh, const uint16_t *sg,
                                                  int E_arr, int records, uint16_t *__restrict__ out) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y;
   const int h8 = blockIdx.x * blockDim.x + threadIdx.x;
   if (8 * h8 >= H || t >= T) return;
@@ -1297,7 +1317,7 @@ __global__ void __launch_bounds__(256) k_combine(const uint16_t *__restrict__ d,
       if (valid) {
         sc[s] = sf32 ? static_cast<const float *>(scores)[t * S + s]
                      : bf16_to_f32(static_cast<const uint16_t *>(scores)[t * S + s]);
-        dv[s] = ldg_u128(reinterpret_cast<const uint4 *>(d + (static_cast<size_t>(t) * S + s) * H + 8 * h8));
+        dv[s] = *reinterpret_cast<const uint4 *>(d + (static_cast<size_t>(t) * S + s) * H + 8 * h8);
       } else {
         sc[s] = __int_as_float(0x7FC00000);  // marks an invalid slot (skipped below)
       }
@@ -1316,9 +1336,9 @@ __global__ void __launch_bounds__(256) k_combine(const uint16_t *__restrict__ d,
   const size_t base = static_cast<size_t>(t) * H + 8 * h8;
   uint4 extra = make_uint4(0u, 0u, 0u, 0u);
   float gate = 0.0f;
-  if (mode == kCombineSharedY) extra = ldg_u128(reinterpret_cast<const uint4 *>(sy + base));
+  if (mode == kCombineSharedY) extra = *reinterpret_cast<const uint4 *>(sy + base);
   if (mode == kCombineParts) {
-    extra = ldg_u128(reinterpret_cast<const uint4 *>(sh + base));
+    extra = *reinterpret_cast<const uint4 *>(sh + base);
     gate = bf16_to_f32(sg[t]);
   }
   uint32_t o[4];
@@ -1340,12 +1360,12 @@ __global__ void __launch_bounds__(256) k_combine(const uint16_t *__restrict__ d,
 }
 
 // Any slot count: one element per thread, loads in the slot loop.
-__global__ void k_combine_any(const uint16_t *__restrict__ d, const uint32_t *__restrict__ routes,
-                              const void *__restrict__ scores, int sf32, int T, int S, int H, int mode,
-                              const uint16_t *__restrict__ sy, const uint16_t *__restrict__ sh,
-                              const uint16_t *__restrict__ sg, int E_arr, int records, uint16_t *__restrict__ out) {
-  pdl_trigger();
+__global__ void k_combine_any(const uint16_t *d, const uint32_t *routes,
+                              const void *scores, int sf32, int T, int S, int H, int mode,
+                              const uint16_t *sy, const uint16_t *sh,
+                              const uint16_t *sg, int E_arr, int records, uint16_t *__restrict__ out) {
   pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y;
   const int h = blockIdx.x * blockDim.x + threadIdx.x;
   if (h >= H || t >= T) return;
@@ -1401,7 +1421,7 @@ cudaError_t launch_combine(const uint16_t *d, const uint32_t *routes, const void
 // staged input element once for both rows; then the xor butterfly.
 template <int CH, int kRouterRW, int kRouterTok, int kRouterWarps>
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
-    const uint16_t *__restrict__ x, const uint16_t *__restrict__ W, int T, int H, int E,
+    const uint16_t *x, const uint16_t *__restrict__ W, int T, int H, int E,
     const uint16_t *__restrict__ wsg, uint16_t *__restrict__ logits,
     uint16_t *__restrict__ shared_logit) {
   extern __shared__ __align__(16) float xs[];  // [kRouterTok][H] float32
@@ -1411,7 +1431,6 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
   const int nchunks = H / 8;
   const int t0 = blockIdx.y * kRouterTok;
   const int tb = min(kRouterTok, T - t0);
-  pdl_trigger();
   float w[kRouterRW][CH * 8];
   bool live[kRouterRW];
 #pragma unroll
@@ -1438,11 +1457,12 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
   }
   // the router rows are constant: their loads above overlap the previous kernel
   pdl_wait();
+  pdl_trigger();
   // stage the token block as float32 (8 bf16 per 16-byte load)
   const uint4 *xsrc = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t0) * H);
   float4 *xdst = reinterpret_cast<float4 *>(xs);
   for (int idx = threadIdx.x; idx < tb * nchunks; idx += blockDim.x) {
-    const uint4 v = ldg_u128(xsrc + idx);
+    const uint4 v = xsrc[idx];
     xdst[2 * idx] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
                                 __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
     xdst[2 * idx + 1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
@@ -1543,13 +1563,13 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
 
 template <int kMaxPerLane>
 __global__ void __launch_bounds__(128) k_softmax_topk(
-    const uint16_t *__restrict__ logits, int T, int E, int k, float blend,
+    const uint16_t *logits, int T, int E, int k, float blend,
     const uint32_t *__restrict__ route_map, int table_routes, uint32_t *__restrict__ inds,
     uint32_t *__restrict__ routes, uint16_t *__restrict__ raw_scores,
     uint16_t *__restrict__ scores, uint16_t *__restrict__ mass,
-    const uint16_t *__restrict__ shl, uint16_t *__restrict__ shg) {
-  pdl_trigger();
+    const uint16_t *shl, uint16_t *__restrict__ shg) {
   pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 4 + warp;
   if (t >= T) return;
@@ -1632,13 +1652,13 @@ constexpr int kRouteSmallTokens = 8;
 
 template <int PER>
 __global__ void __launch_bounds__(1024) k_route_small(
-    const uint16_t *__restrict__ logits, int T, int E, int k, float blend,
+    const uint16_t *logits, int T, int E, int k, float blend,
     const uint32_t *__restrict__ route_map, int table_routes, uint32_t *inds, uint32_t *routes,
-    uint16_t *raw_scores, uint16_t *scores, uint16_t *mass, const uint16_t *__restrict__ shl,
+    uint16_t *raw_scores, uint16_t *scores, uint16_t *mass, const uint16_t *shl,
     uint16_t *shg, int shared_tokens, int E_arr, int records, GroupView gv, int seg_warps, uint32_t *err) {
   extern __shared__ int sm[];
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   float *ev = reinterpret_cast<float *>(sm);  // [T][E]: exps, then keys
   uint32_t *kv = reinterpret_cast<uint32_t *>(sm);
   __shared__ float s_max[kRouteSmallTokens][32];

@@ -48,6 +48,8 @@ DeviceInfo device_info();
 cudaError_t ensure_exp_table(cudaStream_t stream);
 // Device address of the bfloat16 exp table (initialised by ensure_exp_table).
 cudaError_t exp_table_address(const uint16_t **table);
+// Device address of the bfloat16 g*sigmoid(g) table (initialised with the exp table).
+cudaError_t silu_table_address(const uint16_t **table);
 uint32_t *device_error_word();
 
 // Row fixed point of bf16 rows: limbs [rows][groups][2][G] fp16 (fragment
@@ -143,9 +145,13 @@ bool prefill_supported(const ExpertCallArgs &a);
 int prefill_max_tiles(int n_total, int n_bins);
 cudaError_t launch_prefill_tiles(const GroupView &gv, int4 *ptiles, int32_t *n_ptiles, int max_tiles,
                                  cudaStream_t s);
+// Prefill grouped GEMM on tcgen05: gate/up (dual) reads token rows of x
+// ([in_rows = tokens][H]) and writes SwiGLU activations in bin order
+// ([n_total][I], row = position in gv.order); down reads those ([in_rows =
+// n_total][I]) and writes per-pair outputs ([n_total][H]).
 cudaError_t launch_prefill_gemm(bool dual, const ExpertCallArgs &a, const GroupView &gv, const int4 *ptiles,
-                                const int32_t *n_ptiles, int max_tiles, const uint16_t *in, uint16_t *out,
-                                cudaStream_t s);
+                                const int32_t *n_ptiles, int max_tiles, const uint16_t *in, int in_rows,
+                                uint16_t *out, cudaStream_t s);
 
 cudaError_t launch_dequant(const uint32_t *w, const uint16_t *sc,
                            const uint16_t *bi, uint16_t *out, uint64_t rows,

@@ -1,29 +1,40 @@
 // prefill.cu -- grouped expert GEMMs on tcgen05 for prefill-sized batches.
 //
-// For thousands of tokens per layer (a prefill chunk) the experts see ~100
-// pairs each and the projections become GEMMs.  Each work item is a tile of
-// up to 128 pairs of one expert bin (MMA M) times 256 output rows (MMA N):
-// 128 gate + 128 up rows (interleaved in groups of 8, as in the tiled tables)
-// for gate/up, 256 rows for down.  Per 64-wide k-step the CTA
-//   * gathers the tile's 128 input rows (bf16 x, or the bf16 SwiGLU output
-//     for down) with cp.async into a 128B-swizzled K-major shared tile,
-//   * stages the 256 weight rows' packed nibbles, scales and biases from the
-//     tiled tables, and dequantises them to bf16 -- bf16(s*q + b), one
-//     rounding (fma.rn.bf16x2), the reference's dequant rule -- into a second
-//     swizzled tile,
-//   * issues 4 tcgen05.mma (kind::f16, M128 N256 K16, fp32 accumulators in
-//     256 TMEM columns) from one elected thread and commits them to an
-//     mbarrier; the next k-step's copies and dequant overlap the MMAs.
-// The epilogue reads TMEM (tcgen05.ld 32x32b) and writes bf16 SwiGLU
-// activations (gate/up) or bf16 per-slot outputs (down).  Accumulation is
-// float32 in the tensor core's order, so results match the exact decode path
-// within float32 rounding, not bit for bit (the reference likewise switches
-// kernels for large batches).
+// For thousands of tokens per layer (a prefill chunk) each expert sees ~100
+// pairs and its projections become GEMMs.  A work item is a tile of up to 128
+// pairs of one expert bin (MMA M) times 256 output rows (MMA N): 128 gate +
+// 128 up rows (interleaved in groups of 8, as in the tiled tables) for
+// gate/up, 256 rows for down.  One persistent CTA per SM runs the items with
+// warp-specialised roles around mbarrier rings:
+//
+//   warp 0      producer: per 256-wide K block one bulk copy per row group
+//               (the 2560-byte chunks of the tiled tables) into a raw ring;
+//               per 64-wide k-step the 128 input rows into a 128B-swizzled
+//               K-major tile by TMA -- tile::gather4 of token rows of x for
+//               gate/up, a plain 2D tile of the bin-sorted activations for
+//               down;
+//   warp 1      MMA issuer: 4 tcgen05.mma (kind::f16, bf16, M128 N256 K16)
+//               per k-step into one of two 256-column fp32 accumulators in
+//               TMEM, commits releasing the input stages;
+//   warps 2-9   dequantise the raw ring into bf16 swizzled weight tiles,
+//               bf16(s*q + b) with one rounding (fma.rn.bf16x2), the
+//               reference's dequant rule;
+//   warps 10-13 epilogue: tcgen05.ld of the finished accumulator, then bf16
+//               SwiGLU activations in bin order (gate/up) or bf16 per-pair
+//               outputs (down), while the MMAs of the next item fill the
+//               other accumulator.
+//
+// Accumulation is float32 in the tensor core's order, so results match the
+// exact decode path within float32 rounding, not bit for bit.  Every wait is
+// bounded; a timeout sets the device error word, marks the CTA dead (later
+// waits return at once) and the kernel runs to its end.
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "async.cuh"
 #include "common.cuh"
@@ -33,20 +44,27 @@ namespace fnmoe {
 
 namespace {
 
-constexpr int kPM = 128;                 // pairs per tile (MMA M)
-constexpr int kPN = 256;                 // output rows per item (MMA N)
-constexpr int kPThreads = 256;
-constexpr int kARing = 4, kRawRing = 3, kBRing = 2;
-constexpr int kATile = kPM * 128;        // 128 rows x 64 bf16
-constexpr int kBTile = kPN * 128;        // 256 rows x 64 bf16
-constexpr int kRawRow = 40;              // 32 packed bytes, 2 scales, 2 biases
-constexpr int kRawTile = kPN * kRawRow;
+constexpr int kPM = 128;  // pairs per tile (MMA M)
+constexpr int kPN = 256;  // output rows per item (MMA N)
+constexpr int kDeqWarps = 8, kEpiWarps = 4;
+constexpr int kDeqWarp0 = 2, kEpiWarp0 = kDeqWarp0 + kDeqWarps;
+constexpr int kPThreads = 32 * (kEpiWarp0 + kEpiWarps);  // 448
+constexpr int kAStages = 4, kBStages = 2, kRawStages = 2;
+constexpr int kATile = kPM * 128;           // 128 rows x 64 bf16
+constexpr int kBTile = kPN * 128;           // 256 rows x 64 bf16
+constexpr int kRawTile = 16 * kTileChunk;   // 16 row groups x one 256-wide K block
 constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + kARing * kATile;
-constexpr int kOffRaw = kOffB + kBRing * kBTile;
-constexpr int kOffBar = kOffRaw + kRawRing * kRawTile;
-constexpr int kPSmem = kOffBar + 64 + 1024;  // + slack for the 1024-byte alignment of the tiles
-constexpr uint32_t kTmemCols = 256;
+constexpr int kOffB = kOffA + kAStages * kATile;
+constexpr int kOffRaw = kOffB + kBStages * kBTile;
+constexpr int kOffBar = kOffRaw + kRawStages * kRawTile;
+// barriers: a_full[4] a_empty[4] b_full[2] b_empty[2] raw_full[2] raw_empty[2] acc_full[2] acc_empty[2]
+constexpr int kBarA = 0, kBarAE = kBarA + kAStages, kBarB = kBarAE + kAStages, kBarBE = kBarB + kBStages;
+constexpr int kBarR = kBarBE + kBStages, kBarRE = kBarR + kRawStages, kBarC = kBarRE + kRawStages,
+              kBarCE = kBarC + 2, kBars = kBarCE + 2;
+constexpr int kOffMisc = kOffBar + kBars * 8;  // tmem base, dead flag
+constexpr int kPSmem = kOffMisc + 16 + 1024;   // + slack for the 1024-byte alignment of the tiles
+static_assert(kPSmem <= 227 * 1024, "prefill shared memory");
+constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
 constexpr uint32_t kPSpinLimit = 1u << 22;
 
 // Instruction descriptor: kind::f16, bf16 A and B (K-major), f32 D, M 128, N 256.
@@ -60,17 +78,46 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          (2ull << 61);
 }
 
-__device__ __forceinline__ void cp16s(uint32_t s, const void *g) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(g));
+__device__ __forceinline__ void sts128(uint32_t s, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};\n" ::"r"(s), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
 }
-__device__ __forceinline__ void cp8s(uint32_t s, const void *g) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(g));
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void cp4s(uint32_t s, const void *g) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(g));
+__device__ __forceinline__ void mbar_expect_tx_u32(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void sts128(uint32_t s, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};\n" ::"r"(s), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+__device__ __forceinline__ bool mbar_try_wait_u32(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s_u32(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+// Four rows (y0..y3) of 64 bf16 starting at column x, 128B-swizzled into 512 bytes at dst.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, int x, int y0, int y1, int y2,
+                                            int y3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(bar)
+      : "memory");
+}
+// A 64 x 128 box (64 bf16 of 128 rows from row y), 128B-swizzled.
+__device__ __forceinline__ void tma_tile2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
 }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
@@ -80,9 +127,8 @@ __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t 
       "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
-                   smem_u32(bar))
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
                : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
@@ -100,19 +146,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
-// Bounded wait for the next completion of `bar` (parity tracked in `phase`).
-__device__ __forceinline__ void bar_wait(uint64_t *bar, uint32_t &phase, bool &dead, uint32_t *err) {
-  if (!dead) {
-    uint32_t spins = 0;
-    while (!mbar_try_wait(bar, phase)) {
-      if (++spins >= kPSpinLimit) {
-        dead = true;
-        set_error(err, kErrTimeout);
-        break;
-      }
+// Bounded wait on `bar` for the phase of parity `parity`.  A timeout (or a
+// CTA already marked dead) returns false: the caller's role stops waiting.
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, volatile uint32_t *dead, uint32_t *err) {
+  uint32_t spins = 0;
+  while (!mbar_try_wait_u32(bar, parity)) {
+    if (*dead) return false;
+    if (++spins >= kPSpinLimit) {
+      *dead = 1u;
+      set_error(err, kErrTimeout);
+      return false;
     }
   }
-  phase ^= 1u;
+  return true;
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -153,39 +199,68 @@ __device__ __forceinline__ int pair_row(int pair, int n_pairs, int slots) {
   return pair < n_pairs ? pair / slots : pair - n_pairs;
 }
 
+struct PItem {
+  bool ok;
+  int nt, start, len;
+  uint32_t rec;
+};
+
+// Tile `item / NT`, checked against the pair count: a descriptor out of
+// range is not ok (the producer reports it) and every role skips it.
+__device__ __forceinline__ PItem item_of(const ExpertCallArgs &a, const int4 *ptiles, int item, int NT,
+                                         int n_rows) {
+  const int pt = item / NT;
+  const int4 d0 = ptiles[pt];
+  PItem it;
+  it.nt = item - pt * NT;
+  it.start = d0.y;
+  it.len = d0.z;
+  it.rec = 0;
+  it.ok = record_of(a, static_cast<uint32_t>(d0.x), it.rec) && it.start >= 0 && it.len >= 1 && it.len <= kPM &&
+          it.start <= n_rows - it.len;
+  return it;
+}
+
+// Every role walks the same item sequence (blockIdx.x, + gridDim.x, ...) and
+// skips the same bad items, so the rings stay in step.
 template <bool DUAL>
 __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a, GroupView gv,
-                                                               const int4 *__restrict__ ptiles,
-                                                               const int32_t *__restrict__ n_ptiles,
-                                                               const uint16_t *__restrict__ in,
+                                                               const int4 *ptiles, const int32_t *n_ptiles,
+                                                               int max_tiles, int n_rows,
+                                                               const __grid_constant__ CUtensorMap in_map,
                                                                uint16_t *__restrict__ out,
-                                                               const uint16_t *__restrict__ exp_tab,
+                                                               const uint16_t *__restrict__ silu_tab,
                                                                uint32_t *err) {
   extern __shared__ uint8_t psmem_raw[];
+  pdl_wait();
+  pdl_trigger();
   const uint32_t raw0 = smem_u32(psmem_raw);
   const uint32_t sbase = (raw0 + 1023u) & ~1023u;
   uint8_t *sm = psmem_raw + (sbase - raw0);
-  uint64_t *done = reinterpret_cast<uint64_t *>(sm + kOffBar);  // [2]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kOffBar + 16);
+  const uint32_t bars = sbase + kOffBar;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kOffMisc);
+  volatile uint32_t *dead = reinterpret_cast<volatile uint32_t *>(sm + kOffMisc + 4);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = DUAL ? a.H : a.I;
   const int O = DUAL ? a.I : a.H;
   const int NT = DUAL ? O / 128 : O / 256;
-  const int KT = K / 64;
   const int nblk = K / 256;
   const uint64_t rec_bytes = DUAL ? a.tiled.gate_up_record : a.tiled.down_record;
   const uint8_t *tbase = DUAL ? a.tiled.gate_up : a.tiled.down;
-  pdl_trigger();
-  pdl_wait();
-  const int n_items = n_ptiles[0] * NT;
+  const int n_items = min(n_ptiles[0], max_tiles) * NT;
   if (static_cast<int>(blockIdx.x) >= n_items) return;
 
   if (tid == 0) {
-    mbar_init(done + 0, 1);
-    mbar_init(done + 1, 1);
+    for (int i = 0; i < kBars; ++i) {
+      uint32_t count = 1;
+      if ((i >= kBarB && i < kBarB + kBStages) || (i >= kBarRE && i < kBarRE + kRawStages)) count = kDeqWarps;
+      if (i >= kBarCE && i < kBarCE + 2) count = kEpiWarps;
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bars + 8 * i), "r"(count));
+    }
+    *dead = 0u;
     mbar_init_fence();
   }
-  if (warp == 0) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
@@ -194,135 +269,224 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  uint32_t phase[2] = {0u, 0u};
-  bool dead = false;
 
-  const int r = tid >> 1, half = tid & 1;  // A gather: row r, chunks 4*half .. 4*half+3
-  const int n = tid, rg = n >> 4, side = (n >> 3) & 1, rr = n & 7;  // B row n of the item
-
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-    const int pt = item / NT, nt = item - pt * NT;
-    const int4 d0 = ptiles[pt];
-    const int start = d0.y, len = d0.z;
-    uint32_t rec = 0;
-    if (!record_of(a, static_cast<uint32_t>(d0.x), rec)) {
-      if (tid == 0) set_error(err, kErrBadRoute);
-      continue;
-    }
-    const uint8_t *arow = nullptr;
-    if (r < len) {
-      const int pair = gv.order[start + r];
-      const int row = DUAL ? pair_row(pair, a.n_pairs, a.slots) : pair;
-      arow = reinterpret_cast<const uint8_t *>(in + static_cast<size_t>(row) * K);
-    }
-    const uint8_t *brg = tbase + rec * rec_bytes + static_cast<size_t>(nt * 16 + rg) * nblk * kTileChunk;
-    auto issue = [&](int kt) {
-      const uint32_t as = sbase + kOffA + (kt % kARing) * kATile + r * 128;
-      if (arow != nullptr) {
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    uint32_t a_st = 0, a_ph = 0, r_st = 0, r_ph = 0;
+    bool live = true;
+    for (int item = blockIdx.x; item < n_items && live; item += gridDim.x) {
+      const PItem it = item_of(a, ptiles, item, NT, n_rows);
+      if (!it.ok) {
+        if (lane == 0) set_error(err, kErrBadTile);
+        continue;
+      }
+      int tok[4] = {0, 0, 0, 0};
+      if (DUAL) {
+        const int first = gv.order[it.start];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int j = 4 * half + q;
-          cp16s(as + ((j ^ (r & 7)) << 4), arow + kt * 128 + j * 16);
+        for (int j = 0; j < 4; ++j) {
+          const int m = 4 * lane + j;
+          int pair = m < it.len ? gv.order[it.start + m] : first;
+          if (pair < 0 || pair >= n_rows) {
+            set_error(err, kErrBadTile);
+            pair = 0;
+          }
+          tok[j] = pair_row(pair, a.n_pairs, a.slots);
         }
       }
-      const int blk = kt >> 2, h = (kt & 3) >> 1, i0 = 2 * (kt & 1);
-      const uint8_t *ch = brg + static_cast<size_t>(blk) * kTileChunk;
-      const uint32_t rs = sbase + kOffRaw + (kt % kRawRing) * kRawTile + n * kRawRow;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) cp8s(rs + c * 8, ch + h * 1024 + side * 512 + (rr * 4 + c) * 16 + i0 * 4);
-      cp4s(rs + 32, ch + kTileW + (side * 8 + rr) * 32 + (4 * h + i0) * 2);
-      cp4s(rs + 36, ch + kTileW + (side * 8 + rr) * 32 + 16 + (4 * h + i0) * 2);
-      cp_async_commit();
-    };
-
-    issue(0);
-    if (KT > 1) issue(1);
-    else cp_async_commit();  // two groups in flight before the first step, whatever KT
-    for (int kt = 0; kt < KT; ++kt) {
-      if (kt >= 2) bar_wait(done + (kt & 1), phase[kt & 1], dead, err);  // MMA(kt-2) is done
-      if (kt + 2 < KT) issue(kt + 2);
-      else cp_async_commit();  // keep one group per step
-      cp_async_wait<2>();
-      __syncthreads();  // the step's input rows and raw weights landed for every thread
-      {
-        const uint32_t rs = sbase + kOffRaw + (kt % kRawRing) * kRawTile + n * kRawRow;
-        const uint2 w01 = lds64(rs), w23 = lds64(rs + 8), w45 = lds64(rs + 16), w67 = lds64(rs + 24);
-        const uint2 sbw = lds64(rs + 32);
-        const uint32_t wd[4][2] = {{w01.x, w01.y}, {w23.x, w23.y}, {w45.x, w45.y}, {w67.x, w67.y}};
-        const uint32_t bs = sbase + kOffB + (kt & 1) * kBTile + n * 128;
-#pragma unroll
-        for (int gi = 0; gi < 2; ++gi) {
-          const uint32_t s16 = gi ? (sbw.x >> 16) : (sbw.x & 0xFFFFu);
-          const uint32_t b16 = gi ? (sbw.y >> 16) : (sbw.y & 0xFFFFu);
-          const uint32_t ss = s16 | (s16 << 16), bb = b16 | (b16 << 16);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 v = dequant_word(wd[c][gi], ss, bb);
-            const int j = 4 * gi + c;
-            sts128(bs + ((j ^ (n & 7)) << 4), v.x, v.y, v.z, v.w);
+      const uint8_t *brg = tbase + it.rec * rec_bytes + static_cast<size_t>(it.nt * 16) * nblk * kTileChunk;
+      for (int kb = 0; kb < nblk && live; ++kb) {
+        if (lane == 0) {
+          live = bar_wait(bars + 8 * (kBarRE + r_st), r_ph ^ 1u, dead, err);
+          if (live) mbar_expect_tx_u32(bars + 8 * (kBarR + r_st), kRawTile);
+        }
+        live = __shfl_sync(0xFFFFFFFFu, live, 0);
+        if (!live) break;
+        if (lane < 16)
+          bulk_g2s_u32(sbase + kOffRaw + r_st * kRawTile + lane * kTileChunk,
+                       brg + (static_cast<size_t>(lane) * nblk + kb) * kTileChunk, kTileChunk,
+                       bars + 8 * (kBarR + r_st));
+        if (++r_st == kRawStages) {
+          r_st = 0;
+          r_ph ^= 1u;
+        }
+        for (int ks = 0; ks < 4; ++ks) {
+          const int kt = kb * 4 + ks;
+          if (lane == 0) {
+            live = bar_wait(bars + 8 * (kBarAE + a_st), a_ph ^ 1u, dead, err);
+            if (live) mbar_expect_tx_u32(bars + 8 * (kBarA + a_st), kATile);
+          }
+          live = __shfl_sync(0xFFFFFFFFu, live, 0);
+          if (!live) break;
+          const uint32_t dst = sbase + kOffA + a_st * kATile;
+          if (DUAL) {
+            tma_gather4(dst + lane * 512, &in_map, kt * 64, tok[0], tok[1], tok[2], tok[3], bars + 8 * (kBarA + a_st));
+          } else if (lane == 0) {
+            tma_tile2d(dst, &in_map, kt * 64, it.start, bars + 8 * (kBarA + a_st));
+          }
+          if (++a_st == kAStages) {
+            a_st = 0;
+            a_ph ^= 1u;
           }
         }
       }
-      fence_proxy_async();  // generic-proxy tile writes (cp.async, st.shared) -> tensor-core reads
-      __syncthreads();
-      if (tid == 0) {
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t a_st = 0, a_ph = 0, b_st = 0, b_ph = 0;
+      int n = 0;
+      bool live = true;
+      for (int item = blockIdx.x; item < n_items && live; item += gridDim.x) {
+        const PItem it = item_of(a, ptiles, item, NT, n_rows);
+        if (!it.ok) continue;
+        const uint32_t acc = n & 1, acc_ph = (n >> 1) & 1;
+        ++n;
+        if (!bar_wait(bars + 8 * (kBarCE + acc), acc_ph ^ 1u, dead, err)) break;
         tc_fence_after();
-        const uint64_t ad = sw128_desc(sbase + kOffA + (kt % kARing) * kATile);
-        const uint64_t bd = sw128_desc(sbase + kOffB + (kt & 1) * kBTile);
+        const uint32_t d = tmem + acc * 256;
+        for (int kt = 0; kt < 4 * nblk; ++kt) {
+          live = bar_wait(bars + 8 * (kBarA + a_st), a_ph, dead, err) &&
+                 bar_wait(bars + 8 * (kBarB + b_st), b_ph, dead, err);
+          if (!live) break;
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(sbase + kOffA + a_st * kATile);
+          const uint64_t bd = sw128_desc(sbase + kOffB + b_st * kBTile);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, (kt | kk) != 0 ? 1u : 0u);
-        umma_commit(done + (kt & 1));
+          for (int kk = 0; kk < 4; ++kk) umma_bf16(d, ad + 2 * kk, bd + 2 * kk, (kt | kk) != 0 ? 1u : 0u);
+          umma_commit(bars + 8 * (kBarAE + a_st));
+          umma_commit(bars + 8 * (kBarBE + b_st));
+          if (++a_st == kAStages) {
+            a_st = 0;
+            a_ph ^= 1u;
+          }
+          if (++b_st == kBStages) {
+            b_st = 0;
+            b_ph ^= 1u;
+          }
+        }
+        if (live) umma_commit(bars + 8 * (kBarC + acc));
       }
     }
-    // all MMAs of the item complete (the last two commits)
-    if (KT >= 2) bar_wait(done + (KT & 1), phase[KT & 1], dead, err);
-    bar_wait(done + ((KT - 1) & 1), phase[(KT - 1) & 1], dead, err);
-    tc_fence_after();
-    {
-      const int lb = 32 * (warp & 3);
-      const int m = lb + lane;  // pair row of the tile
-      int pair = -1;
-      if (m < len) pair = gv.order[start + m];
+  } else if (warp < kEpiWarp0) {
+    // ---------------- dequantisation ----------------
+    const int dw = warp - kDeqWarp0;
+    const int r = lane >> 2, c = lane & 3;
+    uint32_t b_st = 0, b_ph = 0, r_st = 0, r_ph = 0;
+    bool live = true;
+    for (int item = blockIdx.x; item < n_items && live; item += gridDim.x) {
+      const PItem it = item_of(a, ptiles, item, NT, n_rows);
+      if (!it.ok) continue;
+      for (int kb = 0; kb < nblk && live; ++kb) {
+        live = bar_wait(bars + 8 * (kBarR + r_st), r_ph, dead, err);
+        if (!live) break;
+        const uint32_t raw = sbase + kOffRaw + r_st * kRawTile;
+        for (int ks = 0; ks < 4; ++ks) {
+          live = bar_wait(bars + 8 * (kBarBE + b_st), b_ph ^ 1u, dead, err);
+          if (!live) break;
+          const int h = ks >> 1, i0 = 2 * (ks & 1);
+          const uint32_t bt = sbase + kOffB + b_st * kBTile;
+#pragma unroll
+          for (int task = 0; task < 4; ++task) {
+            const int wt = dw * 4 + task;
+            const int rg = wt >> 1, side = wt & 1;
+            const uint32_t ch = raw + rg * kTileChunk;
+            const uint2 w2 = lds64(ch + h * 1024 + side * 512 + (r * 4 + c) * 16 + i0 * 4);
+            const uint32_t sbo = ch + kTileW + (side * 8 + r) * 32 + (4 * h + i0) * 2;
+            const uint32_t sc = lds32(sbo), bi = lds32(sbo + 16);
+            const int n = rg * 16 + side * 8 + r;
+#pragma unroll
+            for (int gi = 0; gi < 2; ++gi) {
+              const uint32_t ss = prmt(sc, 0u, gi ? 0x3232u : 0x1010u);
+              const uint32_t bb = prmt(bi, 0u, gi ? 0x3232u : 0x1010u);
+              const uint4 v = dequant_word(gi ? w2.y : w2.x, ss, bb);
+              const int j = 4 * gi + c;
+              sts128(bt + n * 128 + ((j ^ r) << 4), v);
+            }
+          }
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bars + 8 * (kBarB + b_st));
+          if (++b_st == kBStages) {
+            b_st = 0;
+            b_ph ^= 1u;
+          }
+        }
+        fence_proxy_async();  // generic reads of the raw stage before the next bulk copy into it
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bars + 8 * (kBarRE + r_st));
+        if (++r_st == kRawStages) {
+          r_st = 0;
+          r_ph ^= 1u;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 belong to this warp
+    const int m = 32 * quarter + lane;
+    int n = 0;
+    bool live = true;
+    for (int item = blockIdx.x; item < n_items && live; item += gridDim.x) {
+      const PItem it = item_of(a, ptiles, item, NT, n_rows);
+      if (!it.ok) continue;
+      const uint32_t acc = n & 1, acc_ph = (n >> 1) & 1;
+      ++n;
+      live = bar_wait(bars + 8 * (kBarC + acc), acc_ph, dead, err);
+      if (!live) break;
+      tc_fence_after();
+      bool valid = m < it.len;
+      int row_i = 0;
+      if (valid) row_i = DUAL ? it.start + m : gv.order[it.start + m];
+      if (valid && (row_i < 0 || row_i >= n_rows)) {
+        set_error(err, kErrBadTile);
+        valid = false;
+      }
+      const size_t row = static_cast<size_t>(row_i);
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + acc * 256;
 #pragma unroll 1
-      for (int qq = 0; qq < 4; ++qq) {
-        const int q = (warp >> 2) * 4 + qq;  // 32-column chunk
+      for (int cc = 0; cc < 8; ++cc) {
         uint32_t v[32];
         __syncwarp();
-        tmem_ld32(tmem + (static_cast<uint32_t>(lb) << 16) + 32 * q, v);
-        if (pair >= 0 && DUAL) {
+        tmem_ld32(taddr + 32 * cc, v);
+        if (valid && DUAL) {
+          // columns: [gate rg 2cc, rows 0-7][up rg 2cc][gate rg 2cc+1][up rg 2cc+1]
           uint32_t o[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            // columns: [gate rg=2q r0-7][up rg=2q][gate rg=2q+1][up rg=2q+1]
             const int base = (j < 4) ? 0 : 16;
             const int jj = 2 * (j & 3);
-            const float g0 = round_bf16(__uint_as_float(v[base + jj])), u0 = round_bf16(__uint_as_float(v[base + 8 + jj]));
-            const float g1 = round_bf16(__uint_as_float(v[base + jj + 1]));
-            const float u1 = round_bf16(__uint_as_float(v[base + 8 + jj + 1]));
-            o[j] = static_cast<uint32_t>(f32_to_bf16(swiglu_bf16(exp_tab, g0, u0))) |
-                   (static_cast<uint32_t>(f32_to_bf16(swiglu_bf16(exp_tab, g1, u1))) << 16);
+            float r2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const uint16_t g = f32_to_bf16(__uint_as_float(v[base + jj + e]));
+              const float u = round_bf16(__uint_as_float(v[base + 8 + jj + e]));
+              r2[e] = bmul(bf16_to_f32(silu_tab[g]), u);
+            }
+            o[j] = static_cast<uint32_t>(f32_to_bf16(r2[0])) | (static_cast<uint32_t>(f32_to_bf16(r2[1])) << 16);
           }
-          uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<size_t>(pair) * O + nt * 128 + 16 * q);
+          uint4 *dst = reinterpret_cast<uint4 *>(out + row * O + it.nt * 128 + 16 * cc);
           dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
           dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-        } else if (pair >= 0) {
+        } else if (valid) {
           uint32_t o[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j)
             o[j] = static_cast<uint32_t>(f32_to_bf16(__uint_as_float(v[2 * j]))) |
                    (static_cast<uint32_t>(f32_to_bf16(__uint_as_float(v[2 * j + 1]))) << 16);
-          uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<size_t>(pair) * O + nt * 256 + 32 * q);
+          uint4 *dst = reinterpret_cast<uint4 *>(out + row * O + it.nt * 256 + 32 * cc);
 #pragma unroll
           for (int j = 0; j < 4; ++j) dst[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars + 8 * (kBarCE + acc));
     }
-    tc_fence_before();
-    __syncthreads();  // TMEM reads are done before the next item's MMAs overwrite the accumulators
-    tc_fence_after();
   }
+  tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
   }
@@ -331,8 +495,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
 // 128-pair tiles of every bin from the grouping counts and offsets (one CTA).
 __global__ void __launch_bounds__(1024) k_prefill_tiles(GroupView gv, int4 *ptiles, int32_t *n_ptiles,
                                                         int max_tiles) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   __shared__ int warp_sums[32];
   __shared__ int total;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -370,6 +534,38 @@ __global__ void __launch_bounds__(1024) k_prefill_tiles(GroupView gv, int4 *ptil
   if (tid == 0) n_ptiles[0] = min(total, max_tiles);
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 matrix [rows][cols] (row pitch cols), 128B swizzle, box 64 x box_rows.
+cudaError_t make_map(CUtensorMap *map, const void *base, int rows, int cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 }  // namespace
 
 bool prefill_supported(const ExpertCallArgs &a) {
@@ -386,27 +582,32 @@ cudaError_t launch_prefill_tiles(const GroupView &gv, int4 *ptiles, int32_t *n_p
 }
 
 cudaError_t launch_prefill_gemm(bool dual, const ExpertCallArgs &a, const GroupView &gv, const int4 *ptiles,
-                                const int32_t *n_ptiles, int max_tiles, const uint16_t *in, uint16_t *out,
-                                cudaStream_t s) {
+                                const int32_t *n_ptiles, int max_tiles, const uint16_t *in, int in_rows,
+                                uint16_t *out, cudaStream_t s) {
+  if (reinterpret_cast<uintptr_t>(in) % 16 != 0) return cudaErrorMisalignedAddress;
   const uint16_t *tab = nullptr;
-  cudaError_t e = exp_table_address(&tab);
+  cudaError_t e = silu_table_address(&tab);
   if (e != cudaSuccess) return e;
+  CUtensorMap map;
+  e = make_map(&map, in, in_rows, dual ? a.H : a.I, dual ? 1 : kPM);
+  if (e != cudaSuccess) return e;
+  // pairs (grouped rows) of the layer: tokens * slots routed + one per token for the shared expert
+  const int n_rows = a.n_pairs + (a.tiled.has_shared ? a.tokens : 0);
   const DeviceInfo di = device_info();
   const int nt = dual ? a.I / 128 : a.H / 256;
   const int grid = std::max(1, std::min(di.sms, max_tiles * nt));
   if (dual) {
     e = cudaFuncSetAttribute(k_prefill_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(k_prefill_gemm<true>, grid, kPThreads, kPSmem, s, a, gv, ptiles, n_ptiles, in, out, tab,
-                   device_error_word());
-    if (e != cudaSuccess) return e;
+    e = launch_pdl(k_prefill_gemm<true>, grid, kPThreads, kPSmem, s, a, gv, ptiles, n_ptiles, max_tiles, n_rows, map,
+                   out, tab, device_error_word());
   } else {
     e = cudaFuncSetAttribute(k_prefill_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(k_prefill_gemm<false>, grid, kPThreads, kPSmem, s, a, gv, ptiles, n_ptiles, in, out, tab,
-                   device_error_word());
-    if (e != cudaSuccess) return e;
+    e = launch_pdl(k_prefill_gemm<false>, grid, kPThreads, kPSmem, s, a, gv, ptiles, n_ptiles, max_tiles, n_rows,
+                   map, out, tab, device_error_word());
   }
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
