@@ -598,6 +598,17 @@ int validate_layer(const FnMoELayerArgs *a) {
   return FNMOE_OK;
 }
 
+// Whether fnmoe_moe_layer runs the tcgen05 prefill GEMMs for these arguments
+// (the same test as prefill_supported on the resolved call, plus the flags
+// and the pair-count threshold).
+bool layer_prefill(const FnMoELayerArgs *a) {
+  const bool supported = a->tiled.gate_up != nullptr && a->tiled.down != nullptr && a->group_size == 32 &&
+                         a->hidden_size % 256 == 0 && a->inter_size % 256 == 0;
+  const uint64_t n_total = static_cast<uint64_t>(a->tokens) * a->top_k + (a->shared_inter_size ? a->tokens : 0);
+  return supported && (a->flags & FNMOE_LAYER_FORCE_DECODE) == 0 &&
+         ((a->flags & FNMOE_LAYER_FORCE_PREFILL) != 0 || n_total >= FNMOE_PREFILL_PAIRS);
+}
+
 struct LayerLayout {
   Layout core;
   uint16_t *logits, *shared_logit, *shared_gate, *scores, *mass;
@@ -605,6 +616,7 @@ struct LayerLayout {
   int4 *ptiles;        // 128-pair tiles of the prefill path
   int32_t *n_ptiles;
   int max_ptiles;
+  uint16_t *xg;        // prefill: x rows gathered into bin order [n_total][H]
 };
 
 uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL) {
@@ -628,6 +640,7 @@ uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL) {
   LL.max_ptiles = prefill_max_tiles(n_total, n_bins);
   LL.ptiles = cv.take<int4>(static_cast<uint64_t>(LL.max_ptiles));
   LL.n_ptiles = cv.take<int32_t>(4);
+  LL.xg = layer_prefill(a) ? cv.take<uint16_t>(static_cast<uint64_t>(n_total) * a->hidden_size) : nullptr;
   return cv.off + 256;
 }
 
@@ -695,8 +708,7 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
   if (int rc = check_expert_alignment(call)) return rc;
 
   const int n_total_pairs = n_pairs + (shared ? T : 0);
-  bool prefill = prefill_supported(call) && (a->flags & FNMOE_LAYER_FORCE_DECODE) == 0 &&
-                 ((a->flags & FNMOE_LAYER_FORCE_PREFILL) != 0 || n_total_pairs >= static_cast<int>(FNMOE_PREFILL_PAIRS));
+  const bool prefill = prefill_supported(call) && layer_prefill(a);
   if ((a->flags & FNMOE_LAYER_FORCE_PREFILL) && !prefill_supported(call))
     return fail(FNMOE_ERR_UNSUPPORTED,
                 "the prefill path needs tiled tables, group size 32 and hidden/inter multiples of 256");
@@ -748,9 +760,14 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
     }
     if (e != cudaSuccess) return cuda_fail(e, "prefill tiles");
     {
+      Prof p("gather_rows", s);
+      e = launch_prefill_gather(call, L.gv, static_cast<const uint16_t *>(a->x), LL.xg, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "prefill gather");
+    {
       Prof p("gate_up", s);
-      e = launch_prefill_gemm(true, call, L.gv, LL.ptiles, LL.n_ptiles, LL.max_ptiles,
-                              static_cast<const uint16_t *>(a->x), T, L.act, s);
+      e = launch_prefill_gemm(true, call, L.gv, LL.ptiles, LL.n_ptiles, LL.max_ptiles, LL.xg, n_total_pairs,
+                              L.act, s);
     }
     if (e != cudaSuccess) return cuda_fail(e, "prefill gate_up");
     {

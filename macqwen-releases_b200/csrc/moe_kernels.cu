@@ -1517,6 +1517,110 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
   }
 }
 
+// Router logits for many tokens: a CTA tile of 32 router rows x 16 tokens,
+// H streamed in 256-wide rounds through double-buffered bf16 shared memory
+// (cp.async, coherent L2 loads).  Warp w owns rows 8*(w&3).. and tokens
+// 8*(w>>2)..; lane j runs the canonical chains of those 8 x 8 (row, token)
+// pairs -- chunk 32*round + j, elements in increasing h, from -0.0 -- then
+// the same xor butterfly as k_router_logits, so logits are bit-identical.
+constexpr int kRtRows = 32, kRtTok = 16, kRtRound = 256;
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float (&f)[8]) {
+  f[0] = __uint_as_float(u.x << 16);
+  f[1] = __uint_as_float(u.x & 0xFFFF0000u);
+  f[2] = __uint_as_float(u.y << 16);
+  f[3] = __uint_as_float(u.y & 0xFFFF0000u);
+  f[4] = __uint_as_float(u.z << 16);
+  f[5] = __uint_as_float(u.z & 0xFFFF0000u);
+  f[6] = __uint_as_float(u.w << 16);
+  f[7] = __uint_as_float(u.w & 0xFFFF0000u);
+}
+
+__global__ void __launch_bounds__(256) k_router_tiled(const uint16_t *x, const uint16_t *__restrict__ W, int T,
+                                                      int H, int E, const uint16_t *__restrict__ wsg,
+                                                      uint16_t *logits, uint16_t *shared_logit) {
+  __shared__ __align__(16) uint16_t sw[2][kRtRows][kRtRound];
+  __shared__ __align__(16) uint16_t sx[2][kRtTok][kRtRound];
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rows = E + (wsg != nullptr ? 1 : 0);
+  const int r0 = blockIdx.x * kRtRows, t0 = blockIdx.y * kRtTok;
+  const int nchunks = H / 8;
+  const int nrounds = (nchunks + 31) / 32;
+  const int wr = 8 * (warp & 3), wt = 8 * (warp >> 2);
+  auto stage = [&](int m, int b) {
+    // 32 rows x 32 chunks of W and 16 tokens x 32 chunks of x, 16 bytes each
+    for (int i = tid; i < (kRtRows + kRtTok) * 32; i += 256) {
+      const int rr = i >> 5, c = i & 31;
+      const int h = (32 * m + c) * 8;
+      const uint16_t *src = nullptr;
+      uint16_t *dst;
+      if (rr < kRtRows) {
+        const int row = r0 + rr;
+        src = row < E ? W + static_cast<size_t>(row) * H : (row < rows ? wsg : nullptr);
+        dst = &sw[b][rr][c * 8];
+      } else {
+        const int t = t0 + rr - kRtRows;
+        src = t < T ? x + static_cast<size_t>(t) * H : nullptr;
+        dst = &sx[b][rr - kRtRows][c * 8];
+      }
+      if (src != nullptr && h < H) cp_async16(dst, src + h);
+    }
+    cp_async_commit();
+  };
+  float acc[8][8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int t = 0; t < 8; ++t) acc[r][t] = -0.0f;
+  stage(0, 0);
+  for (int m = 0; m < nrounds; ++m) {
+    if (m + 1 < nrounds) stage(m + 1, (m + 1) & 1);
+    else cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const int b = m & 1;
+    if (32 * m + lane < nchunks) {
+      // this lane's chunk of the 8 tokens as float32, then per router row its
+      // chunk and 64 FMAs: every (row, token) chain takes the chunk's 8
+      // elements in increasing h
+      float xf[8][8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) bf16x8_to_f32(*reinterpret_cast<const uint4 *>(&sx[b][wt + t][lane * 8]), xf[t]);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        float wf[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4 *>(&sw[b][wr + r][lane * 8]), wf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int t = 0; t < 8; ++t) acc[r][t] = __fmaf_rn(wf[i], xf[t][i], acc[r][t]);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) acc[r][t] = __fadd_rn(acc[r][t], __shfl_xor_sync(0xFFFFFFFFu, acc[r][t], off));
+  // every lane holds every sum; spread the 64 stores over the lanes
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int row = r0 + wr + r;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const int tok = t0 + wt + t;
+      if (lane == ((r * 8 + t) & 31) && row < rows && tok < T) {
+        if (row < E) logits[static_cast<size_t>(tok) * E + row] = f32_to_bf16(acc[r][t]);
+        else shared_logit[tok] = f32_to_bf16(acc[r][t]);
+      }
+    }
+  }
+}
+
 template <int CH, int RW, int TOK, int NW = 8>
 cudaError_t launch_router_cfg(const uint16_t *x, const uint16_t *W, int T, int H, int E,
                               const uint16_t *w_shared_gate, uint16_t *logits, uint16_t *shared_logit,
@@ -1539,6 +1643,13 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
                                  const uint16_t *w_shared_gate, uint16_t *logits,
                                  uint16_t *shared_logit, cudaStream_t s) {
   const int ch = (H / 8 + 31) / 32;
+  if (T >= 64 && H % 8 == 0) {
+    const int rows = E + (w_shared_gate ? 1 : 0);
+    const dim3 grid((rows + kRtRows - 1) / kRtRows, (T + kRtTok - 1) / kRtTok);
+    cudaError_t e = launch_pdl(k_router_tiled, grid, 256, 0, s, x, W, T, H, E, w_shared_gate, logits, shared_logit);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+  }
   // Small batches: one router row per warp and 4-warp CTAs, so ~E/4 CTAs
   // share the weight read instead of E/16.
   if (T <= 4) {

@@ -145,9 +145,12 @@ bool prefill_supported(const ExpertCallArgs &a);
 int prefill_max_tiles(int n_total, int n_bins);
 cudaError_t launch_prefill_tiles(const GroupView &gv, int4 *ptiles, int32_t *n_ptiles, int max_tiles,
                                  cudaStream_t s);
-// Prefill grouped GEMM on tcgen05: gate/up (dual) reads token rows of x
-// ([in_rows = tokens][H]) and writes SwiGLU activations in bin order
-// ([n_total][I], row = position in gv.order); down reads those ([in_rows =
+// Token rows of x gathered into bin order: dst [n_total][H], row p = x row of pair gv.order[p].
+cudaError_t launch_prefill_gather(const ExpertCallArgs &a, const GroupView &gv, const uint16_t *x, uint16_t *dst,
+                                  cudaStream_t s);
+// Prefill grouped GEMM on tcgen05, inputs and activations in bin order:
+// gate/up (dual) reads the gathered x rows ([in_rows = n_total][H]) and
+// writes SwiGLU activations ([n_total][I]); down reads those ([in_rows =
 // n_total][I]) and writes per-pair outputs ([n_total][H]).
 cudaError_t launch_prefill_gemm(bool dual, const ExpertCallArgs &a, const GroupView &gv, const int4 *ptiles,
                                 const int32_t *n_ptiles, int max_tiles, const uint16_t *in, int in_rows,

@@ -9,20 +9,22 @@
 //
 //   warp 0      producer: per 256-wide K block one bulk copy per row group
 //               (the 2560-byte chunks of the tiled tables) into a raw ring;
-//               per 64-wide k-step the 128 input rows into a 128B-swizzled
-//               K-major tile by TMA -- tile::gather4 of token rows of x for
-//               gate/up, a plain 2D tile of the bin-sorted activations for
-//               down;
+//               per 64-wide k-step the tile's 128 input rows as one
+//               128B-swizzled K-major TMA box -- the inputs are in bin order
+//               (x rows gathered by k_gather_rows for gate/up, the bin-ordered
+//               activations for down), so a tile's rows are contiguous;
 //   warp 1      MMA issuer: 4 tcgen05.mma (kind::f16, bf16, M128 N256 K16)
 //               per k-step into one of two 256-column fp32 accumulators in
 //               TMEM, commits releasing the input stages;
-//   warps 2-9   dequantise the raw ring into bf16 swizzled weight tiles,
+//   warps 2-17  dequantise the raw ring into bf16 swizzled weight tiles,
 //               bf16(s*q + b) with one rounding (fma.rn.bf16x2), the
 //               reference's dequant rule;
-//   warps 10-13 epilogue: tcgen05.ld of the finished accumulator, then bf16
+//   warps 18-25 epilogue (two warps per TMEM lane quarter, half the columns
+//               each): tcgen05.ld of the finished accumulator, then bf16
 //               SwiGLU activations in bin order (gate/up) or bf16 per-pair
 //               outputs (down), while the MMAs of the next item fill the
-//               other accumulator.
+//               other accumulator.  g*sigmoid(g) comes from a shared-memory
+//               slice of the bit-identical table for |g| in [2^-9, 2^7).
 //
 // Accumulation is float32 in the tensor core's order, so results match the
 // exact decode path within float32 rounding, not bit for bit.  Every wait is
@@ -46,17 +48,20 @@ namespace {
 
 constexpr int kPM = 128;  // pairs per tile (MMA M)
 constexpr int kPN = 256;  // output rows per item (MMA N)
-constexpr int kDeqWarps = 8, kEpiWarps = 4;
+constexpr int kDeqWarps = 16, kEpiWarps = 8;
 constexpr int kDeqWarp0 = 2, kEpiWarp0 = kDeqWarp0 + kDeqWarps;
-constexpr int kPThreads = 32 * (kEpiWarp0 + kEpiWarps);  // 448
+constexpr int kPThreads = 32 * (kEpiWarp0 + kEpiWarps);  // 832
 constexpr int kAStages = 4, kBStages = 2, kRawStages = 2;
 constexpr int kATile = kPM * 128;           // 128 rows x 64 bf16
 constexpr int kBTile = kPN * 128;           // 256 rows x 64 bf16
 constexpr int kRawTile = 16 * kTileChunk;   // 16 row groups x one 256-wide K block
+constexpr int kSiluLo = 118, kSiluExps = 16;  // bf16 exponents 118..133: |g| in [2^-9, 2^7)
+constexpr int kSiluEntries = 2 * kSiluExps * 128;
 constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + kAStages * kATile;
 constexpr int kOffRaw = kOffB + kBStages * kBTile;
-constexpr int kOffBar = kOffRaw + kRawStages * kRawTile;
+constexpr int kOffSilu = kOffRaw + kRawStages * kRawTile;
+constexpr int kOffBar = kOffSilu + kSiluEntries * 2;
 // barriers: a_full[4] a_empty[4] b_full[2] b_empty[2] raw_full[2] raw_empty[2] acc_full[2] acc_empty[2]
 constexpr int kBarA = 0, kBarAE = kBarA + kAStages, kBarB = kBarAE + kAStages, kBarBE = kBarB + kBStages;
 constexpr int kBarR = kBarBE + kBStages, kBarRE = kBarR + kRawStages, kBarC = kBarRE + kRawStages,
@@ -101,15 +106,6 @@ __device__ __forceinline__ void bulk_g2s_u32(uint32_t dst, const void *src, uint
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(bar)
                : "memory");
-}
-// Four rows (y0..y3) of 64 bf16 starting at column x, 128B-swizzled into 512 bytes at dst.
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, int x, int y0, int y1, int y2,
-                                            int y3, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(bar)
-      : "memory");
 }
 // A 64 x 128 box (64 bf16 of 128 rows from row y), 128B-swizzled.
 __device__ __forceinline__ void tma_tile2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
@@ -265,6 +261,11 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
   }
+  uint16_t *s_silu = reinterpret_cast<uint16_t *>(sm + kOffSilu);
+  for (int i = tid; i < kSiluEntries; i += blockDim.x) {
+    const int sign = i / (kSiluExps * 128), rest = i - sign * (kSiluExps * 128);
+    s_silu[i] = silu_tab[(sign << 15) | ((kSiluLo + (rest >> 7)) << 7) | (rest & 127)];
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -279,20 +280,6 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
       if (!it.ok) {
         if (lane == 0) set_error(err, kErrBadTile);
         continue;
-      }
-      int tok[4] = {0, 0, 0, 0};
-      if (DUAL) {
-        const int first = gv.order[it.start];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int m = 4 * lane + j;
-          int pair = m < it.len ? gv.order[it.start + m] : first;
-          if (pair < 0 || pair >= n_rows) {
-            set_error(err, kErrBadTile);
-            pair = 0;
-          }
-          tok[j] = pair_row(pair, a.n_pairs, a.slots);
-        }
       }
       const uint8_t *brg = tbase + it.rec * rec_bytes + static_cast<size_t>(it.nt * 16) * nblk * kTileChunk;
       for (int kb = 0; kb < nblk && live; ++kb) {
@@ -318,12 +305,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
           }
           live = __shfl_sync(0xFFFFFFFFu, live, 0);
           if (!live) break;
-          const uint32_t dst = sbase + kOffA + a_st * kATile;
-          if (DUAL) {
-            tma_gather4(dst + lane * 512, &in_map, kt * 64, tok[0], tok[1], tok[2], tok[3], bars + 8 * (kBarA + a_st));
-          } else if (lane == 0) {
-            tma_tile2d(dst, &in_map, kt * 64, it.start, bars + 8 * (kBarA + a_st));
-          }
+          if (lane == 0) tma_tile2d(sbase + kOffA + a_st * kATile, &in_map, kt * 64, it.start, bars + 8 * (kBarA + a_st));
           if (++a_st == kAStages) {
             a_st = 0;
             a_ph ^= 1u;
@@ -387,8 +369,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
           const int h = ks >> 1, i0 = 2 * (ks & 1);
           const uint32_t bt = sbase + kOffB + b_st * kBTile;
 #pragma unroll
-          for (int task = 0; task < 4; ++task) {
-            const int wt = dw * 4 + task;
+          for (int task = 0; task < 32 / kDeqWarps; ++task) {
+            const int wt = dw * (32 / kDeqWarps) + task;
             const int rg = wt >> 1, side = wt & 1;
             const uint32_t ch = raw + rg * kTileChunk;
             const uint2 w2 = lds64(ch + h * 1024 + side * 512 + (r * 4 + c) * 16 + i0 * 4);
@@ -425,6 +407,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
     // ---------------- epilogue ----------------
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 belong to this warp
     const int m = 32 * quarter + lane;
+    const int cc0 = ((warp - kEpiWarp0) >> 2) * 4;  // this warp's four 32-column chunks
     int n = 0;
     bool live = true;
     for (int item = blockIdx.x; item < n_items && live; item += gridDim.x) {
@@ -445,7 +428,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
       const size_t row = static_cast<size_t>(row_i);
       const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + acc * 256;
 #pragma unroll 1
-      for (int cc = 0; cc < 8; ++cc) {
+      for (int cc = cc0; cc < cc0 + 4; ++cc) {
         uint32_t v[32];
         __syncwarp();
         tmem_ld32(taddr + 32 * cc, v);
@@ -459,9 +442,13 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
             float r2[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const uint16_t g = f32_to_bf16(__uint_as_float(v[base + jj + e]));
+              const uint32_t g = f32_to_bf16(__uint_as_float(v[base + jj + e]));
               const float u = round_bf16(__uint_as_float(v[base + 8 + jj + e]));
-              r2[e] = bmul(bf16_to_f32(silu_tab[g]), u);
+              const uint32_t ex = ((g >> 7) & 0xFFu) - static_cast<uint32_t>(kSiluLo);
+              const uint16_t sv = ex < static_cast<uint32_t>(kSiluExps)
+                                      ? s_silu[((g >> 15) << 11) | (ex << 7) | (g & 127u)]
+                                      : silu_tab[g];
+              r2[e] = bmul(bf16_to_f32(sv), u);
             }
             o[j] = static_cast<uint32_t>(f32_to_bf16(r2[0])) | (static_cast<uint32_t>(f32_to_bf16(r2[1])) << 16);
           }
@@ -490,6 +477,26 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
   }
+}
+
+// Input rows of the gate/up GEMM in bin order: row p of `dst` is the token
+// row of pair order[p] (one warp per row, 16-byte copies).
+__global__ void __launch_bounds__(256) k_gather_rows(const int32_t *order, int n_rows, int n_pairs, int slots,
+                                                     int n_tokens, const uint16_t *x, int H, uint16_t *dst,
+                                                     uint32_t *err) {
+  pdl_wait();
+  pdl_trigger();
+  const int p = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (p >= n_rows) return;
+  const int pair = order[p];
+  int t = (pair >= 0 && pair < n_rows) ? pair_row(pair, n_pairs, slots) : -1;
+  if (t < 0 || t >= n_tokens) {
+    if (lane == 0) set_error(err, kErrBadTile);
+    t = 0;
+  }
+  const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t) * H);
+  uint4 *d = reinterpret_cast<uint4 *>(dst + static_cast<size_t>(p) * H);
+  for (int i = lane; i < H / 8; i += 32) d[i] = src[i];
 }
 
 // 128-pair tiles of every bin from the grouping counts and offsets (one CTA).
@@ -581,6 +588,16 @@ cudaError_t launch_prefill_tiles(const GroupView &gv, int4 *ptiles, int32_t *n_p
   return cudaGetLastError();
 }
 
+cudaError_t launch_prefill_gather(const ExpertCallArgs &a, const GroupView &gv, const uint16_t *x, uint16_t *dst,
+                                  cudaStream_t s) {
+  const int n_rows = a.n_pairs + (a.tiled.has_shared ? a.tokens : 0);
+  if (a.H % 8 != 0) return cudaErrorInvalidValue;
+  cudaError_t e = launch_pdl(k_gather_rows, (n_rows + 7) / 8, 256, 0, s, gv.order, n_rows, a.n_pairs, a.slots,
+                             a.tokens, x, a.H, dst, device_error_word());
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 cudaError_t launch_prefill_gemm(bool dual, const ExpertCallArgs &a, const GroupView &gv, const int4 *ptiles,
                                 const int32_t *n_ptiles, int max_tiles, const uint16_t *in, int in_rows,
                                 uint16_t *out, cudaStream_t s) {
@@ -589,7 +606,7 @@ cudaError_t launch_prefill_gemm(bool dual, const ExpertCallArgs &a, const GroupV
   cudaError_t e = silu_table_address(&tab);
   if (e != cudaSuccess) return e;
   CUtensorMap map;
-  e = make_map(&map, in, in_rows, dual ? a.H : a.I, dual ? 1 : kPM);
+  e = make_map(&map, in, in_rows, dual ? a.H : a.I, kPM);
   if (e != cudaSuccess) return e;
   // pairs (grouped rows) of the layer: tokens * slots routed + one per token for the shared expert
   const int n_rows = a.n_pairs + (a.tiled.has_shared ? a.tokens : 0);

@@ -111,7 +111,8 @@ def test_weighted_combine_known_answer_on_gpu(golden):
 
 
 @pytest.mark.parametrize("tokens,hidden,experts,zipf", [(1, 2048, 512, None), (64, 2048, 512, 1.1),
-                                                        (5, 3072, 512, None), (3, 256, 40, None)])
+                                                        (5, 3072, 512, None), (3, 256, 40, None),
+                                                        (100, 2176, 40, None), (70, 3072, 512, None)])
 def test_router_topk_bit_exact(cuda_lib, tokens, hidden, experts, zipf):
     from flashnext_b200 import router, synthetic
     if zipf:
