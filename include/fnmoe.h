@@ -46,7 +46,7 @@ extern "C" {
 #define FNMOE_API
 #endif
 
-#define FNMOE_ABI_VERSION 3u
+#define FNMOE_ABI_VERSION 4u
 
 /* Size of the library-owned scratch used by fnmoe_moe_execute_static. */
 #define FNMOE_STATIC_SCRATCH_BYTES (16ull << 20)
@@ -356,7 +356,9 @@ FNMOE_API int fnmoe_paged_decode_workspace_size(const FnPagedArgs *args, uint64_
 FNMOE_API int fnmoe_paged_decode(const FnPagedArgs *args, void *stream);
 
 /* Device error word of the library: bit 0 = an out-of-range route was
- * skipped, bit 1 = a non-finite activation reached the fixed-point stage.
+ * skipped, bit 1 = a non-finite activation reached the fixed-point stage,
+ * bit 2 = a bounded wait in a kernel gave up (its outputs are invalid),
+ * bit 3 = an out-of-range prefill tile descriptor was skipped.
  * Reading synchronises the device; `clear` resets it. */
 FNMOE_API int fnmoe_read_device_errors(uint32_t *flags, int clear);
 

@@ -13,7 +13,7 @@ import threading
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libfnmoe.so"
-ABI_VERSION = 3
+ABI_VERSION = 4
 STATIC_SCRATCH_BYTES = 16 << 20
 
 OK = 0
