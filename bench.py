@@ -457,17 +457,44 @@ def ep_arm(args):
         L = synthetic.moe_layer(tokens * world, HIDDEN, INTER, EXPERTS, TOP_K, GROUP, zipf=1.1, seed=17 + 101 * i)
         local_bank = {n: tuple(t[rank * per:(rank + 1) * per].contiguous() for t in v) for n, v in L.experts.items()}
         backend = CudaBackend(L.router_weight, local_bank, L.shared, L.shared_expert_gate, top_k=TOP_K)
-        eps.append(ExpertParallelMoE(backend, expert_count=EXPERTS, hidden_size=HIDDEN, top_k=TOP_K))
+        eps.append(ExpertParallelMoE(backend, expert_count=EXPERTS, hidden_size=HIDDEN, top_k=TOP_K,
+                                     capacity_tokens=tokens))
         xs.append(L.x[tokens * rank:tokens * (rank + 1)].contiguous())
         del L, local_bank
     torch.cuda.synchronize()
 
-    def step(i):
+    def eager_step(i):
         j = i % layers
         return eps[j](xs[j])
 
     warm = max(3, args.warmup, layers)
     for i in range(warm):
+        eager_step(i)
+    torch.cuda.synchronize()
+    # One CUDA graph per layer (NCCL all-to-alls included: with a fixed
+    # capacity the step reads nothing back to the host).  Every rank must
+    # agree that capture worked before any graph is replayed.
+    graphs, gouts = [], []  # the only references to the graphs: cleared before the process group goes
+    ok = 1
+    try:
+        _capture_ep_graphs(eps, xs, graphs, gouts)
+    except Exception as exc:  # fall back to eager steps on every rank
+        print(f"rank {rank}: graph capture failed: {exc!r}", file=sys.stderr, flush=True)
+        ok = 0
+    flag = torch.tensor([ok], dtype=torch.int32, device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    use_graphs = bool(flag.item())
+    if not use_graphs:
+        graphs.clear()
+        gouts.clear()
+
+    def step(i):
+        if use_graphs:
+            graphs[i % layers].replay()
+            return gouts[i % layers]
+        return eager_step(i)
+
+    for i in range(3):
         step(i)
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
@@ -493,9 +520,10 @@ def ep_arm(args):
     dev_x = [torch.empty_like(x) for x in xs]
 
     def e2e_step(i):
+        # the batch lands in the step's input buffer (the graph's input), the output goes back to the host
         j = i % layers
-        dev_x[j].copy_(host_x[j], non_blocking=True)
-        host_out[j].copy_(eps[j](dev_x[j]), non_blocking=True)
+        xs[j].copy_(host_x[j], non_blocking=True)
+        host_out[j].copy_(step(j), non_blocking=True)
 
     for i in range(3):
         e2e_step(i)
@@ -513,7 +541,7 @@ def ep_arm(args):
     _lib.profile_enable(True)
     _lib.profile_read(reset=True)
     for i in range(args.steps):
-        step(i)
+        eager_step(i)
     torch.cuda.synchronize()
     prof = _lib.profile_read(reset=True)
     _lib.profile_enable(False)
@@ -531,7 +559,8 @@ def ep_arm(args):
                                    f"512 experts sharded {per}/GPU, router + shared expert replicated",
                        "tokens_per_gpu": tokens, "layers_rotated": layers,
                        "l2": f"inputs larger than L2: {layers} distinct layers rotated per step",
-                       "parallelism": f"ep{world}"},
+                       "parallelism": f"ep{world}", "cuda_graph": use_graphs,
+                       "exchange": f"NCCL all_to_all_single, fixed capacity {tokens * TOP_K} slots per peer"},
             "roofline": {"bound": "hbm", "kernel": "gate_up", "avg_launch_us": gu_avg_s * 1e6,
                          "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s", "achieved": None,
                          "frac": None, "traffic": None,
@@ -544,8 +573,31 @@ def ep_arm(args):
         }
         print(json.dumps(line), flush=True)
     dist.barrier()
+    torch.cuda.synchronize()
+    graphs.clear()  # graphs holding NCCL work go before the process group
+    gouts.clear()
+    import gc
+
+    gc.collect()
+    torch.cuda.synchronize()
     dist.destroy_process_group()
     return 0
+
+
+def _capture_ep_graphs(eps, xs, graphs, gouts):
+    """One CUDA graph per expert-parallel layer step (appended to `graphs`,
+    outputs to `gouts`); no other reference to a graph outlives this call."""
+    import torch
+
+    cap_stream = torch.cuda.Stream()
+    cap_stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap_stream):
+        for ep, x in zip(eps, xs):
+            graphs.append(torch.cuda.CUDAGraph())
+            with torch.cuda.graph(graphs[-1], stream=cap_stream):
+                gouts.append(ep(x))
+    torch.cuda.current_stream().wait_stream(cap_stream)
+    torch.cuda.synchronize()
 
 
 def batch1_numbers(hbm_peak):

@@ -48,6 +48,9 @@ extern "C" {
 
 #define FNMOE_ABI_VERSION 4u
 
+/* A route value marking an empty slot (skipped without an error). */
+#define FNMOE_ROUTE_NONE 0xFFFFFFFFu
+
 /* Size of the library-owned scratch used by fnmoe_moe_execute_static. */
 #define FNMOE_STATIC_SCRATCH_BYTES (16ull << 20)
 
@@ -125,7 +128,9 @@ typedef struct FnMoEArgs {
   const uint32_t *down_weight; /* [experts, hidden, inter/8] */
   const void *down_scales;     /* [experts, hidden, inter/group] bf16 */
   const void *down_biases;
-  const uint32_t *routes;      /* [tokens, slots]; bit 31 = table record */
+  const uint32_t *routes;      /* [tokens, slots]; bit 31 = table record;
+                                  FNMOE_ROUTE_NONE = empty slot (no expert runs,
+                                  its per-slot output is left untouched) */
   const void *scores;          /* [tokens, slots] (scores_dtype) or NULL */
   void *output;                /* [tokens, hidden] bf16 (combined) */
   uint32_t tokens;

@@ -16,6 +16,7 @@
 namespace fnmoe {
 
 constexpr uint32_t kSlotBit = 0x80000000u;
+constexpr uint32_t kRouteNone = 0xFFFFFFFFu;  // FNMOE_ROUTE_NONE: an empty slot, skipped
 constexpr int kWarp = 32;
 
 // Device error word bits (fnmoe_read_device_errors).

@@ -292,6 +292,7 @@ __device__ __forceinline__ int bin_of_pair(const uint32_t *routes, int i, int n_
                                            int E_arr, int records, int n_bins) {
   if (i >= n_pairs) return n_bins - 1;  // shared expert bin
   const uint32_t r = __ldcg(routes + i);  // L2 load: routes may come from this same kernel
+  if (r == kRouteNone) return -3;         // an empty slot: no bin, no error
   if (r & kSlotBit) {
     const uint32_t slot = r & 0x7FFFFFFFu;
     return slot < static_cast<uint32_t>(records) ? E_arr + static_cast<int>(slot) : -1;
@@ -327,13 +328,13 @@ __device__ __forceinline__ void group_walk(const uint32_t *routes, int n_pairs, 
                                            const int *off, int32_t *order, uint32_t *err) {
   const int lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
-  const int nbits = 32 - __clz(n_bins + 1);
+  const int nbits = 32 - __clz(n_bins + 2);  // keys b + 3 for b in [-3, n_bins)
   for (int base = i0; base < i1; base += 32 * kGroupUnroll) {
     int b[kGroupUnroll];
 #pragma unroll
     for (int u = 0; u < kGroupUnroll; ++u) {
       const int i = base + 32 * u + lane;
-      b[u] = i < i1 ? bin_of_pair(routes, i, n_pairs, E_arr, records, n_bins) : -2;
+      b[u] = i < i1 ? bin_of_pair(routes, i, n_pairs, E_arr, records, n_bins) : -3;
     }
     if (order == nullptr) {
 #pragma unroll
@@ -345,7 +346,7 @@ __device__ __forceinline__ void group_walk(const uint32_t *routes, int n_pairs, 
     }
 #pragma unroll
     for (int u = 0; u < kGroupUnroll; ++u) {
-      const unsigned m = match_key(b[u] + 2, nbits);
+      const unsigned m = match_key(b[u] + 3, nbits);
       const bool leader = (m >> lane) == 1u;  // highest lane of its bin group
       int pos = 0;
       if (b[u] >= 0) pos = off[b[u]] + row[b[u]] + __popc(m & lt);

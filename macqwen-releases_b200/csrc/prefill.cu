@@ -481,13 +481,13 @@ __global__ void __launch_bounds__(kPThreads, 1) k_prefill_gemm(ExpertCallArgs a,
 
 // Input rows of the gate/up GEMM in bin order: row p of `dst` is the token
 // row of pair order[p] (one warp per row, 16-byte copies).
-__global__ void __launch_bounds__(256) k_gather_rows(const int32_t *order, int n_rows, int n_pairs, int slots,
-                                                     int n_tokens, const uint16_t *x, int H, uint16_t *dst,
-                                                     uint32_t *err) {
+__global__ void __launch_bounds__(256) k_gather_rows(const int32_t *order, const int32_t *grouped, int n_rows,
+                                                     int n_pairs, int slots, int n_tokens, const uint16_t *x, int H,
+                                                     uint16_t *dst, uint32_t *err) {
   pdl_wait();
   pdl_trigger();
   const int p = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (p >= n_rows) return;
+  if (p >= n_rows || p >= grouped[0]) return;  // grouped[0]: pairs placed by the grouping
   const int pair = order[p];
   int t = (pair >= 0 && pair < n_rows) ? pair_row(pair, n_pairs, slots) : -1;
   if (t < 0 || t >= n_tokens) {
@@ -592,8 +592,8 @@ cudaError_t launch_prefill_gather(const ExpertCallArgs &a, const GroupView &gv, 
                                   cudaStream_t s) {
   const int n_rows = a.n_pairs + (a.tiled.has_shared ? a.tokens : 0);
   if (a.H % 8 != 0) return cudaErrorInvalidValue;
-  cudaError_t e = launch_pdl(k_gather_rows, (n_rows + 7) / 8, 256, 0, s, gv.order, n_rows, a.n_pairs, a.slots,
-                             a.tokens, x, a.H, dst, device_error_word());
+  cudaError_t e = launch_pdl(k_gather_rows, (n_rows + 7) / 8, 256, 0, s, gv.order, gv.offsets + gv.n_bins, n_rows,
+                             a.n_pairs, a.slots, a.tokens, x, a.H, dst, device_error_word());
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -31,6 +31,7 @@ DTYPE_F32 = 1
 
 FLAG_RETURN_ALL = 0x1
 FLAG_NO_COMBINE = 0x2
+ROUTE_NONE = 0xFFFFFFFF  # an empty slot: skipped, its per-slot output left untouched
 
 ERR_BAD_ROUTE = 0x1
 ERR_NON_FINITE = 0x2

@@ -8,12 +8,17 @@ tokens (data parallel over tokens).  One layer step:
    expert's sigmoid gate (``fnmoe_router_topk_shared``; the reference computes
    the same on one device, ``models/flashnext/adaptive_topk.py:53-64,263-264``);
 2. dispatch: the (token, slot) pairs are ordered by owner rank (stable in pair
-   order); pair counts are exchanged, then each pair's input row and the
-   owner-local expert id go to the owner (``all_to_all_single``);
-3. the owner runs its experts on the received rows, one slot per row,
-   together with the shared expert on its own tokens (the shared expert is
-   one more record of its tiled table; ``fnmoe_moe_execute`` with per-slot
-   outputs);
+   order) and written into a fixed-capacity send buffer, ``capacity * top_k``
+   slots per peer (enough when every pair goes to one owner; the capacity is
+   the largest per-rank token count, given at construction or agreed per call
+   by an all-reduce); a slot carries the input row and the owner-local expert
+   id, or ``ROUTE_NONE`` when unused.  One ``all_to_all_single`` with equal
+   splits moves it; with a given capacity nothing is read back to the host
+   and the step can be captured in a CUDA graph;
+3. the owner runs its experts on the received rows, one slot per row (empty
+   slots are skipped by the grouping), together with the shared expert on its
+   own tokens (the shared expert is one more record of its tiled table;
+   ``fnmoe_moe_execute`` with per-slot outputs);
 4. the bfloat16 outputs come back along the reverse all-to-all and land in
    their (token, slot) places;
 5. the token's rank combines in slot order and adds the gated shared expert
@@ -21,8 +26,7 @@ tokens (data parallel over tokens).  One layer step:
 
 Every kernel gives a row's result independently of the rest of its batch, so
 the output is bit-identical to the single-device layer (``fnmoe_moe_layer``).
-The counts exchange is read on the host to size the payload all-to-all;
-rows travel as int32 words (pairs of bfloat16), which every backend carries.
+Rows travel as int32 words (pairs of bfloat16), which every backend carries.
 
 The compute steps go through a backend object: ``CudaBackend`` (the product)
 or, for multi-process tests of the dispatch/combine logic on CPU ranks, any
@@ -151,7 +155,8 @@ class CudaBackend:
 class ExpertParallelMoE:
     """One sparse-MoE layer with experts sharded over the ranks of `group`."""
 
-    def __init__(self, backend, *, expert_count: int, hidden_size: int, top_k: int, group=None):
+    def __init__(self, backend, *, expert_count: int, hidden_size: int, top_k: int, group=None,
+                 capacity_tokens: int | None = None):
         import torch.distributed as dist
 
         self.backend = backend
@@ -164,6 +169,21 @@ class ExpertParallelMoE:
         self.per_rank = expert_count // self.world
         self.hidden_size = hidden_size
         self.top_k = top_k
+        # tokens per rank and call that every rank's send buffer can hold; None:
+        # agreed per call with an all-reduce of the ranks' token counts
+        self.capacity_tokens = capacity_tokens
+
+    def _capacity(self, T, device):
+        torch = _torch()
+        import torch.distributed as dist
+
+        if self.capacity_tokens is not None:
+            if T > self.capacity_tokens:
+                raise ValueError(f"{T} tokens exceed capacity_tokens={self.capacity_tokens}")
+            return self.capacity_tokens
+        t = torch.tensor([T], dtype=torch.int64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        return int(t.item())
 
     def _a2a(self, out, inp, out_splits, in_splits):
         import torch.distributed as dist
@@ -175,28 +195,32 @@ class ExpertParallelMoE:
         torch = _torch()
         T, H = x.shape
         k = self.top_k
+        W = self.world
         dev = x.device
         inds, scores, sg = self.backend.route(x)
         flat = inds.reshape(-1).to(torch.int64)
         owner = torch.div(flat, self.per_rank, rounding_mode="floor")
         order = torch.sort(owner, stable=True).indices  # pairs grouped by owner, pair order kept
-        send_counts = torch.bincount(owner, minlength=self.world).to(torch.int64)
-        recv_counts = torch.empty_like(send_counts)
-        self._a2a(recv_counts, send_counts, [1] * self.world, [1] * self.world)
-        sc, rc = send_counts.tolist(), recv_counts.tolist()
-        n_recv = int(sum(rc))
-        # one payload row per pair: the input row as H/2 int32 words, then the
-        # owner-local expert id and three pad words
+        so = owner[order]
+        # pairs per owner (scatter_add into a fixed-size tensor: bincount would read its size back to the host)
+        counts = torch.zeros(W, dtype=torch.int64, device=dev).scatter_add_(0, owner, torch.ones_like(owner))
+        starts = torch.cumsum(counts, 0) - counts
+        pos = torch.arange(T * k, device=dev) - starts[so]  # slot inside the owner's segment
+        cap = self._capacity(T, dev) * k
         w = H // 2
-        send = torch.zeros((T * k, w + 4), dtype=torch.int32, device=dev)
-        send[:, :w] = x.view(torch.int32)[torch.div(order, k, rounding_mode="floor")]
-        send[:, w] = (flat[order] - owner[order] * self.per_rank).to(torch.int32)
-        recv = torch.empty((n_recv, w + 4), dtype=torch.int32, device=dev)
-        self._a2a(recv, send, rc, sc)
-        recv_rows = recv[:, :w].contiguous().view(x.dtype)
-        d_recv, shared = self.backend.experts(recv_rows, recv[:, w].contiguous(), x)
-        d_back = torch.empty((T * k, H), dtype=d_recv.dtype, device=dev)
-        self._a2a(d_back.view(torch.int32), d_recv.contiguous().view(torch.int32), sc, rc)
-        d = torch.empty_like(d_back)
-        d[order] = d_back
+        # one payload row per slot: the input row as H/2 int32 words, then the
+        # owner-local expert id (ROUTE_NONE when the slot is empty) and 3 pad words
+        send = torch.zeros((W, cap, w + 4), dtype=torch.int32, device=dev)
+        send[:, :, w] = -1  # ROUTE_NONE as int32
+        send[so, pos, :w] = x.view(torch.int32)[torch.div(order, k, rounding_mode="floor")]
+        send[so, pos, w] = (flat[order] - so * self.per_rank).to(torch.int32)
+        recv = torch.empty_like(send)
+        self._a2a(recv.view(W * cap, w + 4), send.view(W * cap, w + 4), None, None)
+        recv_rows = recv[:, :, :w].reshape(W * cap, w).view(x.dtype)
+        d_recv, shared = self.backend.experts(recv_rows, recv[:, :, w].reshape(-1).contiguous(), x)
+        back = torch.empty((W, cap, H), dtype=d_recv.dtype, device=dev)
+        self._a2a(back.view(W * cap, H).view(torch.int32), d_recv.reshape(W * cap, H).contiguous().view(torch.int32),
+                  None, None)
+        d = torch.empty((T * k, H), dtype=back.dtype, device=dev)
+        d[order] = back[so, pos]
         return self.backend.combine(d.view(T, k, H), inds, scores, shared, sg)

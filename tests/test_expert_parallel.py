@@ -67,12 +67,12 @@ class OracleBackend:
     def experts(self, rows, local_ids, x):
         from oracle import moe
 
-        if rows.shape[0] == 0:
-            d = np.zeros((0, H), np.float32)
-        else:
-            d = moe.executor(rows.float().numpy(), local_ids.numpy().astype(np.int64).reshape(-1, 1),
-                             self.bank["gate_proj"], self.bank["up_proj"], self.bank["down_proj"],
-                             group_size=G).reshape(-1, H)
+        ids = local_ids.numpy().astype(np.int64)
+        d = np.zeros((rows.shape[0], H), np.float32)
+        live = ids >= 0  # ROUTE_NONE (-1 as int32) marks an empty slot
+        if live.any():
+            d[live] = moe.executor(rows.float().numpy()[live], ids[live].reshape(-1, 1), self.bank["gate_proj"],
+                                   self.bank["up_proj"], self.bank["down_proj"], group_size=G).reshape(-1, H)
         sh, _, _ = moe.shared_expert(x.float().numpy(), *self.shared, self.wg, G)
         return self._bf(d), self._bf(sh)
 
