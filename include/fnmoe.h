@@ -198,6 +198,15 @@ typedef struct FnMoELayerArgs {
   FnTiledExperts tiled;
   uint32_t flags;              /* FNMOE_LAYER_* */
   uint32_t reserved1;
+  /* Adaptive keep (adaptive_topk.py:43-50,75-261): with 0 < keep_threshold < 1
+   * each token keeps its first max(min_keep, n) top-k slots, n the first
+   * position whose cumulative share of the top-k mass (IEEE double, as the
+   * reference's Python floats) reaches the threshold; dropped slots report
+   * slot 0's expert with score 0, run no expert, and the renorm uses the kept
+   * mass.  0 (or >= 1) keeps every slot. */
+  double keep_threshold;
+  uint32_t min_keep;           /* 0 or 1: at least one slot */
+  uint32_t reserved2;
 } FnMoELayerArgs;
 
 /* FnMoELayerArgs.flags: by default a layer with tiled tables (group size 32,

@@ -383,6 +383,10 @@ int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
     e = launch_group(a->routes, n_pairs, 0, call.array_experts, static_cast<int>(call.table.records), L.gv, s);
   }
   if (e != cudaSuccess) return cuda_fail(e, "group");
+  // Empty slots (FNMOE_ROUTE_NONE) leave their activation rows unwritten:
+  // zero them so that the activation fixed point sees finite rows.
+  e = cudaMemsetAsync(L.act, 0, static_cast<size_t>(n_pairs) * a->inter_size * sizeof(uint16_t), s);
+  if (e != cudaSuccess) return cuda_fail(e, "clear activations");
   {
     Prof p("gate_up", s);
     e = launch_gate_up(call, L.gv, L.xl, L.xm, L.act,
@@ -735,7 +739,8 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
     e = launch_route_small(logits, T, E, k, a->renorm_blend, a->table_routes_of_expert, has_table ? 1 : 0, inds,
                            LL.routes, nullptr, scores, LL.mass, shared ? LL.shared_logit : nullptr,
                            shared ? LL.shared_gate : nullptr, shared ? T : 0, call.array_experts,
-                           static_cast<int>(call.table.records), L.gv, s);
+                           static_cast<int>(call.table.records), L.gv, s, a->keep_threshold,
+                           static_cast<int>(a->min_keep));
     if (e != cudaSuccess && e != cudaErrorNotSupported) return cuda_fail(e, "route_group");
   }
   if (e == cudaErrorNotSupported) {
@@ -743,7 +748,8 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
       Prof p("softmax_topk", s);
       e = launch_softmax_topk(logits, T, E, k, a->renorm_blend, a->table_routes_of_expert, has_table ? 1 : 0,
                               inds, LL.routes, nullptr, scores, LL.mass, shared ? LL.shared_logit : nullptr,
-                              shared ? LL.shared_gate : nullptr, s);
+                              shared ? LL.shared_gate : nullptr, s, a->keep_threshold,
+                              static_cast<int>(a->min_keep));
     }
     if (e != cudaSuccess) return cuda_fail(e, "softmax_topk");
     {
@@ -777,6 +783,11 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
     }
     if (e != cudaSuccess) return cuda_fail(e, "prefill down");
   } else {
+    if (a->keep_threshold > 0.0 && a->keep_threshold < 1.0) {
+      // dropped slots leave their activation rows unwritten (see the executor)
+      e = cudaMemsetAsync(L.act, 0, static_cast<size_t>(n_total_pairs) * I * sizeof(uint16_t), s);
+      if (e != cudaSuccess) return cuda_fail(e, "clear activations");
+    }
     {
       Prof p("gate_up", s);
       e = launch_gate_up(call, L.gv, L.xl, L.xm, L.act, nullptr, nullptr, s);

@@ -1673,13 +1673,34 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
 
 // Logits per lane (experts <= 32 * PER) is a template parameter: 16 at 512 experts.
 
+// Adaptive keep (adaptive_topk.py:43-50): with 0 < threshold < 1, the first
+// position whose cumulative share of the top-k mass reaches the threshold
+// (IEEE double, sequential, as the reference's Python floats), at least
+// max(1, min(k, min_keep)); otherwise k.  `sel(s)` is slot s's probability.
+template <typename Sel>
+__device__ __forceinline__ int keep_count(Sel sel, int k, double threshold, int min_keep) {
+  if (!(threshold > 0.0 && threshold < 1.0)) return k;
+  double total = 0.0;
+  for (int s = 0; s < k; ++s) total += static_cast<double>(sel(s));
+  double acc = 0.0;
+  int keep = k;
+  for (int s = 0; s < k; ++s) {
+    acc += static_cast<double>(sel(s)) / total;
+    if (acc >= threshold) {
+      keep = s + 1;
+      break;
+    }
+  }
+  return max(keep, max(1, min(k, min_keep)));
+}
+
 template <int kMaxPerLane>
 __global__ void __launch_bounds__(128) k_softmax_topk(
     const uint16_t *logits, int T, int E, int k, float blend,
     const uint32_t *__restrict__ route_map, int table_routes, uint32_t *__restrict__ inds,
     uint32_t *__restrict__ routes, uint16_t *__restrict__ raw_scores,
     uint16_t *__restrict__ scores, uint16_t *__restrict__ mass,
-    const uint16_t *shl, uint16_t *__restrict__ shg) {
+    const uint16_t *shl, uint16_t *__restrict__ shg, double keep_threshold, int min_keep) {
   pdl_wait();
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1739,16 +1760,20 @@ __global__ void __launch_bounds__(128) k_softmax_topk(
   }
   if (lane == 0) {
     const float topm = round_bf16(acc);
-    const float selected = topm;  // threshold 1.0 keeps every selected slot
+    const int keep = keep_count([&](int s) { return sel[s]; }, k, keep_threshold, min_keep);
+    float kept = 0.0f;  // kept mass in slot order (all of it when nothing is dropped)
+    for (int s = 0; s < keep; ++s) kept = __fadd_rn(kept, sel[s]);
+    const float selected = round_bf16(kept);
     const float bl = round_bf16(blend);
     const float normalizer = badd(topm, bmul(bl, bsub(selected, topm)));
     for (int s = 0; s < k; ++s) {
-      const uint32_t e = idx[s];
+      const bool live = s < keep;  // dropped slots: slot 0's expert, score 0, no expert run
+      const uint32_t e = live ? idx[s] : idx[0];
       inds[static_cast<size_t>(t) * k + s] = e;
       routes[static_cast<size_t>(t) * k + s] =
-          route_map ? route_map[e] : (table_routes ? (kSlotBit | e) : e);
-      if (raw_scores) raw_scores[static_cast<size_t>(t) * k + s] = f32_to_bf16(sel[s]);
-      if (scores) scores[static_cast<size_t>(t) * k + s] = f32_to_bf16(__fdiv_rn(sel[s], normalizer));
+          !live ? kRouteNone : route_map ? route_map[e] : (table_routes ? (kSlotBit | e) : e);
+      if (raw_scores) raw_scores[static_cast<size_t>(t) * k + s] = live ? f32_to_bf16(sel[s]) : 0;
+      if (scores) scores[static_cast<size_t>(t) * k + s] = live ? f32_to_bf16(__fdiv_rn(sel[s], normalizer)) : 0;
     }
     if (mass) mass[t] = f32_to_bf16(topm);
     if (shl && shg) shg[t] = f32_to_bf16(sigmoid_bf16(g_exp_bf16, bf16_to_f32(shl[t])));
@@ -1767,7 +1792,8 @@ __global__ void __launch_bounds__(1024) k_route_small(
     const uint16_t *logits, int T, int E, int k, float blend,
     const uint32_t *__restrict__ route_map, int table_routes, uint32_t *inds, uint32_t *routes,
     uint16_t *raw_scores, uint16_t *scores, uint16_t *mass, const uint16_t *shl,
-    uint16_t *shg, int shared_tokens, int E_arr, int records, GroupView gv, int seg_warps, uint32_t *err) {
+    uint16_t *shg, int shared_tokens, int E_arr, int records, GroupView gv, int seg_warps, double keep_threshold,
+    int min_keep, uint32_t *err) {
   extern __shared__ int sm[];
   pdl_wait();
   pdl_trigger();
@@ -1844,14 +1870,22 @@ __global__ void __launch_bounds__(1024) k_route_small(
       acc = __fadd_rn(acc, p);
     }
     const float topm = round_bf16(acc);
+    // every lane runs the same keep test on the slot probabilities (lane s holds slot s)
+    const int keep = keep_count([&](int s) { return __shfl_sync(0xFFFFFFFFu, sel, s); }, k, keep_threshold, min_keep);
+    float kept = 0.0f;
+    for (int s = 0; s < keep; ++s) kept = __fadd_rn(kept, __shfl_sync(0xFFFFFFFFu, sel, s));
+    const float selected = round_bf16(kept);
+    const uint32_t idx0 = __shfl_sync(0xFFFFFFFFu, idx, 0);
     const float bl = round_bf16(blend);
-    const float normalizer = badd(topm, bmul(bl, bsub(topm, topm)));
+    const float normalizer = badd(topm, bmul(bl, bsub(selected, topm)));
     if (lane < k) {
+      const bool live = lane < keep;  // dropped slots: slot 0's expert, score 0, no expert run
+      const uint32_t e = live ? idx : idx0;
       const size_t o = static_cast<size_t>(t) * k + lane;
-      inds[o] = idx;
-      routes[o] = route_map ? route_map[idx] : (table_routes ? (kSlotBit | idx) : idx);
-      if (raw_scores) raw_scores[o] = f32_to_bf16(sel);
-      if (scores) scores[o] = f32_to_bf16(__fdiv_rn(sel, normalizer));
+      inds[o] = e;
+      routes[o] = !live ? kRouteNone : route_map ? route_map[e] : (table_routes ? (kSlotBit | e) : e);
+      if (raw_scores) raw_scores[o] = live ? f32_to_bf16(sel) : 0;
+      if (scores) scores[o] = live ? f32_to_bf16(__fdiv_rn(sel, normalizer)) : 0;
     }
     if (lane == 0) {
       if (mass) mass[t] = f32_to_bf16(topm);
@@ -1867,7 +1901,7 @@ cudaError_t launch_route_small(const uint16_t *logits, int T, int E, int k, floa
                                uint32_t *routes, uint16_t *raw_scores, uint16_t *scores,
                                uint16_t *mass, const uint16_t *shared_logit, uint16_t *shared_gate,
                                int shared_tokens, int array_experts, int table_records, GroupView gv,
-                               cudaStream_t s) {
+                               cudaStream_t s, double keep_threshold, int min_keep) {
   const int per = (E + 31) / 32;
   if (T > kRouteSmallTokens || per > 32 || k > 32) return cudaErrorNotSupported;
   int seg_warps = 1;
@@ -1883,7 +1917,7 @@ cudaError_t launch_route_small(const uint16_t *logits, int T, int E, int k, floa
     cudaError_t e = launch_pdl(k_route_small<P>, 1, 1024, smem, s, logits, T, E, k, blend, route_map,     \
                                table_routes, inds, routes, raw_scores, scores, mass, shared_logit,      \
                                shared_gate, shared_tokens, array_experts, table_records, gv, seg_warps, \
-                               device_error_word());                                                    \
+                               keep_threshold, min_keep, device_error_word());                          \
     if (e != cudaSuccess) return e;                                                                    \
     return cudaGetLastError();                                                                         \
   }
@@ -1899,13 +1933,13 @@ cudaError_t launch_softmax_topk(const uint16_t *logits, int T, int E, int k, flo
                                 const uint32_t *route_map, int table_routes, uint32_t *inds,
                                 uint32_t *routes, uint16_t *raw_scores, uint16_t *scores,
                                 uint16_t *mass, const uint16_t *shared_logit,
-                                uint16_t *shared_gate, cudaStream_t s) {
+                                uint16_t *shared_gate, cudaStream_t s, double keep_threshold, int min_keep) {
   const int per = (E + 31) / 32;
 #define FNMOE_TOPK_CASE(P)                                                                           \
   if (per <= P) {                                                                                   \
     cudaError_t e = launch_pdl(k_softmax_topk<P>, (T + 3) / 4, 128, 0, s, logits, T, E, k, blend,       \
                                route_map, table_routes, inds, routes, raw_scores, scores, mass,        \
-                               shared_logit, shared_gate);                                              \
+                               shared_logit, shared_gate, keep_threshold, min_keep);                    \
     if (e != cudaSuccess) return e;                                                                    \
     return cudaGetLastError();                                                                    \
   }

@@ -65,7 +65,7 @@ cudaError_t launch_route_small(const uint16_t *logits, int T, int E, int k, floa
                                uint32_t *routes, uint16_t *raw_scores, uint16_t *scores,
                                uint16_t *mass, const uint16_t *shared_logit, uint16_t *shared_gate,
                                int shared_tokens, int array_experts, int table_records, GroupView gv,
-                               cudaStream_t s);
+                               cudaStream_t s, double keep_threshold = 0.0, int min_keep = 0);
 
 // Stable counting-sort grouping of routes (+ optional shared bin).
 cudaError_t launch_group(const uint32_t *routes, int n_pairs, int shared_tokens,
@@ -130,7 +130,8 @@ cudaError_t launch_softmax_topk(const uint16_t *logits, int T, int E, int k,
                                 uint32_t *routes, uint16_t *raw_scores,
                                 uint16_t *scores, uint16_t *mass,
                                 const uint16_t *shared_logit,
-                                uint16_t *shared_gate, cudaStream_t s);
+                                uint16_t *shared_gate, cudaStream_t s,
+                                double keep_threshold = 0.0, int min_keep = 0);
 
 // Repack `experts` experts' projections (reference layout) into tiled
 // records: dual = gate (A) + up (B) rows, else down rows.

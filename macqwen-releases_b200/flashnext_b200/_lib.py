@@ -101,6 +101,7 @@ class FnMoELayerArgs(ctypes.Structure):
         ("workspace", _vp), ("workspace_bytes", _u64),
         ("tiled", FnTiledExperts),
         ("flags", _u32), ("reserved1", _u32),
+        ("keep_threshold", ctypes.c_double), ("min_keep", _u32), ("reserved2", _u32),
     ]
 
 

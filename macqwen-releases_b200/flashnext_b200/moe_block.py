@@ -51,18 +51,25 @@ class SparseMoEBlock:
     only those; ``tiled=False`` keeps reading the reference-layout arrays.
     ``path`` selects the expert kernels: "auto" (tcgen05 GEMMs on dequantised
     bf16 weights for prefill-sized batches, the exact decode kernels
-    otherwise), "prefill" or "decode".
+    otherwise), "prefill" or "decode".  ``keep_threshold`` < 1 turns on the
+    adaptive keep of ``adaptive_topk.py:43-50,75-261`` (``_THRESHOLD`` /
+    ``_MIN_KEEP``): each token keeps the fewest top-k slots whose share of the
+    top-k mass reaches the threshold (at least ``min_keep``), computed on the
+    GPU without a host sync; dropped slots report slot 0's expert with score 0.
     """
 
     def __init__(self, router_weight, experts: Any, *, top_k: int = 10, shared: Mapping | None = None,
                  shared_expert_gate=None, group_size: int = 32, renorm_blend: float = 1.0,
-                 route_map=None, tiled: bool = True, path: str = "auto"):
+                 route_map=None, tiled: bool = True, path: str = "auto", keep_threshold: float = 1.0,
+                 min_keep: int = 1):
         torch = _torch()
         self.router_weight = _bf16(router_weight, "router_weight")
         self.expert_count, self.hidden_size = (int(v) for v in self.router_weight.shape)
         self.top_k = int(top_k)
         self.group_size = int(group_size)
         self.renorm_blend = float(renorm_blend)
+        self.keep_threshold = float(keep_threshold)
+        self.min_keep = int(min_keep)
         if path not in ("auto", "prefill", "decode"):
             raise ValueError("path must be 'auto', 'prefill' or 'decode'")
         self.path = path
@@ -130,6 +137,8 @@ class SparseMoEBlock:
                 setattr(a, f"shared_{key}_biases", b.data_ptr())
             a.shared_expert_gate = self.shared_expert_gate.data_ptr()
         a.flags = {"auto": 0, "prefill": _lib.LAYER_FORCE_PREFILL, "decode": _lib.LAYER_FORCE_DECODE}[self.path]
+        a.keep_threshold = self.keep_threshold if 0.0 < self.keep_threshold < 1.0 else 0.0
+        a.min_keep = max(0, self.min_keep)
         a.output = out.data_ptr()
         a.logits_out = logits.data_ptr()
         a.inds_out = inds.data_ptr()

@@ -505,11 +505,46 @@ def renorm(scores, topk_mass, blend=1.0):
     return bf16.op(np.divide, sc, normalizer), normalizer
 
 
-def router(x, router_weight, k, blend=1.0):
-    """Router chain at threshold 1.0: logits -> softmax -> top-k -> renorm."""
+def keep_for_mass(weights, threshold):
+    """``_keep_for_mass`` (adaptive_topk.py:43-50): Python floats (IEEE double),
+    a sequential total, then the first position whose cumulative share reaches
+    the threshold."""
+    ws = [float(w) for w in weights]
+    total = 0.0
+    for w in ws:
+        total += w
+    accumulated = 0.0
+    for position, w in enumerate(ws):
+        accumulated += w / total if total != 0.0 else float("nan")
+        if accumulated >= threshold:
+            return position + 1
+    return len(ws)
+
+
+def adaptive_keep(inds, scores, threshold, min_keep=1):
+    """Adaptive keep at threshold < 1 (adaptive_topk.py:75-234 without the
+    expert-cache features): the top-k slots, already in descending score order
+    (ties to the lower expert, as the stable ``argsort(-scores)``), keep
+    ``max(minimum, keep_for_mass)`` slots; dropped slots repeat slot 0's expert
+    with score 0.  Returns (inds, scores, keeps).  Threshold >= 1 keeps all."""
+    inds = np.asarray(inds)
+    sc = np.asarray(scores, np.float32)
+    t, k = sc.shape
+    if not 0.0 < threshold < 1.0:
+        return inds, sc, np.full((t,), k, np.int64)
+    minimum = max(1, min(k, int(min_keep)))
+    keeps = np.array([max(minimum, keep_for_mass(row, threshold)) for row in sc.tolist()], np.int64)
+    active = np.arange(k)[None, :] < keeps[:, None]
+    return np.where(active, inds, inds[:, :1]), np.where(active, sc, np.float32(0.0)), keeps
+
+
+def router(x, router_weight, k, blend=1.0, threshold=1.0, min_keep=1):
+    """Router chain: logits -> softmax -> top-k -> adaptive keep (threshold < 1)
+    -> renorm over the kept mass."""
     logits = router_logits(x, router_weight)
     probs = softmax_bf16(logits)
     inds, scores, mass = topk(probs, k)
+    inds, scores, _ = adaptive_keep(inds, scores, threshold, min_keep)
     rs, _ = renorm(scores, mass, blend)
     return inds, rs, mass, logits
 
@@ -536,13 +571,14 @@ def shared_expert(x, gate, up, down, gate_weight, group_size=32):
 
 
 def moe_block(x, router_weight, k, gate, up, down, shared, shared_gate_weight,
-              group_size=32, blend=1.0):
-    """One sparse-MoE block at threshold 1.0 (adaptive_topk.py:53-292).
+              group_size=32, blend=1.0, threshold=1.0, min_keep=1):
+    """One sparse-MoE block (adaptive_topk.py:53-292), adaptive keep when
+    threshold < 1.
 
     Returns dict with logits, inds, scores (renormalised), mass, shared_y and
     the bfloat16 output [T, H].
     """
-    inds, scores, mass, logits = router(x, router_weight, k, blend)
+    inds, scores, mass, logits = router(x, router_weight, k, blend, threshold, min_keep)
     sh, sg, sy = shared_expert(x, *shared, shared_gate_weight, group_size)
     out = executor(x, inds, gate, up, down, scores=scores, shared_y=sy, group_size=group_size)
     return {"logits": logits, "inds": inds, "scores": scores, "mass": mass,

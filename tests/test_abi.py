@@ -91,6 +91,7 @@ int main(void) {
   printf("FnTileArgs %zu %zu %zu\n", sizeof(FnTileArgs), offsetof(FnTileArgs, gate_weight),
          offsetof(FnTileArgs, tiled));
   printf("LayerTiled %zu\n", offsetof(FnMoELayerArgs, tiled));
+  printf("LayerKeep %zu %zu\n", offsetof(FnMoELayerArgs, keep_threshold), offsetof(FnMoELayerArgs, min_keep));
   return 0;
 }
 """
@@ -118,6 +119,8 @@ def test_struct_layout_matches_c_compiler(tmp_path):
     got = [int(v) for v in lines["FnTileArgs"].split()]
     assert got == [s(_lib.FnTileArgs), _lib.FnTileArgs.gate_weight.offset, _lib.FnTileArgs.tiled.offset]
     assert int(lines["LayerTiled"]) == _lib.FnMoELayerArgs.tiled.offset
+    got = [int(v) for v in lines["LayerKeep"].split()]
+    assert got == [_lib.FnMoELayerArgs.keep_threshold.offset, _lib.FnMoELayerArgs.min_keep.offset]
 
 
 def test_tiled_record_bytes_without_gpu():

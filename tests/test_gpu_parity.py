@@ -300,6 +300,46 @@ def test_moe_layer_bit_exact(cuda_lib, tokens, zipf):
     assert_north_star(_np(out), ref["out"])
 
 
+@pytest.mark.parametrize("tokens,zipf,threshold,min_keep", [(1, None, 0.5, 1), (5, None, 0.85, 2),
+                                                              (64, 1.1, 0.5, 1), (64, 1.1, 0.9, 3)])
+def test_moe_layer_adaptive_keep_bit_exact(cuda_lib, tokens, zipf, threshold, min_keep):
+    """Adaptive keep (adaptive_topk.py:43-50,75-261) on the GPU: kept slot
+    counts, indices (dropped -> slot 0's expert), renormalised scores and the
+    layer output against the oracle, bit for bit."""
+    from flashnext_b200 import _lib
+    from flashnext_b200.moe_block import SparseMoEBlock
+    _lib.read_device_errors()  # start from a clear error word
+    L = _layer_inputs(tokens, zipf=zipf, seed=tokens + 31)
+    block = SparseMoEBlock(L.router_weight, L.experts, top_k=10, shared=L.shared,
+                           shared_expert_gate=L.shared_expert_gate, keep_threshold=threshold, min_keep=min_keep)
+    out = block(L.x)
+    nb = _bank_np(L.experts)
+    sh = {k: (_np(w), _np(s), _np(b)) for k, (w, s, b) in L.shared.items()}
+    ref = moe.moe_block(_np(L.x), _np(L.router_weight), 10, nb["gate_proj"], nb["up_proj"], nb["down_proj"],
+                        (sh["gate_proj"], sh["up_proj"], sh["down_proj"]), _np(L.shared_expert_gate),
+                        threshold=threshold, min_keep=min_keep)
+    # some tokens really drop slots at these thresholds
+    assert (ref["scores"] == 0).any()
+    np.testing.assert_array_equal(_np(block.last_inds), ref["inds"])
+    assert_bf16_equal(_np(block.last_scores), ref["scores"], "scores")
+    assert_bf16_equal(_np(out), ref["out"], "layer output")
+    assert _lib.read_device_errors() == 0
+
+
+def test_moe_layer_adaptive_keep_prefill_within_tolerance(cuda_lib):
+    from flashnext_b200 import _lib
+    from flashnext_b200.moe_block import SparseMoEBlock
+    _lib.read_device_errors()
+    L = _layer_inputs(64, zipf=None, seed=77)
+    kw = dict(top_k=10, shared=L.shared, shared_expert_gate=L.shared_expert_gate, keep_threshold=0.6)
+    pre = SparseMoEBlock(L.router_weight, L.experts, path="prefill", **kw)
+    dec = SparseMoEBlock(L.router_weight, L.experts, path="decode", **kw)
+    out_p, out_d = _np(pre(L.x)), _np(dec(L.x))
+    np.testing.assert_array_equal(_np(pre.last_inds), _np(dec.last_inds))
+    assert_north_star(out_p, out_d)
+    assert _lib.read_device_errors() == 0
+
+
 def test_moe_layer_is_batch_invariant(cuda_lib):
     import torch
 
