@@ -1518,13 +1518,14 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
   }
 }
 
-// Router logits for many tokens: a CTA tile of 32 router rows x 16 tokens,
-// H streamed in 256-wide rounds through double-buffered bf16 shared memory
-// (cp.async, coherent L2 loads).  Warp w owns rows 8*(w&3).. and tokens
-// 8*(w>>2)..; lane j runs the canonical chains of those 8 x 8 (row, token)
-// pairs -- chunk 32*round + j, elements in increasing h, from -0.0 -- then
-// the same xor butterfly as k_router_logits, so logits are bit-identical.
-constexpr int kRtRows = 32, kRtTok = 16, kRtRound = 256;
+// Router logits for many tokens: a CTA tile of RC (32 or 16) router rows x 16
+// tokens, H streamed in 256-wide rounds through double-buffered bf16 shared
+// memory (cp.async, coherent L2 loads).  Each warp owns 8 rows x 8 tokens
+// (RC/8 warps per 8-token half); lane j runs the canonical chains of those
+// 8 x 8 (row, token) pairs -- chunk 32*round + j, elements in increasing h,
+// from -0.0 -- then the same xor butterfly as k_router_logits, so logits are
+// bit-identical.
+constexpr int kRtTok = 16, kRtRound = 256;
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float (&f)[8]) {
   f[0] = __uint_as_float(u.x << 16);
@@ -1537,9 +1538,11 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float (&f)[8]) {
   f[7] = __uint_as_float(u.w & 0xFFFF0000u);
 }
 
-__global__ void __launch_bounds__(256) k_router_tiled(const uint16_t *x, const uint16_t *__restrict__ W, int T,
-                                                      int H, int E, const uint16_t *__restrict__ wsg,
-                                                      uint16_t *logits, uint16_t *shared_logit) {
+template <int RC>
+__global__ void __launch_bounds__(RC * 8) k_router_tiled(const uint16_t *x, const uint16_t *__restrict__ W, int T,
+                                                         int H, int E, const uint16_t *__restrict__ wsg,
+                                                         uint16_t *logits, uint16_t *shared_logit) {
+  constexpr int kRtRows = RC, kThreads = RC * 8, kRowWarps = RC / 8;
   __shared__ __align__(16) uint16_t sw[2][kRtRows][kRtRound];
   __shared__ __align__(16) uint16_t sx[2][kRtTok][kRtRound];
   pdl_wait();
@@ -1549,10 +1552,10 @@ __global__ void __launch_bounds__(256) k_router_tiled(const uint16_t *x, const u
   const int r0 = blockIdx.x * kRtRows, t0 = blockIdx.y * kRtTok;
   const int nchunks = H / 8;
   const int nrounds = (nchunks + 31) / 32;
-  const int wr = 8 * (warp & 3), wt = 8 * (warp >> 2);
+  const int wr = 8 * (warp % kRowWarps), wt = 8 * (warp / kRowWarps);
   auto stage = [&](int m, int b) {
-    // 32 rows x 32 chunks of W and 16 tokens x 32 chunks of x, 16 bytes each
-    for (int i = tid; i < (kRtRows + kRtTok) * 32; i += 256) {
+    // RC rows x 32 chunks of W and 16 tokens x 32 chunks of x, 16 bytes each
+    for (int i = tid; i < (kRtRows + kRtTok) * 32; i += kThreads) {
       const int rr = i >> 5, c = i & 31;
       const int h = (32 * m + c) * 8;
       const uint16_t *src = nullptr;
@@ -1646,8 +1649,11 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
   const int ch = (H / 8 + 31) / 32;
   if (T >= 64 && H % 8 == 0) {
     const int rows = E + (w_shared_gate ? 1 : 0);
-    const dim3 grid((rows + kRtRows - 1) / kRtRows, (T + kRtTok - 1) / kRtTok);
-    cudaError_t e = launch_pdl(k_router_tiled, grid, 256, 0, s, x, W, T, H, E, w_shared_gate, logits, shared_logit);
+    const int tok_tiles = (T + kRtTok - 1) / kRtTok;
+    // 16-row tiles: at ~156 registers per thread three 4-warp CTAs fit per SM
+    // (one 8-warp CTA with 32-row tiles), which hides more of the staging latency
+    cudaError_t e = launch_pdl(k_router_tiled<16>, dim3((rows + 15) / 16, tok_tiles), 128, 0, s, x, W, T, H, E,
+                               w_shared_gate, logits, shared_logit);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }
