@@ -740,7 +740,7 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
                            LL.routes, nullptr, scores, LL.mass, shared ? LL.shared_logit : nullptr,
                            shared ? LL.shared_gate : nullptr, shared ? T : 0, call.array_experts,
                            static_cast<int>(call.table.records), L.gv, s, a->keep_threshold,
-                           static_cast<int>(a->min_keep));
+                           static_cast<int>(a->min_keep), !prefill);
     if (e != cudaSuccess && e != cudaErrorNotSupported) return cuda_fail(e, "route_group");
   }
   if (e == cudaErrorNotSupported) {

@@ -288,6 +288,16 @@ __device__ __forceinline__ int block_exclusive_scan_1024(int v, int *warp_sums, 
   return r;
 }
 
+// Bin of a route value (see bin_of_pair): -3 empty slot, -1 bad route.
+__device__ __forceinline__ int bin_of_route(uint32_t r, int E_arr, int records) {
+  if (r == kRouteNone) return -3;
+  if (r & kSlotBit) {
+    const uint32_t slot = r & 0x7FFFFFFFu;
+    return slot < static_cast<uint32_t>(records) ? E_arr + static_cast<int>(slot) : -1;
+  }
+  return r < static_cast<uint32_t>(E_arr) ? static_cast<int>(r) : -1;
+}
+
 __device__ __forceinline__ int bin_of_pair(const uint32_t *routes, int i, int n_pairs,
                                            int E_arr, int records, int n_bins) {
   if (i >= n_pairs) return n_bins - 1;  // shared expert bin
@@ -1538,11 +1548,12 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float (&f)[8]) {
   f[7] = __uint_as_float(u.w & 0xFFFF0000u);
 }
 
-template <int RC>
-__global__ void __launch_bounds__(RC * 8) k_router_tiled(const uint16_t *x, const uint16_t *__restrict__ W, int T,
-                                                         int H, int E, const uint16_t *__restrict__ wsg,
-                                                         uint16_t *logits, uint16_t *shared_logit) {
-  constexpr int kRtRows = RC, kThreads = RC * 8, kRowWarps = RC / 8;
+template <int RC, int WT>
+__global__ void __launch_bounds__(RC / 8 * (kRtTok / WT) * 32) k_router_tiled(const uint16_t *x, const uint16_t *__restrict__ W,
+                                                                            int T, int H, int E,
+                                                                            const uint16_t *__restrict__ wsg,
+                                                                            uint16_t *logits, uint16_t *shared_logit) {
+  constexpr int kRtRows = RC, kRowWarps = RC / 8, kThreads = kRowWarps * (kRtTok / WT) * 32;
   __shared__ __align__(16) uint16_t sw[2][kRtRows][kRtRound];
   __shared__ __align__(16) uint16_t sx[2][kRtTok][kRtRound];
   pdl_wait();
@@ -1552,7 +1563,7 @@ __global__ void __launch_bounds__(RC * 8) k_router_tiled(const uint16_t *x, cons
   const int r0 = blockIdx.x * kRtRows, t0 = blockIdx.y * kRtTok;
   const int nchunks = H / 8;
   const int nrounds = (nchunks + 31) / 32;
-  const int wr = 8 * (warp % kRowWarps), wt = 8 * (warp / kRowWarps);
+  const int wr = 8 * (warp % kRowWarps), wt = WT * (warp / kRowWarps);
   auto stage = [&](int m, int b) {
     // RC rows x 32 chunks of W and 16 tokens x 32 chunks of x, 16 bytes each
     for (int i = tid; i < (kRtRows + kRtTok) * 32; i += kThreads) {
@@ -1573,11 +1584,11 @@ __global__ void __launch_bounds__(RC * 8) k_router_tiled(const uint16_t *x, cons
     }
     cp_async_commit();
   };
-  float acc[8][8];
+  float acc[8][WT];
 #pragma unroll
   for (int r = 0; r < 8; ++r)
 #pragma unroll
-    for (int t = 0; t < 8; ++t) acc[r][t] = -0.0f;
+    for (int t = 0; t < WT; ++t) acc[r][t] = -0.0f;
   stage(0, 0);
   for (int m = 0; m < nrounds; ++m) {
     if (m + 1 < nrounds) stage(m + 1, (m + 1) & 1);
@@ -1586,12 +1597,12 @@ __global__ void __launch_bounds__(RC * 8) k_router_tiled(const uint16_t *x, cons
     __syncthreads();
     const int b = m & 1;
     if (32 * m + lane < nchunks) {
-      // this lane's chunk of the 8 tokens as float32, then per router row its
-      // chunk and 64 FMAs: every (row, token) chain takes the chunk's 8
-      // elements in increasing h
-      float xf[8][8];
+      // this lane's chunk of the warp's tokens as float32, then per router
+      // row its chunk and 8 x WT FMAs: every (row, token) chain takes the
+      // chunk's 8 elements in increasing h
+      float xf[WT][8];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) bf16x8_to_f32(*reinterpret_cast<const uint4 *>(&sx[b][wt + t][lane * 8]), xf[t]);
+      for (int t = 0; t < WT; ++t) bf16x8_to_f32(*reinterpret_cast<const uint4 *>(&sx[b][wt + t][lane * 8]), xf[t]);
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
         float wf[8];
@@ -1599,7 +1610,7 @@ __global__ void __launch_bounds__(RC * 8) k_router_tiled(const uint16_t *x, cons
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
-          for (int t = 0; t < 8; ++t) acc[r][t] = __fmaf_rn(wf[i], xf[t][i], acc[r][t]);
+          for (int t = 0; t < WT; ++t) acc[r][t] = __fmaf_rn(wf[i], xf[t][i], acc[r][t]);
       }
     }
     __syncthreads();
@@ -1607,17 +1618,17 @@ __global__ void __launch_bounds__(RC * 8) k_router_tiled(const uint16_t *x, cons
 #pragma unroll
   for (int r = 0; r < 8; ++r)
 #pragma unroll
-    for (int t = 0; t < 8; ++t)
+    for (int t = 0; t < WT; ++t)
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) acc[r][t] = __fadd_rn(acc[r][t], __shfl_xor_sync(0xFFFFFFFFu, acc[r][t], off));
-  // every lane holds every sum; spread the 64 stores over the lanes
+  // every lane holds every sum; spread the stores over the lanes
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     const int row = r0 + wr + r;
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
+    for (int t = 0; t < WT; ++t) {
       const int tok = t0 + wt + t;
-      if (lane == ((r * 8 + t) & 31) && row < rows && tok < T) {
+      if (lane == ((r * WT + t) & 31) && row < rows && tok < T) {
         if (row < E) logits[static_cast<size_t>(tok) * E + row] = f32_to_bf16(acc[r][t]);
         else shared_logit[tok] = f32_to_bf16(acc[r][t]);
       }
@@ -1652,7 +1663,7 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
     const int tok_tiles = (T + kRtTok - 1) / kRtTok;
     // 16-row tiles: at ~156 registers per thread three 4-warp CTAs fit per SM
     // (one 8-warp CTA with 32-row tiles), which hides more of the staging latency
-    cudaError_t e = launch_pdl(k_router_tiled<16>, dim3((rows + 15) / 16, tok_tiles), 128, 0, s, x, W, T, H, E,
+    cudaError_t e = launch_pdl(k_router_tiled<16, 4>, dim3((rows + 15) / 16, tok_tiles), 256, 0, s, x, W, T, H, E,
                                w_shared_gate, logits, shared_logit);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
@@ -1792,6 +1803,76 @@ __global__ void __launch_bounds__(128) k_softmax_topk(
 // to a power of two).  Max, exps, the canonical 32-lane sum, the key order
 // and the renorm are those of k_softmax_topk, so results are identical.
 constexpr int kRouteSmallTokens = 8;
+constexpr int kRouteSmallPairs = kRouteSmallTokens * 33;  // <= 8 tokens x (32 slots + shared)
+
+// Decode tiles of a few pairs straight from the routes in shared memory (one
+// CTA of 1024 threads): each pair's place in the stable bin order is counted
+// directly (bins, then pair index, as the grouping), and the runs of each bin
+// are cut into 8-pair tiles.  Writes order, tiles and n_tiles only: the
+// decode expert kernels read nothing else.  `sm` holds >= 5 * 264 ints.
+__device__ __forceinline__ void route_tiles(const uint32_t *s_route, int n_pairs, int shared_tokens, int E_arr,
+                                            int records, const GroupView &gv, uint32_t *err, int *sm) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_total = n_pairs + shared_tokens;
+  const int n_bins = gv.n_bins;
+  int *s_bin = sm;                          // [n_total]
+  int *s_ord = sm + kRouteSmallPairs;       // sorted position -> pair
+  int *s_less = sm + 2 * kRouteSmallPairs;  // sorted position -> first position of its bin
+  int *s_cnt = sm + 3 * kRouteSmallPairs;   // sorted position -> pairs in its bin
+  int *s_wsum = sm + 4 * kRouteSmallPairs;  // tile starts per warp
+  __shared__ int s_valid;
+  if (tid == 0) s_valid = 0;
+  if (tid < n_total) {
+    const int b = tid < n_pairs ? bin_of_route(s_route[tid], E_arr, records) : n_bins - 1;
+    s_bin[tid] = b;
+    if (b == -1) set_error(err, kErrBadRoute);
+  }
+  __syncthreads();
+  if (tid < n_total && s_bin[tid] >= 0) {
+    const int b = s_bin[tid];
+    int less = 0, before = 0, cnt = 0;
+    for (int j = 0; j < n_total; ++j) {
+      const int bj = s_bin[j];
+      less += (bj >= 0 && bj < b);
+      cnt += (bj == b);
+      before += (bj == b && j < tid);
+    }
+    const int r = less + before;
+    s_ord[r] = tid;
+    s_less[r] = less;
+    s_cnt[r] = cnt;
+    gv.order[r] = tid;
+    atomicAdd(&s_valid, 1);
+  }
+  __syncthreads();
+  const int n_valid = s_valid;
+  const bool start = tid < n_valid && ((tid - s_less[tid]) % kTokPerItem) == 0;
+  const unsigned bal = __ballot_sync(0xFFFFFFFFu, start);
+  if (lane == 0) s_wsum[warp] = __popc(bal);
+  __syncthreads();
+  int t = __popc(bal & ((1u << lane) - 1u));
+  for (int w = 0; w < warp; ++w) t += s_wsum[w];
+  if (start && t < gv.max_tiles) {
+    const int b = s_bin[s_ord[tid]];
+    const int off = tid - s_less[tid];
+    const int len = min(kTokPerItem, s_cnt[tid] - off);
+    int p[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) p[q] = q < len ? s_ord[tid + q] : -1;
+    const uint32_t key = (b < E_arr) ? static_cast<uint32_t>(b)
+                         : (b < E_arr + records) ? (kSlotBit | static_cast<uint32_t>(b - E_arr))
+                                                 : kSharedKey;
+    gv.tiles[3 * t] = make_int4(static_cast<int>(key), tid, len, b);
+    gv.tiles[3 * t + 1] = make_int4(p[0], p[1], p[2], p[3]);
+    gv.tiles[3 * t + 2] = make_int4(p[4], p[5], p[6], p[7]);
+  }
+  if (tid == 0) {
+    int total = 0;
+    for (int w = 0; w < 32; ++w) total += s_wsum[w];
+    gv.n_tiles[0] = min(total, gv.max_tiles);
+  }
+}
+
 
 template <int PER>
 __global__ void __launch_bounds__(1024) k_route_small(
@@ -1799,7 +1880,7 @@ __global__ void __launch_bounds__(1024) k_route_small(
     const uint32_t *__restrict__ route_map, int table_routes, uint32_t *inds, uint32_t *routes,
     uint16_t *raw_scores, uint16_t *scores, uint16_t *mass, const uint16_t *shl,
     uint16_t *shg, int shared_tokens, int E_arr, int records, GroupView gv, int seg_warps, double keep_threshold,
-    int min_keep, uint32_t *err) {
+    int min_keep, int tiles_only, uint32_t *err) {
   extern __shared__ int sm[];
   pdl_wait();
   pdl_trigger();
@@ -1807,6 +1888,7 @@ __global__ void __launch_bounds__(1024) k_route_small(
   uint32_t *kv = reinterpret_cast<uint32_t *>(sm);
   __shared__ float s_max[kRouteSmallTokens][32];
   __shared__ float s_sum[kRouteSmallTokens];
+  __shared__ uint32_t s_route[kRouteSmallTokens * 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tp = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
   const int wpt = 32 / tp;
@@ -1889,7 +1971,9 @@ __global__ void __launch_bounds__(1024) k_route_small(
       const uint32_t e = live ? idx : idx0;
       const size_t o = static_cast<size_t>(t) * k + lane;
       inds[o] = e;
-      routes[o] = !live ? kRouteNone : route_map ? route_map[e] : (table_routes ? (kSlotBit | e) : e);
+      const uint32_t route = !live ? kRouteNone : route_map ? route_map[e] : (table_routes ? (kSlotBit | e) : e);
+      routes[o] = route;
+      s_route[o] = route;
       if (raw_scores) raw_scores[o] = live ? f32_to_bf16(sel) : 0;
       if (scores) scores[o] = live ? f32_to_bf16(__fdiv_rn(sel, normalizer)) : 0;
     }
@@ -1899,6 +1983,10 @@ __global__ void __launch_bounds__(1024) k_route_small(
     }
   }
   __syncthreads();
+  if (tiles_only) {
+    route_tiles(s_route, T * k, shared_tokens, E_arr, records, gv, err, sm);
+    return;
+  }
   group_body(routes, T * k, shared_tokens, E_arr, records, gv, seg_warps, err, sm);
 }
 
@@ -1907,11 +1995,12 @@ cudaError_t launch_route_small(const uint16_t *logits, int T, int E, int k, floa
                                uint32_t *routes, uint16_t *raw_scores, uint16_t *scores,
                                uint16_t *mass, const uint16_t *shared_logit, uint16_t *shared_gate,
                                int shared_tokens, int array_experts, int table_records, GroupView gv,
-                               cudaStream_t s, double keep_threshold, int min_keep) {
+                               cudaStream_t s, double keep_threshold, int min_keep, bool tiles_only) {
   const int per = (E + 31) / 32;
   if (T > kRouteSmallTokens || per > 32 || k > 32) return cudaErrorNotSupported;
   int seg_warps = 1;
-  const size_t gsm = group_smem_bytes(T * k + shared_tokens, gv.n_bins, &seg_warps);
+  const size_t gsm = tiles_only ? 5 * kRouteSmallPairs * sizeof(int)
+                                : group_smem_bytes(T * k + shared_tokens, gv.n_bins, &seg_warps);
   const size_t smem = std::max(gsm, static_cast<size_t>(T) * E * sizeof(float));
 #define FNMOE_ROUTE_CASE(P)                                                                            \
   if (per <= P) {                                                                                      \
@@ -1923,7 +2012,7 @@ cudaError_t launch_route_small(const uint16_t *logits, int T, int E, int k, floa
     cudaError_t e = launch_pdl(k_route_small<P>, 1, 1024, smem, s, logits, T, E, k, blend, route_map,     \
                                table_routes, inds, routes, raw_scores, scores, mass, shared_logit,      \
                                shared_gate, shared_tokens, array_experts, table_records, gv, seg_warps, \
-                               keep_threshold, min_keep, device_error_word());                          \
+                               keep_threshold, min_keep, tiles_only ? 1 : 0, device_error_word());      \
     if (e != cudaSuccess) return e;                                                                    \
     return cudaGetLastError();                                                                         \
   }

@@ -59,13 +59,16 @@ cudaError_t launch_prep_rows(const uint16_t *rows, int n_rows, int K, int G,
                              uint16_t *limbs, float *meta, cudaStream_t s);
 
 // Softmax/top-k/renorm of <= 8 tokens followed by the grouping, one launch
-// (cudaErrorNotSupported when T or E is too large for it).
+// (cudaErrorNotSupported when T or E is too large for it).  tiles_only:
+// write only the decode tiles (with the pair order), not the per-bin counts
+// and offsets -- enough for the decode expert kernels.
 cudaError_t launch_route_small(const uint16_t *logits, int T, int E, int k, float blend,
                                const uint32_t *route_map, int table_routes, uint32_t *inds,
                                uint32_t *routes, uint16_t *raw_scores, uint16_t *scores,
                                uint16_t *mass, const uint16_t *shared_logit, uint16_t *shared_gate,
                                int shared_tokens, int array_experts, int table_records, GroupView gv,
-                               cudaStream_t s, double keep_threshold = 0.0, int min_keep = 0);
+                               cudaStream_t s, double keep_threshold = 0.0, int min_keep = 0,
+                               bool tiles_only = false);
 
 // Stable counting-sort grouping of routes (+ optional shared bin).
 cudaError_t launch_group(const uint32_t *routes, int n_pairs, int shared_tokens,

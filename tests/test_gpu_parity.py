@@ -129,6 +129,37 @@ def test_router_topk_bit_exact(cuda_lib, tokens, hidden, experts, zipf):
     assert_bf16_equal(_np(mass), o_mass[:, 0], "topk mass")
 
 
+@pytest.mark.parametrize("tokens", [3, 20])
+def test_router_topk_limits_bit_exact(cuda_lib, tokens):
+    """The interface limits: 1,024 experts (32 logits per lane) and top-k 16,
+    through the one-CTA (<= 8 tokens) and the warp-per-token top-k."""
+    from flashnext_b200 import router, synthetic
+    x = synthetic.bf16_normal((tokens, 1024), seed=41)
+    w = synthetic.bf16_normal((1024, 1024), 0.02, seed=42)
+    inds, scores, mass, logits = router.router_topk(x, w, 16)
+    o_inds, o_scores, o_mass, o_logits = moe.router(_np(x), _np(w), 16)
+    assert_bf16_equal(_np(logits), o_logits, "logits")
+    np.testing.assert_array_equal(_np(inds), o_inds)
+    assert_bf16_equal(_np(scores), o_scores, "renormalised scores")
+
+
+@pytest.mark.parametrize("tokens", [2, 24])
+def test_moe_layer_limits_bit_exact(cuda_lib, tokens):
+    """A layer with 1,024 experts and top-k 16 (grouping over 1,025 bins)."""
+    from flashnext_b200 import synthetic
+    from flashnext_b200.moe_block import SparseMoEBlock
+    L = synthetic.moe_layer(tokens, 512, 256, 1024, 16, 32, seed=tokens + 90)
+    block = SparseMoEBlock(L.router_weight, L.experts, top_k=16, shared=L.shared,
+                           shared_expert_gate=L.shared_expert_gate)
+    out = block(L.x)
+    nb = _bank_np(L.experts)
+    sh = {k: (_np(w), _np(s), _np(b)) for k, (w, s, b) in L.shared.items()}
+    ref = moe.moe_block(_np(L.x), _np(L.router_weight), 16, nb["gate_proj"], nb["up_proj"], nb["down_proj"],
+                        (sh["gate_proj"], sh["up_proj"], sh["down_proj"]), _np(L.shared_expert_gate))
+    np.testing.assert_array_equal(_np(block.last_inds), ref["inds"])
+    assert_bf16_equal(_np(out), ref["out"], "layer output")
+
+
 def test_router_ties_resolve_to_lower_expert(cuda_lib):
     import torch
 
