@@ -721,18 +721,22 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
   uint32_t *inds = a->inds_out ? a->inds_out : LL.inds;
   uint16_t *scores = a->scores_out ? static_cast<uint16_t *>(a->scores_out) : LL.scores;
 
-  if (!prefill) {
-    Prof p("prep_x", s);
-    e = launch_prep_rows(static_cast<const uint16_t *>(a->x), T, H, G, L.xl, L.xm, s);
-  }
-  if (e != cudaSuccess) return cuda_fail(e, "prep x");
+  // Small decode batches get the row fixed point of x from extra CTAs of the
+  // router launch; otherwise it is a launch of its own.
+  bool prep_done = false;
   {
     Prof p("router_logits", s);
     e = launch_router_logits(static_cast<const uint16_t *>(a->x), static_cast<const uint16_t *>(a->router_weight),
                              T, H, E, shared ? static_cast<const uint16_t *>(a->shared_expert_gate) : nullptr,
-                             logits, LL.shared_logit, s);
+                             logits, LL.shared_logit, s, prefill ? nullptr : L.xl, prefill ? nullptr : L.xm, G,
+                             &prep_done);
   }
   if (e != cudaSuccess) return cuda_fail(e, "router logits");
+  if (!prefill && !prep_done) {
+    Prof p("prep_x", s);
+    e = launch_prep_rows(static_cast<const uint16_t *>(a->x), T, H, G, L.xl, L.xm, s);
+    if (e != cudaSuccess) return cuda_fail(e, "prep x");
+  }
   e = cudaErrorNotSupported;
   if (T <= 8) {
     Prof p("route_group", s);

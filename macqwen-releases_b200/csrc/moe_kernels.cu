@@ -142,19 +142,19 @@ __device__ __forceinline__ uint32_t half_pair(int lo, int hi) {
 // out as one 16-byte store per limb in fragment order
 // [e0,e4,e1,e5,e2,e6,e3,e7], and each group's sum fl(SX) (G/8 consecutive
 // slices = consecutive lanes) from a shuffle reduction.
+// Body of the row fixed point for CTA `block` (TPR threads per row,
+// blockDim.x / TPR rows per CTA); shared by k_prep_rows and the small-batch
+// router launch, which runs it in extra CTAs.
 template <int G, int SPT>
-__global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *rows, int n_rows, int K, int TPR,
-                                                   uint16_t *__restrict__ limbs, float *__restrict__ meta,
-                                                   uint32_t *err) {
-  pdl_wait();
-  pdl_trigger();
+__device__ __forceinline__ void prep_rows_body(const uint16_t *rows, int n_rows, int K, int TPR, uint16_t *limbs,
+                                               float *meta, uint32_t *err, int block) {
   constexpr int LPG = G / 8;  // lanes per group
   __shared__ uint32_t s_mx[8][8];
   const int lane = threadIdx.x & 31;
   const int rl = threadIdx.x / TPR;  // row within the CTA
   const int tr = threadIdx.x - rl * TPR;
   const int wr = tr >> 5;            // warp within the row
-  const int row = blockIdx.x * (blockDim.x / TPR) + rl;
+  const int row = block * (blockDim.x / TPR) + rl;
   const bool live = row < n_rows;
   const int Gc = K / G;
   const int slices = K / 8;
@@ -230,6 +230,15 @@ __global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *rows, int n_r
     mrow[ai + 2] = 0.0f;
     mrow[ai + 3] = 0.0f;
   }
+}
+
+template <int G, int SPT>
+__global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *rows, int n_rows, int K, int TPR,
+                                                   uint16_t *__restrict__ limbs, float *__restrict__ meta,
+                                                   uint32_t *err) {
+  pdl_wait();
+  pdl_trigger();
+  prep_rows_body<G, SPT>(rows, n_rows, K, TPR, limbs, meta, err, blockIdx.x);
 }
 
 template <int G>
@@ -1430,11 +1439,24 @@ cudaError_t launch_combine(const uint16_t *d, const uint32_t *routes, const void
 // registers (lane j owns 8-element chunks j, j+32, ... of each) and runs the
 // canonical per-lane chain for every (row, token) of the block, reading each
 // staged input element once for both rows; then the xor butterfly.
+// With prep_limbs set, CTAs from router_ctas on (one per token row, blockDim
+// threads per row) compute the row fixed point of x instead (prep_rows_body),
+// which saves small batches a launch.
 template <int CH, int kRouterRW, int kRouterTok, int kRouterWarps>
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
     const uint16_t *x, const uint16_t *__restrict__ W, int T, int H, int E,
     const uint16_t *__restrict__ wsg, uint16_t *__restrict__ logits,
-    uint16_t *__restrict__ shared_logit) {
+    uint16_t *__restrict__ shared_logit, uint16_t *prep_limbs, float *prep_meta, int prep_G, int router_ctas,
+    uint32_t *err) {
+  if (prep_limbs != nullptr && static_cast<int>(blockIdx.x) >= router_ctas) {
+    constexpr int SPT = CH <= 4 ? 1 : CH <= 8 ? 2 : 4;
+    pdl_wait();
+    pdl_trigger();
+    const int block = blockIdx.x - router_ctas;
+    if (prep_G == 32) prep_rows_body<32, SPT>(x, T, H, blockDim.x, prep_limbs, prep_meta, err, block);
+    else prep_rows_body<64, SPT>(x, T, H, blockDim.x, prep_limbs, prep_meta, err, block);
+    return;
+  }
   extern __shared__ __align__(16) float xs[];  // [kRouterTok][H] float32
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = (blockIdx.x * kRouterWarps + warp) * kRouterRW;
@@ -1639,25 +1661,34 @@ __global__ void __launch_bounds__(RC / 8 * (kRtTok / WT) * 32) k_router_tiled(co
 template <int CH, int RW, int TOK, int NW = 8>
 cudaError_t launch_router_cfg(const uint16_t *x, const uint16_t *W, int T, int H, int E,
                               const uint16_t *w_shared_gate, uint16_t *logits, uint16_t *shared_logit,
-                              cudaStream_t s) {
+                              cudaStream_t s, uint16_t *prep_limbs = nullptr, float *prep_meta = nullptr,
+                              int prep_G = 32, bool *prep_done = nullptr) {
   const int rows = E + (w_shared_gate ? 1 : 0);
   const int rows_per_cta = NW * RW;
-  const dim3 grid((rows + rows_per_cta - 1) / rows_per_cta, (T + TOK - 1) / TOK);
+  const int router_ctas = (rows + rows_per_cta - 1) / rows_per_cta;
+  // the fused prep needs one token block and NW*32 threads covering a row in <= 4 passes
+  const bool prep = prep_limbs != nullptr && T <= TOK && H / 8 <= 4 * NW * 32;
+  const dim3 grid(router_ctas + (prep ? T : 0), (T + TOK - 1) / TOK);
   const size_t smem = static_cast<size_t>(TOK) * H * sizeof(float);
   auto kernel = k_router_logits<CH, RW, TOK, NW>;
-  if (smem > 48 * 1024) {
+  if (smem + 1024 > 48 * 1024) {  // the static shared memory (prep rows) counts toward the default limit
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  cudaError_t e = launch_pdl(kernel, grid, NW * 32, smem, s, x, W, T, H, E, w_shared_gate, logits, shared_logit);
+  cudaError_t e = launch_pdl(kernel, grid, NW * 32, smem, s, x, W, T, H, E, w_shared_gate, logits, shared_logit,
+                             prep ? prep_limbs : nullptr, prep_meta, prep_G, router_ctas, device_error_word());
   if (e != cudaSuccess) return e;
-  return cudaGetLastError();
+  e = cudaGetLastError();
+  if (prep_done != nullptr) *prep_done = prep && e == cudaSuccess;
+  return e;
 }
 
 cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, int H, int E,
                                  const uint16_t *w_shared_gate, uint16_t *logits,
-                                 uint16_t *shared_logit, cudaStream_t s) {
+                                 uint16_t *shared_logit, cudaStream_t s, uint16_t *prep_limbs, float *prep_meta,
+                                 int prep_G, bool *prep_done) {
   const int ch = (H / 8 + 31) / 32;
+  if (prep_done != nullptr) *prep_done = false;
   if (T >= 64 && H % 8 == 0) {
     const int rows = E + (w_shared_gate ? 1 : 0);
     const int tok_tiles = (T + kRtTok - 1) / kRtTok;
@@ -1671,10 +1702,15 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
   // Small batches: one router row per warp and 4-warp CTAs, so ~E/4 CTAs
   // share the weight read instead of E/16.
   if (T <= 4) {
-    if (ch <= 4) return launch_router_cfg<4, 1, 4, 4>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
-    if (ch <= 8) return launch_router_cfg<8, 1, 4, 4>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
-    if (ch <= 12) return launch_router_cfg<12, 1, 4, 4>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
-    if (ch <= 16) return launch_router_cfg<16, 1, 4, 4>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
+#define FNMOE_ROUTER_SMALL(C)                                                                                 \
+  if (ch <= C)                                                                                                  \
+    return launch_router_cfg<C, 1, 4, 4>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s, prep_limbs,    \
+                                         prep_meta, prep_G, prep_done);
+    FNMOE_ROUTER_SMALL(4)
+    FNMOE_ROUTER_SMALL(8)
+    FNMOE_ROUTER_SMALL(12)
+    FNMOE_ROUTER_SMALL(16)
+#undef FNMOE_ROUTER_SMALL
     return cudaErrorInvalidValue;
   }
   if (ch <= 4) return launch_router_cfg<4, 2, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);

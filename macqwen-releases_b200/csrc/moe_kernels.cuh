@@ -123,10 +123,15 @@ cudaError_t launch_combine(const uint16_t *d, const uint32_t *routes,
                            uint16_t *out, cudaStream_t s);
 
 // Router.
+// With prep_limbs / prep_meta set, batches of <= 4 tokens also compute the
+// row fixed point of x (launch_prep_rows' output) in extra CTAs of the same
+// launch; *prep_done tells whether that happened (else call launch_prep_rows).
 cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T,
                                  int H, int E, const uint16_t *w_shared_gate,
                                  uint16_t *logits, uint16_t *shared_logit,
-                                 cudaStream_t s);
+                                 cudaStream_t s, uint16_t *prep_limbs = nullptr,
+                                 float *prep_meta = nullptr, int prep_G = 32,
+                                 bool *prep_done = nullptr);
 cudaError_t launch_softmax_topk(const uint16_t *logits, int T, int E, int k,
                                 float blend, const uint32_t *route_map,
                                 int table_routes, uint32_t *inds,
