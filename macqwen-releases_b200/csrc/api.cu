@@ -758,8 +758,12 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
     if (e != cudaSuccess) return cuda_fail(e, "softmax_topk");
     {
       Prof p("group", s);
+      // the prefill GEMMs cut their own 128-pair tiles from the counts and
+      // offsets: no 8-pair decode tiles (max_tiles 0 skips writing them)
+      GroupView gv = L.gv;
+      if (prefill) gv.max_tiles = 0;
       e = launch_group(LL.routes, n_pairs, shared ? T : 0, call.array_experts,
-                       static_cast<int>(call.table.records), L.gv, s);
+                       static_cast<int>(call.table.records), gv, s);
     }
     if (e != cudaSuccess) return cuda_fail(e, "group");
   }
