@@ -621,6 +621,8 @@ struct LayerLayout {
   int32_t *n_ptiles;
   int max_ptiles;
   uint16_t *xg;        // prefill: x rows gathered into bin order [n_total][H]
+  int *ghist;          // prefill: per-chunk bin counts of the multi-CTA grouping
+  uint64_t ghist_bytes;
 };
 
 uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL) {
@@ -645,6 +647,8 @@ uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL) {
   LL.ptiles = cv.take<int4>(static_cast<uint64_t>(LL.max_ptiles));
   LL.n_ptiles = cv.take<int32_t>(4);
   LL.xg = layer_prefill(a) ? cv.take<uint16_t>(static_cast<uint64_t>(n_total) * a->hidden_size) : nullptr;
+  LL.ghist_bytes = layer_prefill(a) ? static_cast<uint64_t>((n_total + 4095) / 4096) * n_bins * sizeof(int) : 0;
+  LL.ghist = LL.ghist_bytes ? cv.take<int>(LL.ghist_bytes / sizeof(int)) : nullptr;
   return cv.off + 256;
 }
 
@@ -761,9 +765,16 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
       // the prefill GEMMs cut their own 128-pair tiles from the counts and
       // offsets: no 8-pair decode tiles (max_tiles 0 skips writing them)
       GroupView gv = L.gv;
-      if (prefill) gv.max_tiles = 0;
-      e = launch_group(LL.routes, n_pairs, shared ? T : 0, call.array_experts,
-                       static_cast<int>(call.table.records), gv, s);
+      e = cudaErrorNotSupported;
+      if (prefill) {
+        gv.max_tiles = 0;
+        e = launch_group_large(LL.routes, n_pairs, shared ? T : 0, call.array_experts,
+                               static_cast<int>(call.table.records), gv, LL.ghist, LL.ghist_bytes, s);
+        if (e != cudaSuccess && e != cudaErrorNotSupported) return cuda_fail(e, "group");
+      }
+      if (e == cudaErrorNotSupported)
+        e = launch_group(LL.routes, n_pairs, shared ? T : 0, call.array_experts,
+                         static_cast<int>(call.table.records), gv, s);
     }
     if (e != cudaSuccess) return cuda_fail(e, "group");
   }

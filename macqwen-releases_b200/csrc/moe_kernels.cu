@@ -498,6 +498,142 @@ cudaError_t launch_group(const uint32_t *routes, int n_pairs, int shared_tokens,
   return cudaGetLastError();
 }
 
+// Grouping of many pairs over many CTAs (prefill-sized batches, no decode
+// tiles): chunks of kGroupChunk pairs are counted per bin in parallel
+// (k_group_count), one CTA turns the per-chunk counts into each chunk's first
+// position inside every bin plus the bin counts and offsets (k_group_scan),
+// and every chunk scatters its pairs stably with the per-warp segments of the
+// single-CTA grouping (k_group_scatter).  Same order as k_group: by bin, then
+// pair index.
+constexpr int kGroupChunk = 4096;
+
+__global__ void __launch_bounds__(1024) k_group_count(const uint32_t *routes, int n_pairs, int shared_tokens,
+                                                      int E_arr, int records, int n_bins, int *hist, uint32_t *err) {
+  extern __shared__ int cnt[];  // [n_bins]
+  pdl_wait();
+  pdl_trigger();
+  const int n_total = n_pairs + shared_tokens;
+  const int i0 = blockIdx.x * kGroupChunk, i1 = min(i0 + kGroupChunk, n_total);
+  for (int b = threadIdx.x; b < n_bins; b += blockDim.x) cnt[b] = 0;
+  __syncthreads();
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const int b = bin_of_pair(routes, i, n_pairs, E_arr, records, n_bins);
+    if (b >= 0) atomicAdd(&cnt[b], 1);
+    else if (b == -1) set_error(err, kErrBadRoute);
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < n_bins; b += blockDim.x) hist[static_cast<size_t>(blockIdx.x) * n_bins + b] = cnt[b];
+}
+
+__global__ void __launch_bounds__(1024) k_group_scan(int *hist, int chunks, int E_arr, int records, GroupView gv) {
+  extern __shared__ int tot[];  // [n_bins]
+  __shared__ int warp_sums[32];
+  __shared__ int total_pairs;
+  pdl_wait();
+  pdl_trigger();
+  const int n_bins = gv.n_bins, tid = threadIdx.x;
+  for (int b = tid; b < n_bins; b += blockDim.x) {  // per bin: each chunk's exclusive prefix
+    int run = 0;
+    for (int c = 0; c < chunks; ++c) {
+      const int v = hist[static_cast<size_t>(c) * n_bins + b];
+      hist[static_cast<size_t>(c) * n_bins + b] = run;
+      run += v;
+    }
+    tot[b] = run;
+  }
+  __syncthreads();
+  const int per = (n_bins + 1023) / 1024;
+  const int b0 = min(tid * per, n_bins), b1 = min(b0 + per, n_bins);
+  int local = 0;
+  for (int b = b0; b < b1; ++b) local += tot[b];
+  int pre = block_exclusive_scan_1024(local, warp_sums, &total_pairs);
+  for (int b = b0; b < b1; ++b) {
+    const int c = tot[b];
+    gv.counts[b] = c;
+    gv.offsets[b] = pre;
+    gv.bin_key[b] = (b < E_arr) ? static_cast<uint32_t>(b)
+                    : (b < E_arr + records) ? (kSlotBit | static_cast<uint32_t>(b - E_arr))
+                                            : kSharedKey;
+    tot[b] = pre;  // first position of the bin
+    pre += c;
+  }
+  if (tid == 0) {
+    gv.offsets[n_bins] = total_pairs;
+    gv.n_tiles[0] = 0;  // no decode tiles from this grouping
+  }
+  __syncthreads();
+  for (int b = tid; b < n_bins; b += blockDim.x)
+    for (int c = 0; c < chunks; ++c) hist[static_cast<size_t>(c) * n_bins + b] += tot[b];
+}
+
+__global__ void __launch_bounds__(1024) k_group_scatter(const uint32_t *routes, int n_pairs, int shared_tokens,
+                                                        int E_arr, int records, int n_bins, const int *hist,
+                                                        int seg_warps, int32_t *order, uint32_t *err) {
+  extern __shared__ int sm[];
+  int *base = sm;            // [n_bins] this chunk's first position inside each bin
+  int *tbl = sm + n_bins;    // [seg_warps][n_bins]
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int n_total = n_pairs + shared_tokens;
+  const int c0 = blockIdx.x * kGroupChunk, c1 = min(c0 + kGroupChunk, n_total);
+  const int seg = ((c1 - c0 + seg_warps - 1) / seg_warps + 31) & ~31;
+  const int i0 = min(c0 + warp * seg, c1), i1 = min(i0 + seg, c1);
+  for (int b = tid; b < n_bins; b += blockDim.x) base[b] = hist[static_cast<size_t>(blockIdx.x) * n_bins + b];
+  for (int j = tid; j < seg_warps * n_bins; j += blockDim.x) tbl[j] = 0;
+  __syncthreads();
+  if (warp < seg_warps)
+    group_walk(routes, n_pairs, E_arr, records, n_bins, i0, i1, tbl + warp * n_bins, nullptr, nullptr, err);
+  __syncthreads();
+  for (int b = tid; b < n_bins; b += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < seg_warps; ++w) {
+      const int v = tbl[w * n_bins + b];
+      tbl[w * n_bins + b] = run;
+      run += v;
+    }
+  }
+  __syncthreads();
+  if (warp < seg_warps)
+    group_walk(routes, n_pairs, E_arr, records, n_bins, i0, i1, tbl + warp * n_bins, base, order, err);
+}
+
+cudaError_t launch_group_large(const uint32_t *routes, int n_pairs, int shared_tokens, int array_experts,
+                               int table_records, GroupView gv, int *hist, size_t hist_bytes, cudaStream_t s) {
+  const int n_total = n_pairs + shared_tokens;
+  const int chunks = (n_total + kGroupChunk - 1) / kGroupChunk;
+  const int n_bins = gv.n_bins;
+  if (chunks == 0 || hist == nullptr) return cudaErrorNotSupported;
+  if (static_cast<size_t>(chunks) * n_bins * sizeof(int) > hist_bytes) return cudaErrorNotSupported;
+  constexpr size_t kBudget = 200 * 1024;
+  const size_t per_bins = static_cast<size_t>(n_bins) * sizeof(int);
+  if (per_bins * 2 > kBudget) return cudaErrorNotSupported;
+  const int seg_warps = static_cast<int>(std::min<size_t>(32, (kBudget - per_bins) / per_bins));
+  const size_t scatter_smem = per_bins * (1 + seg_warps);
+  cudaError_t e;
+  if (per_bins > 48 * 1024) {
+    e = cudaFuncSetAttribute(k_group_count, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(per_bins));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_group_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(per_bins));
+    if (e != cudaSuccess) return e;
+  }
+  if (scatter_smem > 48 * 1024) {
+    e = cudaFuncSetAttribute(k_group_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(scatter_smem));
+    if (e != cudaSuccess) return e;
+  }
+  uint32_t *err = device_error_word();
+  e = launch_pdl(k_group_count, chunks, 1024, per_bins, s, routes, n_pairs, shared_tokens, array_experts,
+                 table_records, n_bins, hist, err);
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(k_group_scan, 1, 1024, per_bins, s, hist, chunks, array_experts, table_records, gv);
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(k_group_scatter, chunks, 1024, scatter_smem, s, routes, n_pairs, shared_tokens, array_experts,
+                 table_records, n_bins, static_cast<const int *>(hist), seg_warps, gv.order, err);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------------------
 // expert pointer resolution
 // ---------------------------------------------------------------------------

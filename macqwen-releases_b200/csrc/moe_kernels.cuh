@@ -70,6 +70,13 @@ cudaError_t launch_route_small(const uint16_t *logits, int T, int E, int k, floa
                                cudaStream_t s, double keep_threshold = 0.0, int min_keep = 0,
                                bool tiles_only = false);
 
+// The same grouping over many CTAs for large pair counts: counts, offsets,
+// bin keys and order only (no decode tiles; n_tiles = 0).  `hist` is scratch
+// of chunks * n_bins ints (chunks = ceil(pairs / 4096)); cudaErrorNotSupported
+// when it or the bins do not fit.
+cudaError_t launch_group_large(const uint32_t *routes, int n_pairs, int shared_tokens, int array_experts,
+                               int table_records, GroupView gv, int *hist, size_t hist_bytes, cudaStream_t s);
+
 // Stable counting-sort grouping of routes (+ optional shared bin).
 cudaError_t launch_group(const uint32_t *routes, int n_pairs, int shared_tokens,
                          int array_experts, int table_records, GroupView gv,
