@@ -59,6 +59,11 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Bulk prefetch of a global range into L2 (16-byte aligned address, size a
+// multiple of 16); a hint with no completion to wait for.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(src), "r"(bytes) : "memory");
+}
 // Order earlier generic shared-memory accesses before later async-proxy
 // (bulk copy) writes.
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }

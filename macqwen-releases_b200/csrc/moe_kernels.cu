@@ -62,6 +62,13 @@ bool pdl_enabled() {
   return on;
 }
 
+// FNMOE_NO_GEMV=1 runs small batches through k_expert_rows' 4-warp CTAs
+// instead of the K-split GEMV (same results; for comparisons).
+bool gemv_disabled() {
+  static const bool off = std::getenv("FNMOE_NO_GEMV") != nullptr;
+  return off;
+}
+
 DeviceInfo device_info() {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1163,12 +1170,29 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a,
 
   // Tiled tables hold whole row groups only: a warp whose rows start past
   // the last row has nothing to do (len -1 marks it: no bad-route error).
+  //
+  // Tiled tables: every warp asks L2 for its item's whole row-group range at
+  // setup (one bulk prefetch), so all of an item's blocks are in flight at
+  // once and the ring's copies find them in L2.  Small batches (4-warp CTAs,
+  // few experts) also prefetch, from the gate/up kernel, the row tile's share
+  // of the same expert's down record, which the down kernel then reads from L2.
   auto setup = [&](const RawDesc &rd, int rt, Src &src) {
     ItemInfo it = item_setup<DUAL, TILED>(a, rd, rt, ROWS, wbase, O, K, xs.Gc, nblk, lane, src);
     if (TILED && it.rt * ROWS + wbase >= O) {
       it.ok = false;
       it.len = -1;
       src = Src{nullptr, nullptr};
+    }
+    if (TILED && it.ok && lane == 0) {
+      bulk_prefetch_l2(src.w, static_cast<unsigned>(nblk) * kTileChunk);
+      uint32_t rec = 0;
+      if (DUAL && WARPS <= 4 && warp == 0 && a.tiled.down != nullptr &&
+          tiled_record(a, static_cast<uint32_t>(rd.d0.x), rec)) {
+        const uint64_t slice = (a.tiled.down_record / row_tiles) & ~static_cast<uint64_t>(15);
+        const uint64_t lo = slice * it.rt;
+        const uint64_t hi = it.rt == row_tiles - 1 ? a.tiled.down_record : lo + slice;
+        if (hi > lo) bulk_prefetch_l2(a.tiled.down + rec * a.tiled.down_record + lo, static_cast<unsigned>(hi - lo));
+      }
     }
     return it;
   };
@@ -1208,11 +1232,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a,
   int nb_cur = cur.ok ? nblk : 0;
   int nb_nxt = nxt.ok ? nblk : 0;
 
+  // tiled weight blocks (bulk copies on mbarriers) start before the
+  // activation stage lands; the generic layout shares the cp.async groups
+  if (TILED) ring_fill<G, R, TILED>(rg, sc, sn, nb_cur, nb_nxt, lane, rowbytes, xs.Gc, sb_mode);
   load_xstage(smem, s_pairs, xs, rd0, rd0.d0.z > 0, xl, xm, a.n_pairs, a.slots, DUAL);
   cp_async_commit();
   cp_async_wait<0>();
   __syncthreads();
-  ring_fill<G, R, TILED>(rg, sc, sn, nb_cur, nb_nxt, lane, rowbytes, xs.Gc, sb_mode);
+  if (!TILED) ring_fill<G, R, TILED>(rg, sc, sn, nb_cur, nb_nxt, lane, rowbytes, xs.Gc, sb_mode);
 
   for (int item = i0; item < i1; ++item) {
     if (!cur.ok) {
@@ -1259,6 +1286,196 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a,
   cp_async_wait<0>();
 }
 
+// Small decode batches on tiled tables: a K-split GEMV.  Work item = (tile,
+// one tiled row group: 8 gate + 8 up rows, or 16 down rows), one CTA of KS
+// warps (KS = min(4, blocks)).  Warp ks bulk-copies its contiguous share of
+// the row group's blocks (all at once, one mbarrier) and the activation limbs
+// and group sums fl(SX) of its groups, then writes the exact per-group MMA
+// sums S = C0 * 4096 + C1 of its groups to shared memory.  After a CTA
+// barrier warp 0 folds the groups in order with the same two fmas per group
+// as k_expert_rows -- scales and biases read from the staged chunks -- and
+// runs the same epilogue, so the results are bit-identical to it.  The work
+// of a long contraction is spread over KS warps instead of one, and an item
+// touches 20 KB (gate/up at K = 2048), so a batch of one token spreads over
+// every SM.  Pairs are processed 4 at a time (one MMA token tile); a tile
+// with more pairs takes several passes over the staged weights.
+constexpr int kGemvMaxBlocks = 16;
+
+template <int G, bool DUAL>
+__global__ void __launch_bounds__(128) k_expert_gemv(ExpertCallArgs a, GroupView gv, const uint16_t *xl,
+                                                     const float *xm, int P, uint16_t *out, uint16_t *g_out,
+                                                     uint16_t *u_out, uint32_t *err) {
+  constexpr int GPB = 2 * kBlkBytes / G;  // groups per block
+  constexpr int QG = GPB / 2;             // groups per half block
+  constexpr int WB = G / 32;
+  constexpr int RPW = DUAL ? 8 : 16;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t bar[4];
+  __shared__ int s_pairs[kTokPerItem];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KS = blockDim.x >> 5;
+  const int K = DUAL ? a.H : a.I;
+  const int O = DUAL ? a.I : a.H;
+  const XStage xs = xstage_geom(K, G);
+  const int Gc = xs.Gc;
+  const int nblk = (K / 2 + kBlkBytes - 1) / kBlkBytes;
+  const int n_rg = O / RPW;
+  if (lane == 0) {
+    mbar_init(bar + warp, 1);
+    mbar_init_fence();
+  }
+  __syncwarp();
+  pdl_wait();
+  pdl_trigger();
+  // the tile count and the whole descriptor in one round trip (the grid never
+  // exceeds max_tiles tiles, so the descriptor slot exists even past n_tiles)
+  const int tile = blockIdx.x / n_rg, rg = blockIdx.x - tile * n_rg;
+  const int n_tiles = gv.n_tiles[0];
+  const int4 d0 = gv.tiles[3 * tile];
+  const int4 dp = threadIdx.x < kTokPerItem ? gv.tiles[3 * tile + 1 + (threadIdx.x >> 2)] : make_int4(0, 0, 0, 0);
+  if (tile >= n_tiles) return;
+  const int len = d0.z;
+  if (len <= 0) return;  // nothing to run: issue no copy
+  uint32_t rec = 0;
+  if (!tiled_record(a, static_cast<uint32_t>(d0.x), rec)) {
+    if (threadIdx.x == 0) set_error(err, kErrBadRoute);
+    return;
+  }
+  if (threadIdx.x < kTokPerItem) {
+    const int q = threadIdx.x & 3;
+    s_pairs[threadIdx.x] = q == 0 ? dp.x : q == 1 ? dp.y : q == 2 ? dp.z : dp.w;
+  }
+  // smem: staged blocks | limbs [P][Xrow] | metadata [P][Mp] | sums [Gc][32] float2
+  uint8_t *stages = smem;
+  uint8_t *xst = stages + static_cast<size_t>(nblk) * kTileChunk;
+  const int m_off = P * xs.Xrow;
+  float2 *sums = reinterpret_cast<float2 *>(xst + ((m_off + P * xs.Mp + 15) & ~15));
+  const int b0 = warp * nblk / KS, b1 = (warp + 1) * nblk / KS;
+  const int g0 = b0 * GPB, g1 = min(b1 * GPB, Gc);
+  if (lane == 0 && b1 > b0) {
+    const uint8_t *base = (DUAL ? a.tiled.gate_up + rec * a.tiled.gate_up_record
+                                : a.tiled.down + rec * a.tiled.down_record) +
+                          static_cast<size_t>(rg) * nblk * kTileChunk;
+    fence_proxy_async();
+    mbar_expect_tx(bar + warp, static_cast<unsigned>(b1 - b0) * kTileChunk);
+    for (int b = b0; b < b1; ++b)
+      bulk_g2s(stages + static_cast<size_t>(b) * kTileChunk, base + static_cast<size_t>(b) * kTileChunk, kTileChunk,
+               bar + warp);
+  }
+  __syncthreads();  // s_pairs
+  const int r = lane >> 2, c = lane & 3;
+  const uint32_t x0 = smem_u32(xst);
+  const int passes = (len + P - 1) / P;
+  bool waited = false;
+  for (int pass = 0; pass < passes; ++pass) {
+    const int q0 = pass * P, np = min(P, len - q0);
+    // this warp's groups of the pass's pairs (and warp 0: every pair's {A, B})
+    for (int q = 0; q < np; ++q) {
+      const int pair = s_pairs[q0 + q];
+      const int row = DUAL ? token_of_pair(pair, a.n_pairs, a.slots) : pair;
+      const uint8_t *src = reinterpret_cast<const uint8_t *>(xl) + static_cast<size_t>(row) * xs.Xrow;
+      const uint8_t *msrc = reinterpret_cast<const uint8_t *>(xm) + static_cast<size_t>(row) * xs.Mp;
+      const int lb0 = g0 * 4 * G, lb1 = g1 * 4 * G;
+      for (int o = lb0 + lane * 16; o < lb1; o += 512) cp_async16(xst + q * xs.Xrow + o, src + o);
+      const int mb0 = g0 * 4, mb1 = (g1 * 4 + 15) & ~15;
+      for (int o = mb0 + lane * 16; o < mb1; o += 512) cp_async16(xst + m_off + q * xs.Mp + o, msrc + o);
+      if (warp == 0 && lane == 0) cp_async16(xst + m_off + q * xs.Mp + xs.a_off, msrc + xs.a_off);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    if (!waited && b1 > b0) {
+      uint32_t spins = 0;
+      while (!mbar_try_wait(bar + warp, 0)) {
+        if (++spins >= kSpinLimit) {
+          set_error(err, kErrTimeout);
+          break;
+        }
+      }
+    }
+    waited = true;
+    __syncwarp();
+    // exact group sums of this warp's blocks; token columns past np reuse pair np - 1
+    const uint32_t xb = x0 + min(r >> 1, np - 1) * xs.Xrow + (r & 1) * (G * 2) + c * 16;
+    for (int b = b0; b < b1; ++b) {
+      const uint32_t wq = smem_u32(stages + static_cast<size_t>(b) * kTileChunk) + (r * 4 + c) * 16;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint4 wA4 = lds128(wq + (2 * h) * 512);
+        const uint4 wB4 = lds128(wq + (2 * h + 1) * 512);
+#pragma unroll
+        for (int j = 0; j < QG; ++j) {
+          const int g = b * GPB + h * QG + j;
+          if (g >= Gc) break;
+          uint32_t A0[WB][4], A1[WB][4];
+#pragma unroll
+          for (int wb = 0; wb < WB; ++wb) nibble_operands(word_at(wA4, j * WB + wb), word_at(wB4, j * WB + wb), A0[wb], A1[wb]);
+          float C[4];
+#pragma unroll
+          for (int wb = 0; wb < WB; ++wb) {
+            const uint4 v = lds128(xb + g * (4 * G) + wb * 64);
+            if (wb == 0) mma_16816_z(C, A0[wb], v.x, v.y);
+            else mma_16816(C, A0[wb], v.x, v.y);
+            mma_16816(C, A1[wb], v.z, v.w);
+          }
+          sums[g * 32 + lane] = make_float2(__fmaf_rn(C[0], 4096.0f, C[1]), __fmaf_rn(C[2], 4096.0f, C[3]));
+        }
+      }
+    }
+    // canonical fold over the groups in order (k_expert_rows' group_step):
+    // warp 0 folds its own blocks, the first ones, before the barrier and the
+    // other warps' blocks after it
+    const uint32_t mrow = x0 + m_off + min(c, np - 1) * xs.Mp;
+    float accA = -0.0f, accB = -0.0f;
+    auto fold = [&](int bs, int be) {
+      for (int b = bs; b < be; ++b) {
+        // the block's scales and biases of rows r (A) and r + 8 (B): 8 bf16 each
+        const uint32_t sbA = smem_u32(stages + static_cast<size_t>(b) * kTileChunk) + kTileW + r * 32;
+        const uint4 sA8 = lds128(sbA), bA8 = lds128(sbA + 16);
+        const uint4 sB8 = lds128(sbA + 8 * 32), bB8 = lds128(sbA + 8 * 32 + 16);
+#pragma unroll
+        for (int j = 0; j < GPB; ++j) {
+          const int g = b * GPB + j;
+          if (g >= Gc) break;
+          const int sh = 16 * (j & 1);
+          const float sA = bf16_to_f32(static_cast<uint16_t>(word_at(sA8, j >> 1) >> sh));
+          const float bA = bf16_to_f32(static_cast<uint16_t>(word_at(bA8, j >> 1) >> sh));
+          const float sB = bf16_to_f32(static_cast<uint16_t>(word_at(sB8, j >> 1) >> sh));
+          const float bB = bf16_to_f32(static_cast<uint16_t>(word_at(bB8, j >> 1) >> sh));
+          const float fs = __uint_as_float(lds32(mrow + 4 * g));
+          const float2 S = sums[g * 32 + lane];
+          accA = __fmaf_rn(bA, fs, __fmaf_rn(sA, S.x, accA));
+          accB = __fmaf_rn(bB, fs, __fmaf_rn(sB, S.y, accB));
+        }
+      }
+    };
+    if (warp == 0) fold(0, b1);
+    __syncthreads();
+    if (warp == 0) {
+      fold(b1, nblk);
+      if (c < np) {
+        const int pair = s_pairs[q0 + c];
+        const uint2 abw = lds64(mrow + xs.a_off);
+        const float2 ab = make_float2(__uint_as_float(abw.x), __uint_as_float(abw.y));
+        const float yA = __fmul_rn(__fmul_rn(accA, ab.x), ab.y);
+        const float yB = __fmul_rn(__fmul_rn(accB, ab.x), ab.y);
+        const int oA = rg * RPW + r;
+        if (DUAL) {
+          const float gvv = round_bf16(yA), uvv = round_bf16(yB);
+          out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(swiglu_bf16(g_exp_bf16, gvv, uvv));
+          if (g_out != nullptr && pair < a.n_pairs) {
+            g_out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(gvv);
+            u_out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(uvv);
+          }
+        } else {
+          out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(yA);
+          out[static_cast<size_t>(pair) * O + oA + 8] = f32_to_bf16(yB);
+        }
+      }
+    }
+    if (pass + 1 < passes) __syncthreads();  // sums and limbs are rewritten by the next pass
+  }
+}
+
 namespace {
 
 constexpr size_t kSmemLimit = 227 * 1024;
@@ -1301,13 +1518,54 @@ cudaError_t launch_ring(const ExpertCallArgs &a, const GroupView &gv, int K, con
   return cudaErrorInvalidValue;
 }
 
+// Shared memory of k_expert_gemv for P pairs per pass.
+size_t gemv_smem(int K, int G, int P) {
+  const XStage xs = xstage_geom(K, G);
+  const int nblk = (K / 2 + kBlkBytes - 1) / kBlkBytes;
+  const size_t x = (static_cast<size_t>(P) * (xs.Xrow + xs.Mp) + 15) & ~static_cast<size_t>(15);
+  return static_cast<size_t>(nblk) * kTileChunk + x + static_cast<size_t>(xs.Gc) * 32 * sizeof(float2);
+}
+
+template <int G, bool DUAL>
+cudaError_t launch_gemv(const ExpertCallArgs &a, const GroupView &gv, int K, const uint16_t *xl, const float *xm,
+                        uint16_t *out, uint16_t *g_out, uint16_t *u_out, cudaStream_t s) {
+  const int O = DUAL ? a.I : a.H;
+  const int rpw = DUAL ? 8 : 16;
+  const int nblk = (K / 2 + kBlkBytes - 1) / kBlkBytes;
+  if (nblk > kGemvMaxBlocks || O % rpw != 0) return cudaErrorNotSupported;
+  const int ks = std::min(4, nblk);
+  const int P = std::min(4, std::max(1, a.tokens));
+  const size_t smem = gemv_smem(K, G, P);
+  if (smem > kSmemLimit) return cudaErrorNotSupported;
+  auto kernel = k_expert_gemv<G, DUAL>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  // every tile holds at least one pair: pairs + shared tokens bound the tiles
+  const long long tiles = std::min<long long>(gv.max_tiles, static_cast<long long>(a.n_pairs) + a.tokens);
+  const long long grid = tiles * (O / rpw);
+  if (grid <= 0) return cudaSuccess;
+  if (grid > 0x7FFFFFFF) return cudaErrorNotSupported;
+  cudaError_t e = launch_pdl(kernel, static_cast<int>(grid), ks * 32, smem, s, a, gv, xl, xm, P, out, g_out, u_out,
+                             device_error_word());
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 template <int G, bool DUAL, bool TILED>
 cudaError_t launch_width(const ExpertCallArgs &a, const GroupView &gv, int K, const uint16_t *xl, const float *xm,
                          uint16_t *out, uint16_t *g_out, uint16_t *u_out, int sb_mode, cudaStream_t s) {
   // Many pairs -> 16-warp CTAs (one per SM); few pairs (batch-1 decode) ->
   // 4-warp CTAs so that the handful of experts still spreads over every SM.
+  // Tiled tables and few pairs: the K-split GEMV spreads each expert's rows
+  // over many more warps.
   if ((a.n_pairs + a.tokens) >= 64)
     return launch_ring<G, 16, DUAL, TILED>(a, gv, K, xl, xm, out, g_out, u_out, sb_mode, s);
+  if (TILED && !gemv_disabled()) {
+    cudaError_t e = launch_gemv<G, DUAL>(a, gv, K, xl, xm, out, g_out, u_out, s);
+    if (e != cudaErrorNotSupported) return e;
+  }
   return launch_ring<G, 4, DUAL, TILED>(a, gv, K, xl, xm, out, g_out, u_out, sb_mode, s);
 }
 
@@ -1936,8 +2194,7 @@ __global__ void __launch_bounds__(128) k_softmax_topk(
     uint32_t best = 0u;
 #pragma unroll
     for (int m = 0; m < kMaxPerLane; ++m) best = max(best, key[m]);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, off));
+    best = __reduce_max_sync(0xFFFFFFFFu, best);  // one redux.sync: keys are unique, order-free
 #pragma unroll
     for (int m = 0; m < kMaxPerLane; ++m)
       if (key[m] == best) key[m] = 0u;
@@ -2117,8 +2374,7 @@ __global__ void __launch_bounds__(1024) k_route_small(
       uint32_t best = 0u;
 #pragma unroll
       for (int m = 0; m < PER; ++m) best = max(best, key[m]);
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, off));
+      best = __reduce_max_sync(0xFFFFFFFFu, best);  // one redux.sync: keys are unique, order-free
 #pragma unroll
       for (int m = 0; m < PER; ++m)
         if (key[m] == best) key[m] = 0u;

@@ -407,6 +407,7 @@ def test_moe_layer_with_expert_table(cuda_lib):
     (64, 2048, 512, 512, 32),   # headline layer, Zipf routing
     (5, 2560, 640, 24, 32),     # down rows (320 bytes) end in a partial block; Gc = 20
     (7, 1024, 256, 16, 64),     # group size 64
+    (2, 1024, 256, 16, 64),     # group size 64, small-batch K-split path
     (3, 3072, 640, 12, 32),     # qwen4 full-depth layer shape
 ])
 def test_tiled_layer_matches_arrays_and_oracle(cuda_lib, tokens, hidden, inter, experts, group):
