@@ -157,12 +157,22 @@ def _barrier(world):
 # --------------------------------------------------------------------------
 
 
-def cpu_sample_inputs(tokens: int, seed: int = 0):
-    """NumPy inputs with the workload's shapes, restricted to the experts the
-    sampled tokens route to (the oracle only touches those)."""
+# The C2 layer on the host cores.  One step = the whole 64-token layer: the
+# router (softmax, top-k, renorm) in the parent, the routed experts' groups
+# split over spawn worker processes (the oracle's per-expert projections), the
+# shared expert as one more task, then the slot-ordered combine.  Expert
+# weights are generated once per process from a per-expert seed (each worker
+# holds only its experts; they stay resident, as the GPU's tables do).
+
+_CPU_STATE: dict = {}
+
+
+def _cpu_layer_inputs(tokens: int, seed: int):
+    """x [T,H] and router weight [E,H] (bfloat16 values as float32) with the
+    C2 distributions: Zipf(1.1) expert popularity through a shared direction."""
     import numpy as np
 
-    from oracle import bf16, moe
+    from oracle import bf16
 
     rng = np.random.default_rng(seed)
     u = rng.standard_normal(HIDDEN)
@@ -171,99 +181,171 @@ def cpu_sample_inputs(tokens: int, seed: int = 0):
     p = ranks ** -1.1
     p /= p.sum()
     x = bf16.round_f32((rng.standard_normal((tokens, HIDDEN)) + 8.0 * u).astype(np.float32))
-    w = bf16.round_f32((rng.standard_normal((EXPERTS, HIDDEN)) * 0.02 + (0.43 * np.log(p) / 8.0)[:, None] * u).astype(np.float32))
-    inds, _, _, _ = moe.router(x, w, TOP_K)
-    used = np.unique(inds)
-
-    def proj(o, k, n=EXPERTS):
-        # Only routed experts are materialised; the rest are never read.
-        words = np.zeros((n, o, k // 8), np.uint32)
-        s = np.zeros((n, o, k // GROUP), np.float32)
-        for e in (used if n == EXPERTS else range(n)):
-            words[e] = rng.integers(0, 2 ** 32, (o, k // 8), dtype=np.uint32)
-            s[e] = bf16.round_f32(np.abs(rng.normal(0, 0.01, (o, k // GROUP))).astype(np.float32))
-        return words, s, bf16.round_f32(-8 * s)
-
-    gate, up, down = proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER)
-    sh = tuple(tuple(a[0] for a in t) for t in (proj(INTER, HIDDEN, 1), proj(INTER, HIDDEN, 1), proj(HIDDEN, INTER, 1)))
+    w = bf16.round_f32((rng.standard_normal((EXPERTS, HIDDEN)) * 0.02
+                        + (0.43 * np.log(p) / 8.0)[:, None] * u).astype(np.float32))
     wg = bf16.round_f32((rng.standard_normal(HIDDEN) * 0.02).astype(np.float32))
-    return x, w, gate, up, down, sh, wg, len(used)
+    return x, w, wg
 
 
-def _cpu_worker(job):
-    """One host process: time the oracle on its own 4-token sample for `seconds`."""
-    seed, seconds = job
-    from oracle import moe
+def _cpu_expert(seed: int, e: int):
+    """(gate, up, down) of expert e (e = -1: the shared expert) as oracle triples."""
+    import numpy as np
 
-    tokens = 4
-    x, w, gate, up, down, sh, wg, used = cpu_sample_inputs(tokens, seed=seed)
-    moe.moe_block(x, w, TOP_K, gate, up, down, sh, wg)  # warm-up
-    t0 = time.perf_counter()
-    done = 0
-    while True:
-        moe.moe_block(x, w, TOP_K, gate, up, down, sh, wg)
-        done += tokens
-        if time.perf_counter() - t0 >= seconds:
-            break
-    return done, time.perf_counter() - t0, used
+    from oracle import bf16
+
+    rng = np.random.default_rng([seed, e + 1])
+
+    def proj(o, k):
+        words = rng.integers(0, 2 ** 32, (o, k // 8), dtype=np.uint32)
+        sc = bf16.round_f32(np.abs(rng.normal(0, 0.01, (o, k // GROUP))).astype(np.float32))
+        return words, sc, bf16.round_f32(-8 * sc)
+
+    return proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER)
 
 
-def _cpu_pool_run(seconds: float, workers: int):
-    """Run the oracle in `workers` single-threaded spawn processes at once.
-
-    Returns (tokens/s summed over workers, sample description, workers)."""
-    import multiprocessing as mp
-
+def _cpu_worker_init(seed: int, tokens: int):
     for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
-        os.environ[var] = "1"  # one thread per worker process (inherited at spawn)
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(workers) as pool:
-        res = pool.map(_cpu_worker, [(1000 + i, seconds) for i in range(workers)])
-    rate = sum(d / el for d, el, _ in res)
-    tokens = sum(d for d, _, _ in res)
-    experts = sum(u for _, _, u in res) / len(res)
-    sample = (f"{workers} spawn processes x {seconds:.0f} s, each timing 4-token batches of the workload "
-              f"(own seeded sample, ~{experts:.0f} distinct experts); {tokens} tokens in total")
-    return rate, sample, workers
+        os.environ[var] = "1"
+    x, _, wg = _cpu_layer_inputs(tokens, seed)
+    _CPU_STATE.update(seed=seed, x=x, wg=wg, experts={})
+
+
+def _cpu_task(job):
+    """Worker: the per-slot down rows of its expert groups, or the shared expert."""
+    import numpy as np
+
+    from oracle import bf16, moe
+
+    kind, payload = job
+    st = _CPU_STATE
+    x = st["x"]
+    if kind == "shared":
+        if "shared" not in st:
+            st["shared"] = _cpu_expert(st["seed"], -1)
+        sh, sg, sy = moe.shared_expert(x, *st["shared"], st["wg"])
+        return kind, sy
+    out = []
+    for e, pairs in payload:
+        if e not in st["experts"]:
+            st["experts"][e] = _cpu_expert(st["seed"], e)
+        gate, up, down = st["experts"][e]
+        rows = x[np.asarray(pairs) // TOP_K]
+        g = bf16.round_f32(moe.qmv(rows, moe.unpack_q4(gate[0]), gate[1], gate[2], GROUP))
+        u = bf16.round_f32(moe.qmv(rows, moe.unpack_q4(up[0]), up[1], up[2], GROUP))
+        act = moe.swiglu_bf16(g, u)
+        d = bf16.round_f32(moe.qmv(act, moe.unpack_q4(down[0]), down[1], down[2], GROUP))
+        out.append((pairs, d))
+    return kind, out
+
+
+class CpuLayer:
+    """The C2 layer (64 tokens) on `workers` host processes; step() runs it once."""
+
+    def __init__(self, workers: int, tokens: int = 64, seed: int = 1000):
+        import multiprocessing as mp
+
+        for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+            os.environ[var] = "1"  # one thread per process (inherited at spawn)
+        self.tokens, self.seed, self.workers = tokens, seed, workers
+        self.x, self.w, _ = _cpu_layer_inputs(tokens, seed)
+        self.pool = mp.get_context("spawn").Pool(workers, initializer=_cpu_worker_init, initargs=(seed, tokens))
+        self.distinct = None
+
+    def step(self):
+        import numpy as np
+
+        from oracle import moe
+
+        inds, scores, _, _ = moe.router(self.x, self.w, TOP_K)
+        flat = inds.reshape(-1)
+        experts = np.unique(flat)
+        self.distinct = int(experts.size)
+        groups = [(int(e), np.nonzero(flat == e)[0].tolist()) for e in experts]
+        # largest groups first, dealt round-robin: balanced per-process work
+        groups.sort(key=lambda g: -len(g[1]))
+        jobs = [("routed", groups[i::self.workers]) for i in range(self.workers)] + [("shared", None)]
+        d = np.zeros((self.tokens * TOP_K, HIDDEN), np.float32)
+        sy = None
+        for kind, res in self.pool.map(_cpu_task, jobs, chunksize=1):
+            if kind == "shared":
+                sy = res
+            else:
+                for pairs, rows in res:
+                    d[pairs] = rows
+        return moe.combine(d.reshape(self.tokens, TOP_K, HIDDEN), scores, shared_y=sy)
+
+    def close(self):
+        self.pool.terminate()
+        self.pool.join()
 
 
 def _cpu_workers():
     return max(1, min(os.cpu_count() or 1, 32))
 
 
-def cpu_baseline(target_s: float = 12.0):
-    """Time the oracle port on all host cores; returns (tokens/s, sample, cores)."""
-    return _cpu_pool_run(target_s, _cpu_workers())
+def cpu_time_steps(steps: int, warmup: int, workers: int | None = None):
+    """Wall time of `steps` CPU layer steps after `warmup` (each step one 64-token layer)."""
+    workers = workers or _cpu_workers()
+    layer = CpuLayer(workers)
+    try:
+        for _ in range(max(1, warmup)):  # the first step also generates each worker's experts
+            layer.step()
+        times = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            layer.step()
+            times.append(time.perf_counter() - t0)
+    finally:
+        layer.close()
+    return times, layer.distinct, workers
+
+
+def cpu_baseline(steps: int = 4):
+    """The C2 layer on all host cores; returns (tokens/s, sample, cores)."""
+    times, distinct, workers = cpu_time_steps(steps, 1)
+    rate = 64 * len(times) / sum(times)
+    sample = (f"{len(times)} steps of the 64-token C2 layer (router in the parent; {distinct} distinct experts "
+              f"split over {workers} spawn processes + the shared expert; median "
+              f"{1000 * statistics.median(times):.0f} ms/step)")
+    return rate, sample, workers
 
 
 def reference_arm(args):
     world, rank, _ = _dist()
     if rank != 0:
         return 0
-    sample_s = max(2.0, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
-    workers = _cpu_workers()
-    if args.warmup:
-        _cpu_pool_run(min(2.0, sample_s), workers)
-    rates = []
-    samples = []
-    for _ in range(args.steps):
-        r, sample, _ = _cpu_pool_run(sample_s, workers)
-        rates.append(r)
-        samples.append(sample)
-    value = statistics.mean(rates)
+    times, distinct, workers = cpu_time_steps(args.steps, args.warmup)
+    total = sum(times)
+    value = 64 * len(times) / total
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sample_s,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "C2: one MoE layer, 64-token ragged decode, Zipf(1.1) routing, H2048/I512/E512 top-10 Q4/G32 + shared",
-                   "sample": "4-token batches per worker process"},
+        "config": {"workload": "C2: one qwen4_exp MoE layer, 64-token ragged decode, Zipf(1.1) routing, "
+                               "H2048/I512/E512 top-10 Q4/G32 + Q4/G32 shared expert",
+                   "tokens_per_gpu": 64, "distinct_experts_per_layer": distinct},
+        "step_ms": {"median": 1000 * statistics.median(times), "p10": 1000 * _pct(times, 10),
+                    "p90": 1000 * _pct(times, 90)},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": workers, "kind": "port",
-                         "sample": f"each step: {samples[-1]}"},
+                         "sample": f"{len(times)} steps, each the whole 64-token layer: router in the parent, "
+                                   f"{distinct} expert groups over {workers} spawn processes + the shared expert"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "NumPy restatement of the reference semantics on host cores (the MLX runtime of the reference is not installable here)",
+        "note": "NumPy restatement of the reference semantics on host cores (the MLX runtime of the "
+                "reference is not installable here)",
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def _pct(values, q):
+    """q-th percentile (linear interpolation) of a list of numbers."""
+    v = sorted(values)
+    if not v:
+        return None
+    pos = (len(v) - 1) * q / 100.0
+    lo = int(pos)
+    hi = min(lo + 1, len(v) - 1)
+    return v[lo] + (v[hi] - v[lo]) * (pos - lo)
 
 
 # --------------------------------------------------------------------------

@@ -4,9 +4,13 @@
  * Every entry point takes plain device pointers, sizes and a cudaStream_t
  * passed as `void*` (NULL = legacy default stream).  Nothing here allocates
  * device memory: scratch comes from a caller-provided workspace whose size
- * the matching *_workspace_size call reports.  Each call returns FNMOE_OK (0)
- * or a negative FNMOE_ERR_* code; fnmoe_get_last_error() returns the message
- * of the calling thread's last failure.
+ * the matching *_workspace_size call reports -- except
+ * fnmoe_moe_execute_static, whose scratch is a fixed array inside the
+ * library.  A workspace may start at any address: the library rounds its
+ * start up to a 256-byte boundary, and the reported sizes include the 256
+ * bytes that rounding can skip.  Each call returns FNMOE_OK (0) or a negative
+ * FNMOE_ERR_* code; fnmoe_get_last_error() returns the message of the
+ * calling thread's last failure.
  *
  * Reference interfaces replaced (paths inside 1architect/macqwen-releases):
  *   fnmoe_available / fnmoe_get_last_error
@@ -281,13 +285,16 @@ FNMOE_API int fnmoe_moe_execute(const FnMoEArgs *args, void *stream);
  * allocator (a C or ctypes bridge like the reference's native one, which
  * keeps process-wide scratch instead of per-call buffers).  No reference
  * counterpart: the reference's bridge allocates and caches its scratch.
- * A call whose fnmoe_moe_workspace_size exceeds the static size fails with
- * FNMOE_ERR_WORKSPACE.  The scratch is shared by every call on a device:
- * calls that may overlap on the GPU (other streams, other threads) race and
- * must be serialised by the caller.  Its contents persist between calls;
- * nothing in it needs to start at zero (each call rewrites what it reads).
- * The first call on a device resolves the array's address
- * (cudaGetSymbolAddress); make that first call before any stream capture. */
+ * A call whose scratch (fnmoe_moe_workspace_size less its 256 bytes of
+ * alignment slack, which the aligned array does not need) exceeds the static
+ * size fails with FNMOE_ERR_WORKSPACE.  The scratch is shared by every call
+ * on a device: calls that may overlap on the GPU (other streams, other
+ * threads) race and must be serialised by the caller.  Its contents persist
+ * between calls; nothing in it needs to start at zero (each call rewrites
+ * what it reads).  Every call resolves the array's address on the current
+ * device (cudaGetSymbolAddress; no allocation, no synchronisation); the first
+ * call on a device may load the library's device code, so make that first
+ * call before any stream capture. */
 FNMOE_API int fnmoe_moe_execute_static(const FnMoEArgs *args, void *stream);
 
 /* Combine-only probe: out[t,h] = sum_s outputs[t,s,h]*scores[t,s] (float32),

@@ -66,11 +66,23 @@ int cuda_fail(cudaError_t e, const char *where) {
 }
 
 // Bump allocator over the caller's workspace (or a size probe when base is
-// null).  Every carve is 256-byte aligned.
+// null).  The base is first rounded up to a 256-byte boundary (`shift`
+// bytes of the workspace are skipped), so every carve is 256-byte aligned
+// whatever pointer the caller passes; the *_workspace_size calls add 256
+// bytes of slack for that shift.
+constexpr uint64_t kWorkspaceSlack = 256;
+
 struct Carver {
   uint8_t *base;
+  uint64_t shift = 0;
   uint64_t off = 0;
-  explicit Carver(void *b) : base(static_cast<uint8_t *>(b)) {}
+  explicit Carver(void *b) : base(static_cast<uint8_t *>(b)) {
+    if (base != nullptr) {
+      const uintptr_t p = reinterpret_cast<uintptr_t>(base);
+      shift = ((p + 255) & ~uintptr_t(255)) - p;
+      base += shift;
+    }
+  }
   template <typename T>
   T *take(uint64_t count) {
     off = (off + 255) & ~uint64_t(255);
@@ -78,6 +90,8 @@ struct Carver {
     off += count * sizeof(T);
     return p;
   }
+  // workspace bytes the carves so far use, the alignment shift included
+  uint64_t used() const { return shift + off; }
 };
 
 bool device_ok(std::string &why) {
@@ -194,7 +208,8 @@ int validate_moe(const FnMoEArgs *a) {
   return FNMOE_OK;
 }
 
-uint64_t moe_workspace(const FnMoEArgs *a) {
+// Bytes of the executor's carves from a 256-byte aligned base (no slack).
+uint64_t moe_workspace_aligned(const FnMoEArgs *a) {
   Carver cv(nullptr);
   Layout L{};
   const bool has_table = a->table.base != nullptr;
@@ -202,8 +217,11 @@ uint64_t moe_workspace(const FnMoEArgs *a) {
   const int n_total = static_cast<int>(a->tokens * a->slots);
   const bool per_slot = (a->flags & (FNMOE_FLAG_RETURN_ALL | FNMOE_FLAG_NO_COMBINE)) || a->scores == nullptr;
   carve_core(cv, L, a->tokens, a->hidden_size, a->inter_size, a->group_size, n_total, n_bins, !per_slot);
-  return cv.off + 256;
+  return cv.off;
 }
+
+// Workspace bytes for any base pointer (aligned carves plus the slack).
+uint64_t moe_workspace(const FnMoEArgs *a) { return moe_workspace_aligned(a) + kWorkspaceSlack; }
 
 bool aligned(const void *p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) & (n - 1)) == 0; }
 
@@ -285,28 +303,22 @@ ExpertCallArgs make_call(const FnMoEArgs *a) {
 }  // namespace
 
 // Library-owned scratch of fnmoe_moe_execute_static: file-scope device
-// storage, no runtime allocation.  Its address is looked up once per device.
+// storage, no runtime allocation.
 static __device__ __align__(256) uint8_t g_static_scratch[FNMOE_STATIC_SCRATCH_BYTES];
 
 namespace {
 
-std::mutex g_static_mu;
-std::map<int, void *> g_static_ptr;  // device -> address of g_static_scratch
-
+// Device address of g_static_scratch on the current device.  In host code
+// the symbol's name is only a host-side stand-in, so the address is looked
+// up with the device current, on every call: the lookup allocates nothing
+// and does not synchronise, and a per-device cache would outlive a
+// cudaDeviceReset (or primary-context teardown) and hand out a stale
+// address afterwards.  The first lookup on a device may load the library's
+// device code, which is why the first call belongs before any stream capture.
 int static_scratch(void **ptr) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "static scratch: cudaGetDevice");
-  std::lock_guard<std::mutex> lock(g_static_mu);
-  auto it = g_static_ptr.find(dev);
-  if (it != g_static_ptr.end()) {
-    *ptr = it->second;
-    return FNMOE_OK;
-  }
   void *p = nullptr;
-  e = cudaGetSymbolAddress(&p, g_static_scratch);
+  cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
   if (e != cudaSuccess || p == nullptr) return cuda_fail(e, "static scratch: cudaGetSymbolAddress");
-  g_static_ptr[dev] = p;
   *ptr = p;
   return FNMOE_OK;
 }
@@ -351,9 +363,8 @@ int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
   if (v != FNMOE_OK) return v;
   std::string why;
   if (!device_ok(why)) return fail(FNMOE_ERR_DEVICE, why);
-  const uint64_t need = moe_workspace(a);
-  if (a->workspace == nullptr || a->workspace_bytes < need)
-    return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes");
+  if (a->workspace == nullptr)
+    return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(moe_workspace(a)) + " bytes");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = ensure_exp_table(s);
   if (e != cudaSuccess) return cuda_fail(e, "exp table");
@@ -369,6 +380,8 @@ int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
   Carver cv(a->workspace);
   Layout L{};
   carve_core(cv, L, T, H, I, G, n_pairs, n_bins, !per_slot);
+  if (cv.used() > a->workspace_bytes)
+    return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(moe_workspace(a)) + " bytes");
   uint16_t *d = per_slot ? static_cast<uint16_t *>(a->down_out) : L.d;
   ExpertCallArgs call = make_call(a);
   if (int rc = check_expert_alignment(call)) return rc;
@@ -422,7 +435,8 @@ int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
 int fnmoe_moe_execute_static(const FnMoEArgs *a, void *stream) {
   const int v = validate_moe(a);
   if (v != FNMOE_OK) return v;
-  const uint64_t need = moe_workspace(a);
+  // the array is 256-byte aligned: the carves need no slack
+  const uint64_t need = moe_workspace_aligned(a);
   if (need > FNMOE_STATIC_SCRATCH_BYTES)
     return fail(FNMOE_ERR_WORKSPACE, "this call needs " + std::to_string(need) +
                                          " bytes of scratch; the static scratch holds " +
@@ -548,8 +562,8 @@ int fnmoe_group_tokens(const uint32_t *routes, uint32_t pairs, uint32_t array_ex
   gv.tiles = cv.take<int4>(3 * static_cast<uint64_t>(gv.max_tiles));
   gv.n_tiles = cv.take<int32_t>(4);
   gv.bin_key = cv.take<uint32_t>(n_bins);
-  if (workspace == nullptr || workspace_bytes < cv.off)
-    return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(cv.off) + " bytes");
+  if (workspace == nullptr || workspace_bytes < cv.used())
+    return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(cv.off + kWorkspaceSlack) + " bytes");
   gv.counts = counts;
   gv.offsets = offsets;
   gv.order = order;
@@ -623,9 +637,13 @@ struct LayerLayout {
   uint16_t *xg;        // prefill: x rows gathered into bin order [n_total][H]
   int *ghist;          // prefill: per-chunk bin counts of the multi-CTA grouping
   uint64_t ghist_bytes;
+  uint32_t *amax;      // batch-1 persistent kernel: activation row maxima
 };
 
-uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL) {
+// Carves the layer workspace from `base` (null: a size probe).  Returns the
+// bytes any base pointer needs (carves plus the alignment slack); `used`
+// receives the bytes these carves take from this base.
+uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL, uint64_t *used = nullptr) {
   Carver cv(base);
   const int T = a->tokens, k = a->top_k, E = a->expert_count;
   const bool has_table = a->table.base != nullptr;
@@ -649,7 +667,9 @@ uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL) {
   LL.xg = layer_prefill(a) ? cv.take<uint16_t>(static_cast<uint64_t>(n_total) * a->hidden_size) : nullptr;
   LL.ghist_bytes = layer_prefill(a) ? static_cast<uint64_t>((n_total + 4095) / 4096) * n_bins * sizeof(int) : 0;
   LL.ghist = LL.ghist_bytes ? cv.take<int>(LL.ghist_bytes / sizeof(int)) : nullptr;
-  return cv.off + 256;
+  LL.amax = cv.take<uint32_t>(32);
+  if (used != nullptr) *used = cv.used();
+  return cv.off + kWorkspaceSlack;
 }
 
 }  // namespace
@@ -670,9 +690,10 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
   if (!device_ok(why)) return fail(FNMOE_ERR_DEVICE, why);
   LayerLayout LL{};
   const uint64_t need = carve_layer(a, nullptr, LL);
-  if (a->workspace == nullptr || a->workspace_bytes < need)
+  uint64_t used = 0;
+  if (a->workspace != nullptr) carve_layer(a, a->workspace, LL, &used);
+  if (a->workspace == nullptr || a->workspace_bytes < used)
     return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes");
-  carve_layer(a, a->workspace, LL);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = ensure_exp_table(s);
   if (e != cudaSuccess) return cuda_fail(e, "exp table");
@@ -724,6 +745,41 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
   uint16_t *logits = a->logits_out ? static_cast<uint16_t *>(a->logits_out) : LL.logits;
   uint32_t *inds = a->inds_out ? a->inds_out : LL.inds;
   uint16_t *scores = a->scores_out ? static_cast<uint16_t *>(a->scores_out) : LL.scores;
+
+  // One token on tiled tables: the whole layer in one persistent kernel
+  // (same arithmetic, same bits as the launches below).
+  if (T == 1 && !prefill && call.tiled.gate_up != nullptr && a->table_routes_of_expert == nullptr &&
+      !fused_disabled()) {
+    FusedLayer f{};
+    f.x = static_cast<const uint16_t *>(a->x);
+    f.W = static_cast<const uint16_t *>(a->router_weight);
+    f.wsg = shared ? static_cast<const uint16_t *>(a->shared_expert_gate) : nullptr;
+    f.tiled = call.tiled;
+    f.E = E;
+    f.k = k;
+    f.H = H;
+    f.I = I;
+    f.blend = a->renorm_blend;
+    f.keep_threshold = a->keep_threshold;
+    f.min_keep = static_cast<int>(a->min_keep);
+    f.logits = logits;
+    f.shared_logit = LL.shared_logit;
+    f.inds = inds;
+    f.scores = scores;
+    f.mass = LL.mass;
+    f.shared_gate = LL.shared_gate;
+    f.act = L.act;
+    e = grid_barrier_slot(a->workspace, &f.bar);
+    if (e != cudaSuccess) return cuda_fail(e, "grid barrier slot");
+    f.out = static_cast<uint16_t *>(a->output);
+    f.amax = LL.amax;
+    {
+      Prof p("decode_layer", s);
+      e = launch_decode_layer(f, G, s);
+    }
+    if (e == cudaSuccess) return FNMOE_OK;
+    if (e != cudaErrorNotSupported) return cuda_fail(e, "decode layer");
+  }
 
   // Small decode batches get the row fixed point of x from extra CTAs of the
   // router launch; otherwise it is a launch of its own.
@@ -864,6 +920,13 @@ int fnmoe_read_device_errors(uint32_t *flags, int clear) {
   if (clear) {
     e = cudaMemset(p, 0, sizeof(uint32_t));
     if (e != cudaSuccess) return cuda_fail(e, "clear device errors");
+  }
+  // a bounded wait that gave up may have left a grid-barrier counter of the
+  // batch-1 kernel mid-barrier: start them over (the device is idle here)
+  if (*flags & kErrTimeout) {
+    e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = reset_grid_barriers();
+    if (e != cudaSuccess) return cuda_fail(e, "reset grid barriers");
   }
   return FNMOE_OK;
 }

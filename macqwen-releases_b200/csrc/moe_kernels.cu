@@ -19,6 +19,7 @@
 #include <algorithm>
 #include <climits>
 #include <cstdlib>
+#include <map>
 #include <mutex>
 
 #include "async.cuh"
@@ -66,6 +67,13 @@ bool pdl_enabled() {
 // instead of the K-split GEMV (same results; for comparisons).
 bool gemv_disabled() {
   static const bool off = std::getenv("FNMOE_NO_GEMV") != nullptr;
+  return off;
+}
+
+// FNMOE_NO_FUSED=1 runs batch-1 layers through the multi-launch chain
+// instead of the persistent kernel (same results; for comparisons).
+bool fused_disabled() {
+  static const bool off = std::getenv("FNMOE_NO_FUSED") != nullptr;
   return off;
 }
 
@@ -2545,5 +2553,8 @@ cudaError_t launch_weighted_combine(const float *outputs, const int32_t *routes,
   k_weighted_combine<<<grid, 256, 0, s>>>(outputs, routes, scores, out, T, S, E, H);
   return cudaGetLastError();
 }
+
+// the batch-1 layer as one persistent kernel (uses the kernels above)
+#include "decode_layer.cuh"
 
 }  // namespace fnmoe

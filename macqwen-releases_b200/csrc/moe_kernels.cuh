@@ -172,6 +172,43 @@ cudaError_t launch_prefill_gemm(bool dual, const ExpertCallArgs &a, const GroupV
                                 const int32_t *n_ptiles, int max_tiles, const uint16_t *in, int in_rows,
                                 uint16_t *out, cudaStream_t s);
 
+// Batch-1 layer as one persistent kernel (decode_layer.cuh): router,
+// top-k, gate/up, down and combine of one token with two grid barriers.
+struct FusedLayer {
+  const uint16_t *x;        // [H] bf16
+  const uint16_t *W;        // [E][H] bf16 router rows
+  const uint16_t *wsg;      // [H] bf16 shared-expert gate row, or null (no shared expert)
+  TiledView tiled;          // routed records [0, E) (+ the shared expert as the last record)
+  int E, k, H, I;
+  float blend;
+  double keep_threshold;
+  int min_keep;
+  uint16_t *logits;         // [E] bf16
+  uint16_t *shared_logit;   // [1] bf16
+  uint32_t *inds;           // [k]
+  uint16_t *scores;         // [k] bf16 (renormalised)
+  uint16_t *mass;           // [1] bf16 (top-k mass)
+  uint16_t *shared_gate;    // [1] bf16 sigmoid(shared logit)
+  uint16_t *act;            // [k + 1][I] bf16: slot s at row s, the shared expert at row k
+  uint32_t *bar;            // grid-barrier counter (grid_barrier_slot)
+  uint32_t *amax;           // [k + 1] activation row maxima (bfloat16 magnitude bits), workspace
+  uint16_t *out;            // [H] bf16
+  // shared-memory carve (byte offsets into the dynamic allocation)
+  int nslot;                // ring slots = most gate/up items a CTA can get
+  int alias;                // 1: the down stage and activation limbs reuse the ring
+  int off_x, off_xl, off_xm, off_soft, off_d, off_ring, off_down, off_al, off_am;
+};
+
+// cudaErrorNotSupported when the sizes do not fit the fused kernel (the
+// caller then runs the multi-launch layer).
+cudaError_t launch_decode_layer(FusedLayer p, int G, cudaStream_t s);
+// true when FNMOE_NO_FUSED is set: batch-1 layers run the multi-launch chain.
+bool fused_disabled();
+// The fused kernel's grid-barrier counter for workspace `key` (library-owned,
+// zero-initialised, self-cleaning); reset_grid_barriers() after a timeout.
+cudaError_t grid_barrier_slot(const void *key, uint32_t **bar);
+cudaError_t reset_grid_barriers();
+
 cudaError_t launch_dequant(const uint32_t *w, const uint16_t *sc,
                            const uint16_t *bi, uint16_t *out, uint64_t rows,
                            int K, int G, cudaStream_t s);

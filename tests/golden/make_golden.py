@@ -1,9 +1,9 @@
 """Generate golden vectors by running the reference's own NumPy code.
 
-Run in a container that has the reference checkout (read-only) at
-``$FLASHNEXT_REFERENCE`` (default ``/root/reference``):
+Run with ``FLASHNEXT_REFERENCE`` set to a read-only checkout of the
+reference (the variable is required):
 
-    python -B tests/golden/make_golden.py
+    FLASHNEXT_REFERENCE=<checkout> python -B tests/golden/make_golden.py
 
 It imports ``models.flashnext.metal_runtime`` and ``models.flashnext.slab_pack``
 from the reference (both import with NumPy only) and records, for seeded
@@ -29,7 +29,13 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("FLASHNEXT_REFERENCE", "/root/reference"))
+
+
+def _reference_root() -> Path:
+    root = os.environ.get("FLASHNEXT_REFERENCE")
+    if not root:
+        sys.exit("set FLASHNEXT_REFERENCE to a checkout of the reference repository")
+    return Path(root)
 
 
 def _bf16_values(a):
@@ -54,7 +60,7 @@ def _projection(rng, experts, out_w, in_w, group):
 
 
 def main() -> None:
-    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(_reference_root()))
     sys.dont_write_bytecode = True
     from models.flashnext import metal_runtime as mr
     from models.flashnext import slab_pack as sp

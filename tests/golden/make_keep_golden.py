@@ -1,9 +1,9 @@
 """Golden vectors for the adaptive keep from the reference's own function.
 
-Run in a container that has the reference checkout (read-only) at
-``$FLASHNEXT_REFERENCE`` (default ``/root/reference``):
+Run with ``FLASHNEXT_REFERENCE`` set to a read-only checkout of the
+reference (the variable is required):
 
-    python -B tests/golden/make_keep_golden.py
+    FLASHNEXT_REFERENCE=<checkout> python -B tests/golden/make_keep_golden.py
 
 ``models/flashnext/adaptive_topk.py`` imports MLX at module level, which is
 not installable here, so the script takes the source text of the pure-Python
@@ -37,7 +37,10 @@ def _bf16(a):
 
 
 def main():
-    root = Path(os.environ.get("FLASHNEXT_REFERENCE", "/root/reference"))
+    root_env = os.environ.get("FLASHNEXT_REFERENCE")
+    if not root_env:
+        raise SystemExit("set FLASHNEXT_REFERENCE to a checkout of the reference repository")
+    root = Path(root_env)
     keep = _reference_keep_for_mass(root)
     rng = np.random.default_rng(20261202)
     rows = []

@@ -7,6 +7,8 @@ too.  Every floating-point comparison also states the north-star tolerance
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -231,6 +233,40 @@ def test_executor_bit_exact(cuda_lib, tokens, slots, hidden, inter, experts, gro
     assert_bf16_equal(_np(d), od, "down")
     per_slot = ex.execute(x, torch.tensor(routes).cuda(), bank)
     assert_bf16_equal(_np(per_slot), od, "per-slot down")
+
+
+@pytest.mark.parametrize("offset", [8, 100, 255])
+def test_executor_misaligned_workspace(cuda_lib, offset):
+    """A workspace pointer on any byte boundary works: the library rounds its
+    start up to 256 bytes within the reported size (which includes that
+    slack); the result equals the oracle's."""
+    import torch
+
+    from flashnext_b200 import _lib
+    bank, x, routes, scores = _executor_case(3, 4, 256, 128, 6, 32, seed=61)
+    r = torch.tensor(routes).cuda()
+    sc = torch.tensor(scores).cuda()
+    out = torch.empty((3, 256), dtype=torch.bfloat16, device="cuda")
+    a = _lib.FnMoEArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.x = x.data_ptr()
+    for name, key in (("gate_proj", "gate"), ("up_proj", "up"), ("down_proj", "down")):
+        w, s, b = bank[name]
+        setattr(a, f"{key}_weight", w.data_ptr())
+        setattr(a, f"{key}_scales", s.data_ptr())
+        setattr(a, f"{key}_biases", b.data_ptr())
+    a.routes, a.scores, a.scores_dtype, a.output = r.data_ptr(), sc.data_ptr(), _lib.DTYPE_F32, out.data_ptr()
+    a.tokens, a.slots, a.hidden_size, a.inter_size, a.expert_count, a.group_size = 3, 4, 256, 128, 6, 32
+    need = ctypes.c_uint64(0)
+    _lib.check(cuda_lib.fnmoe_moe_workspace_size(ctypes.byref(a), ctypes.byref(need)), "workspace_size")
+    ws = torch.empty(need.value + offset, dtype=torch.uint8, device="cuda")
+    a.workspace, a.workspace_bytes = ws.data_ptr() + offset, need.value
+    _lib.check(cuda_lib.fnmoe_moe_execute(ctypes.byref(a), torch.cuda.current_stream().cuda_stream), "execute")
+    a.workspace_bytes = need.value - 256 - 1  # below the aligned carves themselves: rejected, nothing runs
+    assert cuda_lib.fnmoe_moe_execute(ctypes.byref(a), torch.cuda.current_stream().cuda_stream) == _lib.ERR_WORKSPACE
+    nb = _bank_np(bank)
+    want = moe.executor(_np(x), routes, nb["gate_proj"], nb["up_proj"], nb["down_proj"], scores=scores)
+    assert_bf16_equal(_np(out), want, "combined output")
 
 
 def test_executor_shared_epilogues_bit_exact(cuda_lib):
