@@ -6,7 +6,8 @@
  * device memory: scratch comes from a caller-provided workspace whose size
  * the matching *_workspace_size call reports -- except
  * fnmoe_moe_execute_static, whose scratch is a fixed array inside the
- * library.  A workspace may start at any address: the library rounds its
+ * library, and fnmoe_ep_create, which allocates an expert-parallel exchange
+ * window once at set-up.  A workspace may start at any address: the library rounds its
  * start up to a 256-byte boundary, and the reported sizes include the 256
  * bytes that rounding can skip.  Each call returns FNMOE_OK (0) or a negative
  * FNMOE_ERR_* code; fnmoe_get_last_error() returns the message of the
@@ -144,7 +145,13 @@ typedef struct FnMoEArgs {
   uint32_t expert_count;       /* experts in the *_weight arrays */
   /* extensions */
   uint32_t group_size;         /* 32 or 64 */
-  uint32_t x_dtype;            /* FNMOE_DTYPE_BF16 */
+  uint32_t x_dtype;            /* FNMOE_DTYPE_BF16, or FNMOE_DTYPE_F32: float32
+                                  activations (metal_runtime.py:371-373) -- then
+                                  output, gate_out/up_out/down_out, shared_y,
+                                  shared and shared_gate are float32 too, and
+                                  every intermediate is rounded to float32 instead
+                                  of bfloat16 (the reference's kernels with
+                                  T = float) */
   uint32_t scores_dtype;       /* FNMOE_DTYPE_F32 or FNMOE_DTYPE_BF16 */
   uint32_t reserved0;
   const void *shared_y;        /* [tokens, hidden] bf16 or NULL */
@@ -375,6 +382,62 @@ FNMOE_API int fnmoe_swiglu(const void *gate, const void *up, void *out, uint64_t
 
 FNMOE_API int fnmoe_paged_decode_workspace_size(const FnPagedArgs *args, uint64_t *bytes);
 FNMOE_API int fnmoe_paged_decode(const FnPagedArgs *args, void *stream);
+
+/* ---- Expert-parallel exchange over NVLink peer memory ----
+ * No reference counterpart: the reference runs on one device.  One process
+ * per GPU of a node; rank r owns routed experts [r*experts_per_rank,
+ * (r+1)*experts_per_rank).  fnmoe_ep_create allocates this rank's exchange
+ * window (once, at set-up: the only entry point besides the static-scratch
+ * array that owns device memory); every rank passes its IPC handle to the
+ * others (any host transport), then opens theirs.  A step is
+ *   fnmoe_ep_dispatch        (x rows and owner-local expert ids of every
+ *                             token to the ranks that own its slots; waits
+ *                             for every rank's rows to arrive),
+ *   fnmoe_moe_execute        on the window (FnEpWindow: world*capacity rows,
+ *                             top_k + 1 slots, slot top_k = the shared
+ *                             expert, the last local record; per-slot
+ *                             outputs into window.slot_outputs),
+ *   fnmoe_ep_return_combine  (per-slot outputs back to the tokens' ranks,
+ *                             slot-ordered combine + gated shared expert).
+ * Every rank takes every step (with 0 tokens if it has none), in the same
+ * order, on one stream; nothing synchronises with the host, so a step can be
+ * captured in a CUDA graph.  Waits on peers give up after about a second and
+ * set bit 2 of the device error word; the exchange is then unusable (destroy
+ * and recreate it on every rank).  Stores to peers are plain stores: no TMA
+ * or multicast. */
+#define FNMOE_EP_IPC_BYTES 64
+
+typedef struct FnEpConfig {
+  uint32_t abi_version;
+  uint32_t world;              /* ranks, 1..8, one GPU each */
+  uint32_t rank;
+  uint32_t capacity_tokens;    /* most tokens a rank dispatches per step */
+  uint32_t hidden_size;        /* multiple of 8, <= 4096 */
+  uint32_t top_k;              /* 1..16 */
+  uint32_t experts_per_rank;   /* routed experts per rank */
+  uint32_t reserved;
+} FnEpConfig;
+
+typedef struct FnEpWindow {
+  const void *rows;            /* [world * capacity][hidden] bf16 received rows */
+  const uint32_t *ids;         /* [world * capacity][top_k + 1] local expert ids (FNMOE_ROUTE_NONE = empty) */
+  void *slot_outputs;          /* [world * capacity][top_k + 1][hidden] bf16: per-slot outputs of the experts */
+  uint32_t row_count;          /* world * capacity */
+  uint32_t slots;              /* top_k + 1 */
+  uint64_t bytes;              /* window size */
+} FnEpWindow;
+
+FNMOE_API int fnmoe_ep_create(const FnEpConfig *config, void **handle);
+FNMOE_API int fnmoe_ep_ipc_handle(void *handle, void *out);          /* FNMOE_EP_IPC_BYTES bytes */
+FNMOE_API int fnmoe_ep_open_peers(void *handle, const void *handles); /* world handles in rank order */
+FNMOE_API int fnmoe_ep_window(void *handle, FnEpWindow *window);
+FNMOE_API int fnmoe_ep_dispatch(void *handle, const void *x, const uint32_t *inds, uint32_t tokens,
+                                void *stream);
+FNMOE_API int fnmoe_ep_return_combine(void *handle, const void *scores, const void *shared_gate,
+                                      uint32_t tokens, void *out, void *stream);
+/* Synchronises the device, unmaps the peers' windows and frees this one;
+ * call it on every rank after a barrier (no peer may still write here). */
+FNMOE_API int fnmoe_ep_destroy(void *handle);
 
 /* Device error word of the library: bit 0 = an out-of-range route was
  * skipped, bit 1 = a non-finite activation reached the fixed-point stage,

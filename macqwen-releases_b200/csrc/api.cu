@@ -126,8 +126,9 @@ struct Layout {
 };
 
 // Carve the shared part of the executor / layer workspace.
+// elem: bytes per activation element (2: bfloat16, 4: float32 activations).
 void carve_core(Carver &cv, Layout &L, int T, int H, int I, int G, int n_total, int n_bins,
-                bool need_d) {
+                bool need_d, int elem = 2) {
   const int Gh = H / G, Gi = I / G;
   L.xl = cv.take<uint16_t>(static_cast<uint64_t>(T) * Gh * 2 * G);
   L.xm = cv.take<float>(static_cast<uint64_t>(T) * meta_pitch(Gh));
@@ -139,10 +140,10 @@ void carve_core(Carver &cv, Layout &L, int T, int H, int I, int G, int n_total, 
   L.gv.tiles = cv.take<int4>(3 * static_cast<uint64_t>(L.gv.max_tiles));
   L.gv.n_tiles = cv.take<int32_t>(4);
   L.gv.bin_key = cv.take<uint32_t>(n_bins);
-  L.act = cv.take<uint16_t>(static_cast<uint64_t>(n_total) * I);
+  L.act = cv.take<uint16_t>(static_cast<uint64_t>(n_total) * I * (elem / 2));
   L.al = cv.take<uint16_t>(static_cast<uint64_t>(n_total) * Gi * 2 * G);
   L.am = cv.take<float>(static_cast<uint64_t>(n_total) * meta_pitch(Gi));
-  L.d = need_d ? cv.take<uint16_t>(static_cast<uint64_t>(n_total) * H) : nullptr;
+  L.d = need_d ? cv.take<uint16_t>(static_cast<uint64_t>(n_total) * H * (elem / 2)) : nullptr;
 }
 
 constexpr int kMaxBins = 16384;
@@ -165,8 +166,10 @@ int validate_moe(const FnMoEArgs *a) {
     return fail(FNMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64");
   if (a->hidden_size % a->group_size || a->inter_size % a->group_size)
     return fail(FNMOE_ERR_SHAPE, "Q4 projection inputs must be group aligned");
-  if (a->x_dtype != FNMOE_DTYPE_BF16)
-    return fail(FNMOE_ERR_UNSUPPORTED, "x must be bfloat16");
+  if (a->x_dtype != FNMOE_DTYPE_BF16 && a->x_dtype != FNMOE_DTYPE_F32)
+    return fail(FNMOE_ERR_UNSUPPORTED, "x must be bfloat16 or float32");
+  if (a->x_dtype == FNMOE_DTYPE_F32 && a->hidden_size > 4096)
+    return fail(FNMOE_ERR_SHAPE, "float32 activations need hidden_size <= 4096");
   if (a->x == nullptr || a->routes == nullptr) return fail(FNMOE_ERR_NULL, "x and routes are required");
   const bool has_table = a->table.base != nullptr;
   const bool has_stream = a->stream_table.base != nullptr;
@@ -216,7 +219,8 @@ uint64_t moe_workspace_aligned(const FnMoEArgs *a) {
   const int n_bins = static_cast<int>(non_slot_keys(a) + (has_table ? a->table.records : 0));
   const int n_total = static_cast<int>(a->tokens * a->slots);
   const bool per_slot = (a->flags & (FNMOE_FLAG_RETURN_ALL | FNMOE_FLAG_NO_COMBINE)) || a->scores == nullptr;
-  carve_core(cv, L, a->tokens, a->hidden_size, a->inter_size, a->group_size, n_total, n_bins, !per_slot);
+  carve_core(cv, L, a->tokens, a->hidden_size, a->inter_size, a->group_size, n_total, n_bins, !per_slot,
+             a->x_dtype == FNMOE_DTYPE_F32 ? 4 : 2);
   return cv.off;
 }
 
@@ -297,6 +301,7 @@ ExpertCallArgs make_call(const FnMoEArgs *a) {
   c.I = static_cast<int>(a->inter_size);
   c.I_shared = c.I;
   c.G = static_cast<int>(a->group_size);
+  c.f32 = a->x_dtype == FNMOE_DTYPE_F32 ? 1 : 0;
   return c;
 }
 
@@ -377,9 +382,10 @@ int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
   const int G = static_cast<int>(a->group_size);
   const int n_pairs = T * S;
   const int n_bins = static_cast<int>(non_slot_keys(a) + (has_table ? a->table.records : 0));
+  const bool f32 = a->x_dtype == FNMOE_DTYPE_F32;
   Carver cv(a->workspace);
   Layout L{};
-  carve_core(cv, L, T, H, I, G, n_pairs, n_bins, !per_slot);
+  carve_core(cv, L, T, H, I, G, n_pairs, n_bins, !per_slot, f32 ? 4 : 2);
   if (cv.used() > a->workspace_bytes)
     return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(moe_workspace(a)) + " bytes");
   uint16_t *d = per_slot ? static_cast<uint16_t *>(a->down_out) : L.d;
@@ -388,7 +394,8 @@ int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
 
   {
     Prof p("prep_x", s);
-    e = launch_prep_rows(static_cast<const uint16_t *>(a->x), T, H, G, L.xl, L.xm, s);
+    e = f32 ? launch_prep_rows_f32(static_cast<const float *>(a->x), T, H, G, L.xl, L.xm, s)
+            : launch_prep_rows(static_cast<const uint16_t *>(a->x), T, H, G, L.xl, L.xm, s);
   }
   if (e != cudaSuccess) return cuda_fail(e, "prep x");
   {
@@ -396,10 +403,6 @@ int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
     e = launch_group(a->routes, n_pairs, 0, call.array_experts, static_cast<int>(call.table.records), L.gv, s);
   }
   if (e != cudaSuccess) return cuda_fail(e, "group");
-  // Empty slots (FNMOE_ROUTE_NONE) leave their activation rows unwritten:
-  // zero them so that the activation fixed point sees finite rows.
-  e = cudaMemsetAsync(L.act, 0, static_cast<size_t>(n_pairs) * a->inter_size * sizeof(uint16_t), s);
-  if (e != cudaSuccess) return cuda_fail(e, "clear activations");
   {
     Prof p("gate_up", s);
     e = launch_gate_up(call, L.gv, L.xl, L.xm, L.act,
@@ -409,7 +412,10 @@ int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
   if (e != cudaSuccess) return cuda_fail(e, "gate_up");
   {
     Prof p("prep_act", s);
-    e = launch_prep_rows(L.act, n_pairs, I, G, L.al, L.am, s);
+    // empty slots (FNMOE_ROUTE_NONE) have no activation row: skipped
+    e = f32 ? launch_prep_rows_f32(reinterpret_cast<const float *>(L.act), n_pairs, I, G, L.al, L.am, s, a->routes,
+                                   n_pairs)
+            : launch_prep_rows(L.act, n_pairs, I, G, L.al, L.am, s, a->routes, n_pairs);
   }
   if (e != cudaSuccess) return cuda_fail(e, "prep act");
   {
@@ -423,10 +429,17 @@ int fnmoe_moe_execute(const FnMoEArgs *a, void *stream) {
   else if (a->shared) mode = kCombineParts;
   {
     Prof p("combine", s);
-    e = launch_combine(d, a->routes, a->scores, a->scores_dtype == FNMOE_DTYPE_F32, T, S, H, mode,
-                       static_cast<const uint16_t *>(a->shared_y), static_cast<const uint16_t *>(a->shared),
-                       static_cast<const uint16_t *>(a->shared_gate), call.array_experts,
-                       static_cast<int>(call.table.records), static_cast<uint16_t *>(a->output), s);
+    if (f32)
+      e = launch_combine_f32(reinterpret_cast<const float *>(d), a->routes, a->scores,
+                             a->scores_dtype == FNMOE_DTYPE_F32, T, S, H, mode,
+                             static_cast<const float *>(a->shared_y), static_cast<const float *>(a->shared),
+                             static_cast<const float *>(a->shared_gate), call.array_experts,
+                             static_cast<int>(call.table.records), static_cast<float *>(a->output), s);
+    else
+      e = launch_combine(d, a->routes, a->scores, a->scores_dtype == FNMOE_DTYPE_F32, T, S, H, mode,
+                         static_cast<const uint16_t *>(a->shared_y), static_cast<const uint16_t *>(a->shared),
+                         static_cast<const uint16_t *>(a->shared_gate), call.array_experts,
+                         static_cast<int>(call.table.records), static_cast<uint16_t *>(a->output), s);
   }
   if (e != cudaSuccess) return cuda_fail(e, "combine");
   return FNMOE_OK;
@@ -858,11 +871,6 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
     }
     if (e != cudaSuccess) return cuda_fail(e, "prefill down");
   } else {
-    if (a->keep_threshold > 0.0 && a->keep_threshold < 1.0) {
-      // dropped slots leave their activation rows unwritten (see the executor)
-      e = cudaMemsetAsync(L.act, 0, static_cast<size_t>(n_total_pairs) * I * sizeof(uint16_t), s);
-      if (e != cudaSuccess) return cuda_fail(e, "clear activations");
-    }
     {
       Prof p("gate_up", s);
       e = launch_gate_up(call, L.gv, L.xl, L.xm, L.act, nullptr, nullptr, s);
@@ -870,7 +878,8 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
     if (e != cudaSuccess) return cuda_fail(e, "gate_up");
     {
       Prof p("prep_act", s);
-      e = launch_prep_rows(L.act, n_pairs + (shared ? T : 0), I, G, L.al, L.am, s);
+      // dropped slots (adaptive keep) have no activation row: skipped
+      e = launch_prep_rows(L.act, n_pairs + (shared ? T : 0), I, G, L.al, L.am, s, LL.routes, n_pairs);
     }
     if (e != cudaSuccess) return cuda_fail(e, "prep act");
     {
@@ -1021,5 +1030,30 @@ int fnmoe_tile_experts(const FnTileArgs *a, void *stream) {
   if (e != cudaSuccess) return cuda_fail(e, "tile down");
   return FNMOE_OK;
 }
+
+int fnmoe_ep_create(const FnEpConfig *config, void **handle) {
+  std::string why;
+  if (!device_ok(why)) return fail(FNMOE_ERR_DEVICE, why);
+  return ep_create(config, handle, g_last_error);
+}
+
+int fnmoe_ep_ipc_handle(void *handle, void *out) { return ep_ipc_handle(handle, out, g_last_error); }
+
+int fnmoe_ep_open_peers(void *handle, const void *handles) { return ep_open_peers(handle, handles, g_last_error); }
+
+int fnmoe_ep_window(void *handle, FnEpWindow *window) { return ep_window(handle, window, g_last_error); }
+
+int fnmoe_ep_dispatch(void *handle, const void *x, const uint32_t *inds, uint32_t tokens, void *stream) {
+  Prof p("ep_dispatch", static_cast<cudaStream_t>(stream));
+  return ep_dispatch(handle, x, inds, tokens, static_cast<cudaStream_t>(stream), g_last_error);
+}
+
+int fnmoe_ep_return_combine(void *handle, const void *scores, const void *shared_gate, uint32_t tokens, void *out,
+                            void *stream) {
+  Prof p("ep_return_combine", static_cast<cudaStream_t>(stream));
+  return ep_return_combine(handle, scores, shared_gate, tokens, out, static_cast<cudaStream_t>(stream), g_last_error);
+}
+
+int fnmoe_ep_destroy(void *handle) { return ep_destroy(handle, g_last_error); }
 
 }  // extern "C"

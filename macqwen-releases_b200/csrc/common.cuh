@@ -85,6 +85,16 @@ __device__ __forceinline__ float swiglu_bf16(const uint16_t *tab, float g, float
   return bmul(bmul(g, sigmoid_bf16(tab, g)), u);
 }
 
+// The same sequence with float32 activations (the reference's kernel with
+// T = float): every op rounded to float32, exp correctly rounded (float64
+// exp, one rounding).
+__device__ __forceinline__ float swiglu_f32(float g, float u) {
+  const float ex = __double2float_rn(exp(static_cast<double>(fabsf(g))));
+  const float small = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
+  const float sig = (g < 0.0f) ? small : __fsub_rn(1.0f, small);
+  return __fmul_rn(__fmul_rn(g, sig), u);
+}
+
 // m16n8k16 fp16 MMA, fp32 accumulate (exact here: all operands are small
 // integers and every partial sum stays below 2^24).
 __device__ __forceinline__ void mma_16816(float c[4], const uint32_t a[4],

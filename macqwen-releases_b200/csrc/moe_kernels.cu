@@ -144,6 +144,16 @@ __device__ __forceinline__ int fixed_x(uint32_t h, int E) {
   return (h & 0x8000u) ? -static_cast<int>(mag) : static_cast<int>(mag);
 }
 
+// The same for one float32 input (bits), E the row exponent.
+__device__ __forceinline__ int fixed_x32(uint32_t bits, int E) {
+  const uint32_t ef = (bits >> 23) & 0xFFu, mf = bits & 0x7FFFFFu;
+  if ((bits & 0x7FFFFFFFu) == 0 || ef == 255u) return 0;
+  const uint32_t M = ef ? (mf | 0x800000u) : mf;
+  const int sh = ef ? (static_cast<int>(ef) - 128 - E) : (-127 - E);
+  const uint32_t mag = sh >= 0 ? (M << sh) : ((-sh >= 32) ? 0u : (M >> (-sh)));
+  return (bits & 0x80000000u) ? -static_cast<int>(mag) : static_cast<int>(mag);
+}
+
 __device__ __forceinline__ uint32_t half_pair(int lo, int hi) {
   return static_cast<uint32_t>(__half_as_ushort(__int2half_rn(lo))) |
          (static_cast<uint32_t>(__half_as_ushort(__int2half_rn(hi))) << 16);
@@ -162,7 +172,8 @@ __device__ __forceinline__ uint32_t half_pair(int lo, int hi) {
 // router launch, which runs it in extra CTAs.
 template <int G, int SPT>
 __device__ __forceinline__ void prep_rows_body(const uint16_t *rows, int n_rows, int K, int TPR, uint16_t *limbs,
-                                               float *meta, uint32_t *err, int block) {
+                                               float *meta, uint32_t *err, int block,
+                                               const uint32_t *skip_routes = nullptr, int n_skip = 0) {
   constexpr int LPG = G / 8;  // lanes per group
   __shared__ uint32_t s_mx[8][8];
   const int lane = threadIdx.x & 31;
@@ -170,7 +181,9 @@ __device__ __forceinline__ void prep_rows_body(const uint16_t *rows, int n_rows,
   const int tr = threadIdx.x - rl * TPR;
   const int wr = tr >> 5;            // warp within the row
   const int row = block * (blockDim.x / TPR) + rl;
-  const bool live = row < n_rows;
+  // rows of empty slots (route FNMOE_ROUTE_NONE; rows past n_skip have no
+  // route) are neither read nor written: no kernel reads their limbs
+  const bool live = row < n_rows && !(row < n_skip && __ldcg(skip_routes + row) == kRouteNone);
   const int Gc = K / G;
   const int slices = K / 8;
   const int mp = meta_pitch(Gc);
@@ -250,14 +263,110 @@ __device__ __forceinline__ void prep_rows_body(const uint16_t *rows, int n_rows,
 template <int G, int SPT>
 __global__ void __launch_bounds__(256) k_prep_rows(const uint16_t *rows, int n_rows, int K, int TPR,
                                                    uint16_t *__restrict__ limbs, float *__restrict__ meta,
-                                                   uint32_t *err) {
+                                                   uint32_t *err, const uint32_t *skip_routes, int n_skip) {
   pdl_wait();
   pdl_trigger();
-  prep_rows_body<G, SPT>(rows, n_rows, K, TPR, limbs, meta, err, blockIdx.x);
+  prep_rows_body<G, SPT>(rows, n_rows, K, TPR, limbs, meta, err, blockIdx.x, skip_routes, n_skip);
+}
+
+// prep_rows_body for float32 rows: the same fixed point (trunc(x*2^(22-E)),
+// E = floor(log2 max|x|) over the row's finite values), limbs and metadata.
+// One thread per row slice of 8 inputs (TPR threads per row, as above).
+template <int G, int SPT>
+__global__ void __launch_bounds__(256) k_prep_rows_f32(const float *rows, int n_rows, int K, int TPR,
+                                                       uint16_t *__restrict__ limbs, float *__restrict__ meta,
+                                                       uint32_t *err, const uint32_t *skip_routes, int n_skip) {
+  constexpr int LPG = G / 8;
+  __shared__ uint32_t s_mx[8][8];
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int rl = threadIdx.x / TPR;
+  const int tr = threadIdx.x - rl * TPR;
+  const int wr = tr >> 5;
+  const int row = blockIdx.x * (blockDim.x / TPR) + rl;
+  const bool live = row < n_rows && !(row < n_skip && __ldcg(skip_routes + row) == kRouteNone);
+  const int Gc = K / G;
+  const int slices = K / 8;
+  const int mp = meta_pitch(Gc);
+  const uint4 *src = reinterpret_cast<const uint4 *>(rows + static_cast<size_t>(live ? row : 0) * K);
+  uint4 v[SPT][2];
+#pragma unroll
+  for (int q = 0; q < SPT; ++q) {
+    const int i = tr + q * TPR;
+    const bool ok = live && i < slices;
+    v[q][0] = ok ? src[2 * i] : make_uint4(0u, 0u, 0u, 0u);
+    v[q][1] = ok ? src[2 * i + 1] : make_uint4(0u, 0u, 0u, 0u);
+  }
+  uint32_t mx = 0;
+  bool bad = false;
+#pragma unroll
+  for (int q = 0; q < SPT; ++q) {
+    const uint32_t w[8] = {v[q][0].x, v[q][0].y, v[q][0].z, v[q][0].w, v[q][1].x, v[q][1].y, v[q][1].z, v[q][1].w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t a = w[e] & 0x7FFFFFFFu;
+      if (a >= 0x7F800000u) bad = true;
+      else mx = max(mx, a);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) set_error(err, kErrNonFinite);
+  if (TPR > 32) {
+    if (lane == 0) s_mx[rl][wr] = mx;
+    __syncthreads();
+    for (int q = 0; q < TPR / 32; ++q) mx = max(mx, s_mx[rl][q]);
+  }
+  if (!live) return;
+  int E = 0;
+  if (mx != 0) E = (mx >> 23) ? static_cast<int>(mx >> 23) - 127 : (31 - __clz(static_cast<int>(mx))) - 149;
+  float *mrow = meta + static_cast<size_t>(row) * mp;
+#pragma unroll
+  for (int q = 0; q < SPT; ++q) {
+    const int i = tr + q * TPR;
+    int sx = 0;
+    if (i < slices) {
+      const uint32_t w[8] = {v[q][0].x, v[q][0].y, v[q][0].z, v[q][0].w, v[q][1].x, v[q][1].y, v[q][1].z, v[q][1].w};
+      int X[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        X[e] = fixed_x32(w[e], E);
+        sx += X[e];
+      }
+      int l0[8], l1[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        l1[e] = ((X[e] + 2048) & 4095) - 2048;
+        l0[e] = (X[e] - l1[e]) >> 12;
+      }
+      const int g = (8 * i) / G;
+      const int within = (8 * i) - g * G;
+      uint16_t *dst = limbs + (static_cast<size_t>(row) * Gc + g) * 2 * G + within;
+      *reinterpret_cast<uint4 *>(dst) = make_uint4(half_pair(l0[0], l0[4]), half_pair(l0[1], l0[5]),
+                                                   half_pair(l0[2], l0[6]), half_pair(l0[3], l0[7]));
+      *reinterpret_cast<uint4 *>(dst + G) = make_uint4(half_pair(l1[0], l1[4]), half_pair(l1[1], l1[5]),
+                                                       half_pair(l1[2], l1[6]), half_pair(l1[3], l1[7]));
+    }
+#pragma unroll
+    for (int off = 1; off < LPG; off <<= 1) sx += __shfl_xor_sync(0xFFFFFFFFu, sx, off);
+    if (i < slices && (lane & (LPG - 1)) == 0) mrow[(8 * i) / G] = __int2float_rn(sx);
+  }
+  if (tr == 0) {
+    const int ai = meta_a_index(Gc);
+    for (int g = Gc; g < ai; ++g) mrow[g] = 0.0f;
+    const int k = E - 22;
+    const int ka = max(k, -126);
+    mrow[ai] = __int_as_float((ka + 127) << 23);
+    mrow[ai + 1] = __int_as_float((k - ka + 127) << 23);
+    mrow[ai + 2] = 0.0f;
+    mrow[ai + 3] = 0.0f;
+  }
 }
 
 template <int G>
-cudaError_t launch_prep_g(const uint16_t *rows, int n_rows, int K, uint16_t *limbs, float *meta, cudaStream_t s) {
+cudaError_t launch_prep_f32_g(const float *rows, int n_rows, int K, uint16_t *limbs, float *meta, cudaStream_t s,
+                              const uint32_t *skip_routes, int n_skip) {
   const int slices = K / 8;
   const int tpr = std::min(256, ((slices + 31) / 32) * 32);
   const int spt = (slices + tpr - 1) / tpr;
@@ -266,19 +375,47 @@ cudaError_t launch_prep_g(const uint16_t *rows, int n_rows, int K, uint16_t *lim
   const int threads = rpc * tpr;
   uint32_t *err = device_error_word();
   cudaError_t e = cudaSuccess;
-  if (spt == 1) e = launch_pdl(k_prep_rows<G, 1>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err);
-  else if (spt == 2) e = launch_pdl(k_prep_rows<G, 2>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err);
-  else if (spt <= 4) e = launch_pdl(k_prep_rows<G, 4>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err);
-  else if (spt <= 8) e = launch_pdl(k_prep_rows<G, 8>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err);
+  if (spt == 1) e = launch_pdl(k_prep_rows_f32<G, 1>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err, skip_routes, n_skip);
+  else if (spt == 2) e = launch_pdl(k_prep_rows_f32<G, 2>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err, skip_routes, n_skip);
+  else return cudaErrorInvalidValue;
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prep_rows_f32(const float *rows, int n_rows, int K, int G, uint16_t *limbs, float *meta,
+                                 cudaStream_t s, const uint32_t *skip_routes, int n_skip) {
+  if (n_rows <= 0) return cudaSuccess;
+  if (skip_routes == nullptr) n_skip = 0;
+  return G == 32 ? launch_prep_f32_g<32>(rows, n_rows, K, limbs, meta, s, skip_routes, n_skip)
+                 : launch_prep_f32_g<64>(rows, n_rows, K, limbs, meta, s, skip_routes, n_skip);
+}
+
+template <int G>
+cudaError_t launch_prep_g(const uint16_t *rows, int n_rows, int K, uint16_t *limbs, float *meta, cudaStream_t s,
+                          const uint32_t *skip_routes, int n_skip) {
+  const int slices = K / 8;
+  const int tpr = std::min(256, ((slices + 31) / 32) * 32);
+  const int spt = (slices + tpr - 1) / tpr;
+  const int rpc = std::min(8, 256 / tpr);
+  const int blocks = (n_rows + rpc - 1) / rpc;
+  const int threads = rpc * tpr;
+  uint32_t *err = device_error_word();
+  cudaError_t e = cudaSuccess;
+  if (spt == 1) e = launch_pdl(k_prep_rows<G, 1>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err, skip_routes, n_skip);
+  else if (spt == 2) e = launch_pdl(k_prep_rows<G, 2>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err, skip_routes, n_skip);
+  else if (spt <= 4) e = launch_pdl(k_prep_rows<G, 4>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err, skip_routes, n_skip);
+  else if (spt <= 8) e = launch_pdl(k_prep_rows<G, 8>, blocks, threads, 0, s, rows, n_rows, K, tpr, limbs, meta, err, skip_routes, n_skip);
   else return cudaErrorInvalidValue;
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
 cudaError_t launch_prep_rows(const uint16_t *rows, int n_rows, int K, int G,
-                             uint16_t *limbs, float *meta, cudaStream_t s) {
+                             uint16_t *limbs, float *meta, cudaStream_t s, const uint32_t *skip_routes, int n_skip) {
   if (n_rows <= 0) return cudaSuccess;
-  return G == 32 ? launch_prep_g<32>(rows, n_rows, K, limbs, meta, s) : launch_prep_g<64>(rows, n_rows, K, limbs, meta, s);
+  if (skip_routes == nullptr) n_skip = 0;
+  return G == 32 ? launch_prep_g<32>(rows, n_rows, K, limbs, meta, s, skip_routes, n_skip)
+                 : launch_prep_g<64>(rows, n_rows, K, limbs, meta, s, skip_routes, n_skip);
 }
 
 // ---------------------------------------------------------------------------
@@ -1057,6 +1194,45 @@ __device__ __forceinline__ void compute_block(uint32_t st, uint32_t xg, uint32_t
   }
 }
 
+// Epilogue of one (pair, row pair): bfloat16 activations -- gate/up rounded
+// to bfloat16, the bfloat16 SwiGLU sequence, bfloat16 stores -- or, with
+// float32 activations (a.f32), the same in float32 into float32 rows.
+// DUAL: yA = gate and yB = up of row oA; else yA, yB = rows oA, oB.
+template <bool DUAL>
+__device__ __forceinline__ void store_rows(const ExpertCallArgs &a, int pair, int O, int oA, int oB, float yA,
+                                           float yB, uint16_t *out, uint16_t *g_out, uint16_t *u_out) {
+  const size_t base = static_cast<size_t>(pair) * O;
+  if (a.f32) {
+    float *o = reinterpret_cast<float *>(out);
+    if (DUAL) {
+      if (oA < O) {
+        o[base + oA] = swiglu_f32(yA, yB);
+        if (g_out != nullptr && pair < a.n_pairs) {
+          reinterpret_cast<float *>(g_out)[base + oA] = yA;
+          reinterpret_cast<float *>(u_out)[base + oA] = yB;
+        }
+      }
+    } else {
+      if (oA < O) o[base + oA] = yA;
+      if (oB < O) o[base + oB] = yB;
+    }
+    return;
+  }
+  if (DUAL) {
+    if (oA < O) {
+      const float gvv = round_bf16(yA), uvv = round_bf16(yB);
+      out[base + oA] = f32_to_bf16(swiglu_bf16(g_exp_bf16, gvv, uvv));
+      if (g_out != nullptr && pair < a.n_pairs) {
+        g_out[base + oA] = f32_to_bf16(gvv);
+        u_out[base + oA] = f32_to_bf16(uvv);
+      }
+    }
+  } else {
+    if (oA < O) out[base + oA] = f32_to_bf16(yA);
+    if (oB < O) out[base + oB] = f32_to_bf16(yB);
+  }
+}
+
 // Compute one item's rows for NT token tiles (4 pairs each) and write them.
 template <int G, int WARPS, bool DUAL, int R, bool TILED, int NT>
 __device__ __forceinline__ void run_item(const ExpertCallArgs &a, const ItemInfo &cur, const uint8_t *xst,
@@ -1111,19 +1287,7 @@ __device__ __forceinline__ void run_item(const ExpertCallArgs &a, const ItemInfo
       const float2 ab = make_float2(__uint_as_float(abw.x), __uint_as_float(abw.y));
       const float yA = __fmul_rn(__fmul_rn(accA[t], ab.x), ab.y);
       const float yB = __fmul_rn(__fmul_rn(accB[t], ab.x), ab.y);
-      if (DUAL) {
-        if (oA < O) {
-          const float gvv = round_bf16(yA), uvv = round_bf16(yB);
-          out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(swiglu_bf16(g_exp_bf16, gvv, uvv));
-          if (g_out != nullptr && pair < a.n_pairs) {
-            g_out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(gvv);
-            u_out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(uvv);
-          }
-        }
-      } else {
-        if (oA < O) out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(yA);
-        if (oB < O) out[static_cast<size_t>(pair) * O + oB] = f32_to_bf16(yB);
-      }
+      store_rows<DUAL>(a, pair, O, oA, oB, yA, yB, out, g_out, u_out);
     }
   }
 }
@@ -1467,17 +1631,7 @@ __global__ void __launch_bounds__(128) k_expert_gemv(ExpertCallArgs a, GroupView
         const float yA = __fmul_rn(__fmul_rn(accA, ab.x), ab.y);
         const float yB = __fmul_rn(__fmul_rn(accB, ab.x), ab.y);
         const int oA = rg * RPW + r;
-        if (DUAL) {
-          const float gvv = round_bf16(yA), uvv = round_bf16(yB);
-          out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(swiglu_bf16(g_exp_bf16, gvv, uvv));
-          if (g_out != nullptr && pair < a.n_pairs) {
-            g_out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(gvv);
-            u_out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(uvv);
-          }
-        } else {
-          out[static_cast<size_t>(pair) * O + oA] = f32_to_bf16(yA);
-          out[static_cast<size_t>(pair) * O + oA + 8] = f32_to_bf16(yB);
-        }
+        store_rows<DUAL>(a, pair, O, oA, oA + 8, yA, yB, out, g_out, u_out);
       }
     }
     if (pass + 1 < passes) __syncthreads();  // sums and limbs are rewritten by the next pass
@@ -1826,6 +1980,45 @@ cudaError_t launch_combine(const uint16_t *d, const uint32_t *routes, const void
   dim3 grid((chunks + threads - 1) / threads, tokens);
   cudaError_t e = launch_pdl(k_combine, grid, threads, 0, s, d, routes, scores, scores_f32, tokens, slots, H, mode, shared_y,
                              shared, shared_gate, array_experts, table_records, out);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+// The combine with float32 activations: float32 per-slot rows, shared_y /
+// shared / shared_gate float32, float32 output; the same operations without
+// the bfloat16 roundings (the reference's kernel with T = float).
+__global__ void k_combine_f32(const float *d, const uint32_t *routes, const void *scores, int sf32, int T, int S,
+                              int H, int mode, const float *sy, const float *sh, const float *sg, int E_arr,
+                              int records, float *__restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.y;
+  const int h = blockIdx.x * blockDim.x + threadIdx.x;
+  if (h >= H || t >= T) return;
+  float acc = 0.0f;
+  for (int s = 0; s < S; ++s) {
+    const uint32_t r = routes[t * S + s];
+    const bool valid = (r & kSlotBit) ? ((r & 0x7FFFFFFFu) < static_cast<uint32_t>(records))
+                                      : (r < static_cast<uint32_t>(E_arr));
+    if (!valid) continue;
+    const float sc = sf32 ? static_cast<const float *>(scores)[t * S + s]
+                          : bf16_to_f32(static_cast<const uint16_t *>(scores)[t * S + s]);
+    acc = __fadd_rn(acc, __fmul_rn(d[(static_cast<size_t>(t) * S + s) * H + h], sc));
+  }
+  const size_t o = static_cast<size_t>(t) * H + h;
+  float res = acc;
+  if (mode == kCombineSharedY) res = __fadd_rn(acc, sy[o]);
+  else if (mode == kCombineParts) res = __fadd_rn(acc, __fmul_rn(sh[o], sg[t]));
+  out[o] = res;
+}
+
+cudaError_t launch_combine_f32(const float *d, const uint32_t *routes, const void *scores, int scores_f32,
+                               int tokens, int slots, int H, int mode, const float *shared_y, const float *shared,
+                               const float *shared_gate, int array_experts, int table_records, float *out,
+                               cudaStream_t s) {
+  dim3 grid((H + 255) / 256, tokens);
+  cudaError_t e = launch_pdl(k_combine_f32, grid, 256, 0, s, d, routes, scores, scores_f32, tokens, slots, H, mode,
+                             shared_y, shared, shared_gate, array_experts, table_records, out);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

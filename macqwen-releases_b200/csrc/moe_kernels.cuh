@@ -55,8 +55,16 @@ uint32_t *device_error_word();
 // Row fixed point of bf16 rows: limbs [rows][groups][2][G] fp16 (fragment
 // order), meta [rows][meta_pitch(groups)] float (fl(SX) per group, then
 // {A, B}; see meta_a_index).
+// With skip_routes, row r < n_skip whose route skip_routes[r] is
+// FNMOE_ROUTE_NONE (an empty slot) is skipped: its row is not read and its
+// limbs are not written.
 cudaError_t launch_prep_rows(const uint16_t *rows, int n_rows, int K, int G,
-                             uint16_t *limbs, float *meta, cudaStream_t s);
+                             uint16_t *limbs, float *meta, cudaStream_t s,
+                             const uint32_t *skip_routes = nullptr, int n_skip = 0);
+
+// The same fixed point of float32 rows (K <= 4096).
+cudaError_t launch_prep_rows_f32(const float *rows, int n_rows, int K, int G, uint16_t *limbs, float *meta,
+                                 cudaStream_t s, const uint32_t *skip_routes = nullptr, int n_skip = 0);
 
 // Softmax/top-k/renorm of <= 8 tokens followed by the grouping, one launch
 // (cudaErrorNotSupported when T or E is too large for it).  tiles_only:
@@ -108,6 +116,7 @@ struct ExpertCallArgs {
   int sb_async;                       // scale/bias bases 4-byte aligned (rows too when the group count is even)
   int sb_bulk;                        // scale/bias bases 16-byte aligned
   TiledView tiled;                    // tiled tables replace the arrays when set
+  int f32;                            // float32 activations: outputs float32, float32 SwiGLU
 };
 
 // gate/up + SwiGLU over all grouped tiles -> act [n_total, I] bf16.
@@ -128,6 +137,12 @@ cudaError_t launch_combine(const uint16_t *d, const uint32_t *routes,
                            const uint16_t *shared, const uint16_t *shared_gate,
                            int array_experts, int table_records,
                            uint16_t *out, cudaStream_t s);
+
+// The combine with float32 per-slot rows, shared inputs and output.
+cudaError_t launch_combine_f32(const float *d, const uint32_t *routes, const void *scores, int scores_f32,
+                               int tokens, int slots, int H, int mode, const float *shared_y, const float *shared,
+                               const float *shared_gate, int array_experts, int table_records, float *out,
+                               cudaStream_t s);
 
 // Router.
 // With prep_limbs / prep_meta set, batches of <= 4 tokens also compute the
@@ -218,4 +233,18 @@ cudaError_t launch_weighted_combine(const float *outputs, const int32_t *routes,
                                     const float *scores, float *out, int T,
                                     int S, int E, int H, cudaStream_t s);
 
+// Expert-parallel exchange (ep.cu); the FnEp* types come from fnmoe.h.
+}  // namespace fnmoe
+#include <string>
+struct FnEpConfig;
+struct FnEpWindow;
+namespace fnmoe {
+int ep_create(const FnEpConfig *cfg, void **out, std::string &err);
+int ep_ipc_handle(void *handle, void *out64, std::string &err);
+int ep_open_peers(void *handle, const void *handles, std::string &err);
+int ep_destroy(void *handle, std::string &err);
+int ep_window(void *handle, FnEpWindow *w, std::string &err);
+int ep_dispatch(void *handle, const void *x, const uint32_t *inds, uint32_t tokens, cudaStream_t s, std::string &err);
+int ep_return_combine(void *handle, const void *scores, const void *shared_gate, uint32_t tokens, void *out,
+                      cudaStream_t s, std::string &err);
 }  // namespace fnmoe

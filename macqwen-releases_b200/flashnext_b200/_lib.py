@@ -132,6 +132,23 @@ class FnPagedArgs(ctypes.Structure):
     ]
 
 
+EP_IPC_BYTES = 64
+
+
+class FnEpConfig(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", _u32), ("world", _u32), ("rank", _u32), ("capacity_tokens", _u32),
+        ("hidden_size", _u32), ("top_k", _u32), ("experts_per_rank", _u32), ("reserved", _u32),
+    ]
+
+
+class FnEpWindow(ctypes.Structure):
+    _fields_ = [
+        ("rows", _vp), ("ids", _vp), ("slot_outputs", _vp),
+        ("row_count", _u32), ("slots", _u32), ("bytes", _u64),
+    ]
+
+
 # Every exported symbol of include/fnmoe.h with its ctypes signature.
 SIGNATURES = {
     "fnmoe_available": ([], ctypes.c_int),
@@ -158,6 +175,13 @@ SIGNATURES = {
     "fnmoe_paged_decode": ([ctypes.POINTER(FnPagedArgs), _vp], ctypes.c_int),
     "fnmoe_read_device_errors": ([ctypes.POINTER(_u32), ctypes.c_int], ctypes.c_int),
     "fnmoe_profile_enable": ([ctypes.c_int], ctypes.c_int),
+    "fnmoe_ep_create": ([ctypes.POINTER(FnEpConfig), ctypes.POINTER(_vp)], ctypes.c_int),
+    "fnmoe_ep_ipc_handle": ([_vp, _vp], ctypes.c_int),
+    "fnmoe_ep_open_peers": ([_vp, _vp], ctypes.c_int),
+    "fnmoe_ep_window": ([_vp, ctypes.POINTER(FnEpWindow)], ctypes.c_int),
+    "fnmoe_ep_dispatch": ([_vp, _vp, _vp, _u32, _vp], ctypes.c_int),
+    "fnmoe_ep_return_combine": ([_vp, _vp, _vp, _u32, _vp, _vp], ctypes.c_int),
+    "fnmoe_ep_destroy": ([_vp], ctypes.c_int),
     "fnmoe_profile_read": ([ctypes.c_char_p, _u32, ctypes.c_int], ctypes.c_int),
 }
 

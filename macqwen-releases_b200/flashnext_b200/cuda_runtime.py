@@ -414,7 +414,12 @@ class MoEExecutor:
         torch = _torch()
         lib = _lib.ensure_device()
         host = isinstance(x, np.ndarray)
-        xt = _bf16(x, "x")
+        # float32 activations keep float32 arithmetic end to end (the
+        # reference's kernels with T = float, metal_runtime.py:371-373);
+        # bfloat16 activations the bfloat16 sequence
+        f32 = (x.dtype == np.float32) if host else (x.dtype == torch.float32)
+        act = torch.float32 if f32 else torch.bfloat16
+        xt = _dev(x, torch.float32) if f32 else _bf16(x, "x")
         rt = _u32(routes, "routes")
         tokens, slots = _shape(rt)
         H = self.hidden_size
@@ -439,7 +444,7 @@ class MoEExecutor:
         a.inter_size = inter
         a.expert_count = _shape(gate.weight)[0]
         a.group_size = self.group_size
-        a.x_dtype = _lib.DTYPE_BF16
+        a.x_dtype = _lib.DTYPE_F32 if f32 else _lib.DTYPE_BF16
         if scores is not None:
             st = _dev(scores)
             if st.dtype not in (torch.float32, torch.bfloat16):
@@ -447,13 +452,14 @@ class MoEExecutor:
             keep.append(st)
             a.scores = st.data_ptr()
             a.scores_dtype = _lib.DTYPE_F32 if st.dtype == torch.float32 else _lib.DTYPE_BF16
+        as_act = (lambda v, what: _dev(v, torch.float32)) if f32 else _bf16
         if shared_y is not None:
-            sy = _bf16(shared_y, "shared_y").reshape(tokens, H)
+            sy = as_act(shared_y, "shared_y").reshape(tokens, H)
             keep.append(sy)
             a.shared_y = sy.data_ptr()
         if shared is not None:
-            sh = _bf16(shared, "shared").reshape(tokens, H)
-            sg = _bf16(shared_gate, "shared_gate").reshape(tokens)
+            sh = as_act(shared, "shared").reshape(tokens, H)
+            sg = as_act(shared_gate, "shared_gate").reshape(tokens)
             keep += [sh, sg]
             a.shared = sh.data_ptr()
             a.shared_gate = sg.data_ptr()
@@ -467,16 +473,16 @@ class MoEExecutor:
         g_out = u_out = d_out = None
         if return_all:
             a.flags |= _lib.FLAG_RETURN_ALL
-            g_out = torch.empty((tokens, slots, inter), dtype=torch.bfloat16, device="cuda")
+            g_out = torch.empty((tokens, slots, inter), dtype=act, device="cuda")
             u_out = torch.empty_like(g_out)
-            d_out = torch.empty((tokens, slots, H), dtype=torch.bfloat16, device="cuda")
+            d_out = torch.empty((tokens, slots, H), dtype=act, device="cuda")
             a.gate_out, a.up_out, a.down_out = g_out.data_ptr(), u_out.data_ptr(), d_out.data_ptr()
         elif scores is None:
             a.flags |= _lib.FLAG_NO_COMBINE
-            d_out = torch.empty((tokens, slots, H), dtype=torch.bfloat16, device="cuda")
+            d_out = torch.empty((tokens, slots, H), dtype=act, device="cuda")
             a.down_out = d_out.data_ptr()
         else:
-            out = torch.empty((tokens, H), dtype=torch.bfloat16, device="cuda")
+            out = torch.empty((tokens, H), dtype=act, device="cuda")
             a.output = out.data_ptr()
         need = ctypes.c_uint64(0)
         _lib.check(lib.fnmoe_moe_workspace_size(ctypes.byref(a), ctypes.byref(need)), "workspace_size")

@@ -2,35 +2,42 @@
 
 Rank r of W owns routed experts [r*E/W, (r+1)*E/W) (tiled tables on the GPU);
 the router and the shared expert are replicated, and each rank routes its own
-tokens (data parallel over tokens).  One layer step:
+tokens (data parallel over tokens).  The reference runs the layer on one
+device (``models/flashnext/adaptive_topk.py:53-292``); this file distributes
+it without changing a bit of its result.  One layer step:
 
 1. route locally: logits -> softmax -> top-k -> renorm, plus the shared
-   expert's sigmoid gate (``fnmoe_router_topk_shared``; the reference computes
-   the same on one device, ``models/flashnext/adaptive_topk.py:53-64,263-264``);
-2. dispatch: the (token, slot) pairs are ordered by owner rank (stable in pair
-   order) and written into a fixed-capacity send buffer, ``capacity * top_k``
-   slots per peer (enough when every pair goes to one owner; the capacity is
-   the largest per-rank token count, given at construction or agreed per call
-   by an all-reduce); a slot carries the input row and the owner-local expert
-   id, or ``ROUTE_NONE`` when unused.  One ``all_to_all_single`` with equal
-   splits moves it; with a given capacity nothing is read back to the host
-   and the step can be captured in a CUDA graph;
-3. the owner runs its experts on the received rows, one slot per row (empty
-   slots are skipped by the grouping), together with the shared expert on its
-   own tokens (the shared expert is one more record of its tiled table;
-   ``fnmoe_moe_execute`` with per-slot outputs);
-4. the bfloat16 outputs come back along the reverse all-to-all and land in
-   their (token, slot) places;
+   expert's sigmoid gate (``fnmoe_router_topk_shared``; the reference
+   computes the same on one device, ``adaptive_topk.py:53-64,263-264``);
+2. dispatch: for every (token t, destination rank d) one row -- t's input
+   row and the k + 1 owner-local expert ids of t's slots on d
+   (``ROUTE_NONE`` elsewhere); slot k is the shared expert, which the
+   token's own rank runs (the shared expert is the last record of every
+   rank's tiled table).  A token's row crosses to a rank once, however many
+   of its slots that rank owns;
+3. every rank runs its experts on the rows it received, one executor call
+   with k + 1 slots per row (empty slots are skipped);
+4. return: each live routed (row, slot) output goes back to the token's
+   rank, into place [t][slot];
 5. the token's rank combines in slot order and adds the gated shared expert
-   (``fnmoe_combine``, ``metal_runtime.py:301-333``).
+   (``metal_runtime.py:301-333``).
 
 Every kernel gives a row's result independently of the rest of its batch, so
 the output is bit-identical to the single-device layer (``fnmoe_moe_layer``).
-Rows travel as int32 words (pairs of bfloat16), which every backend carries.
+
+Two transports carry steps 2 and 4:
+
+* ``PeerExchange`` (CUDA, the product): each rank's exchange window is
+  mapped into its peers through CUDA IPC; dispatch and return are kernels
+  that store straight into the peers' windows over NVLink, exactly the rows
+  that must move, with epoch flags and bounded waits (``fnmoe_ep_*``).  No
+  host synchronisation, so a step can be captured in a CUDA graph.
+* the collective path (``ExpertParallelMoE._collective``): the same protocol
+  over ``all_to_all_single`` with fixed-size buffers (any backend, e.g. gloo
+  ranks on CPU in the tests).
 
 The compute steps go through a backend object: ``CudaBackend`` (the product)
-or, for multi-process tests of the dispatch/combine logic on CPU ranks, any
-object with the same three methods (route, experts, combine).
+or, for multi-process tests on CPU ranks, any object with the same methods.
 """
 from __future__ import annotations
 
@@ -40,6 +47,8 @@ from typing import Mapping
 from . import _lib
 from .cuda_runtime import _bf16, _dev, _stream, _Workspace
 from .tiled import TiledExperts
+
+ROUTE_NONE_I32 = -1  # FNMOE_ROUTE_NONE as int32
 
 
 def _torch():
@@ -54,8 +63,13 @@ def _triple(p):
     return tuple(p)
 
 
+def _capturing() -> bool:
+    torch = _torch()
+    return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+
+
 class CudaBackend:
-    """The sm_100a kernels behind the four compute steps."""
+    """The sm_100a kernels behind the compute steps."""
 
     def __init__(self, router_weight, local_experts: Mapping, shared: Mapping, shared_expert_gate,
                  *, top_k: int, group_size: int = 32, renorm_blend: float = 1.0):
@@ -66,7 +80,7 @@ class CudaBackend:
         self.renorm_blend = float(renorm_blend)
         # Local records: this rank's routed experts, then the shared expert as
         # one more record (an ordinary expert to the executor), so received
-        # pairs and this rank's shared-expert rows go through one call.
+        # rows and this rank's shared-expert slots go through one call.
         torch = _torch()
         merged = {}
         for name in ("gate_proj", "up_proj", "down_proj"):
@@ -91,72 +105,123 @@ class CudaBackend:
         logits = torch.empty((T, self.expert_count), dtype=torch.bfloat16, device="cuda")
         sl = torch.empty((T,), dtype=torch.bfloat16, device="cuda")
         sg = torch.empty((T,), dtype=torch.bfloat16, device="cuda")
-        _lib.check(lib.fnmoe_router_topk_shared(
-            x.data_ptr(), self.router_weight.data_ptr(), self.shared_gate_weight.data_ptr(), T, self.hidden_size,
-            self.expert_count, self.top_k, self.renorm_blend, inds.data_ptr(), scores.data_ptr(), mass.data_ptr(),
-            logits.data_ptr(), sl.data_ptr(), sg.data_ptr(), _stream()), "router_topk_shared")
+        if T:
+            _lib.check(lib.fnmoe_router_topk_shared(
+                x.data_ptr(), self.router_weight.data_ptr(), self.shared_gate_weight.data_ptr(), T,
+                self.hidden_size, self.expert_count, self.top_k, self.renorm_blend, inds.data_ptr(),
+                scores.data_ptr(), mass.data_ptr(), logits.data_ptr(), sl.data_ptr(), sg.data_ptr(), _stream()),
+                "router_topk_shared")
         return inds, scores, sg
 
-    def _execute(self, x, routes, tiled, weights, expert_count, ws):
-        """Per-slot outputs [rows, H] of routes [rows, 1] (one slot per row)."""
-        torch = _torch()
+    def run_experts(self, x_ptr: int, ids_ptr: int, rows: int, slots: int, out_ptr: int) -> None:
+        """Per-slot outputs [rows, slots, H] of rows [rows, H] with local ids [rows, slots]."""
         lib = _lib.ensure_device()
-        rows = x.shape[0]
-        out = torch.empty((rows, self.hidden_size), dtype=torch.bfloat16, device="cuda")
-        if rows == 0:
-            return out
         a = _lib.FnMoEArgs()
         a.abi_version = _lib.ABI_VERSION
         a.flags = _lib.FLAG_NO_COMBINE
-        a.x = x.data_ptr()
-        if tiled is not None:
-            a.tiled = tiled.abi()
-        else:
-            for name, key in (("gate_proj", "gate"), ("up_proj", "up"), ("down_proj", "down")):
-                w, s, b = weights[name]
-                setattr(a, f"{key}_weight", w.data_ptr())
-                setattr(a, f"{key}_scales", s.data_ptr())
-                setattr(a, f"{key}_biases", b.data_ptr())
-        a.routes = routes.data_ptr()
-        a.tokens, a.slots = rows, 1
-        a.hidden_size, a.inter_size, a.expert_count = self.hidden_size, self.inter_size, expert_count
+        a.x = x_ptr
+        a.tiled = self.local.abi()
+        a.routes = ids_ptr
+        a.tokens, a.slots = rows, slots
+        a.hidden_size, a.inter_size, a.expert_count = self.hidden_size, self.inter_size, self.local_count + 1
         a.group_size = self.group_size
         a.x_dtype = _lib.DTYPE_BF16
-        a.down_out = out.data_ptr()
+        a.down_out = out_ptr
         need = ctypes.c_uint64(0)
         _lib.check(lib.fnmoe_moe_workspace_size(ctypes.byref(a), ctypes.byref(need)), "workspace_size")
-        w = ws.get(need.value)
+        w = self._ws.get(need.value)
         a.workspace, a.workspace_bytes = w.data_ptr(), w.numel()
         _lib.check(lib.fnmoe_moe_execute(ctypes.byref(a), _stream()), "moe_execute")
-        return out
 
-    def experts(self, rows, local_ids, x):
-        """Per-pair outputs of the received rows, and the shared expert on x."""
+    def experts(self, rows, ids):
+        """Per-slot outputs [R, S, H] of the received rows [R, H] (ids [R, S], -1 = empty)."""
         torch = _torch()
-        n = rows.shape[0]
-        all_rows = torch.cat([rows, x]).contiguous()
-        routes = torch.cat([local_ids.to(torch.int32),
-                            torch.full((x.shape[0],), self.local_count, dtype=torch.int32, device=x.device)])
-        out = self._execute(all_rows, routes.reshape(-1, 1).contiguous(), self.local, None, self.local_count + 1,
-                            self._ws)
-        return out[:n], out[n:]
+        R, S = ids.shape
+        out = torch.empty((R, S, self.hidden_size), dtype=torch.bfloat16, device="cuda")
+        if R:
+            self.run_experts(rows.data_ptr(), ids.contiguous().data_ptr(), R, S, out.data_ptr())
+        return out
 
     def combine(self, d, inds, scores, shared, shared_gate):
         torch = _torch()
         lib = _lib.ensure_device()
         T, S, H = d.shape
         out = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
-        _lib.check(lib.fnmoe_combine(d.data_ptr(), inds.data_ptr(), scores.data_ptr(), _lib.DTYPE_BF16, T, S, H,
-                                     self.expert_count, None, shared.data_ptr(), shared_gate.data_ptr(),
-                                     out.data_ptr(), _stream()), "combine")
+        if T:
+            _lib.check(lib.fnmoe_combine(d.data_ptr(), inds.data_ptr(), scores.data_ptr(), _lib.DTYPE_BF16, T, S, H,
+                                         self.expert_count, None, shared.data_ptr(), shared_gate.data_ptr(),
+                                         out.data_ptr(), _stream()), "combine")
         return out
 
 
+class PeerExchange:
+    """Dispatch and return over NVLink peer memory (``fnmoe_ep_*``).
+
+    Creating it is collective (every rank of ``group``): each rank allocates
+    its window, the IPC handles go round with ``all_gather_object``, and
+    every rank maps its peers' windows.  ``close()`` is collective too."""
+
+    def __init__(self, group, *, capacity_tokens: int, hidden_size: int, top_k: int, experts_per_rank: int):
+        import torch.distributed as dist
+
+        lib = _lib.ensure_device()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        cfg = _lib.FnEpConfig()
+        cfg.abi_version = _lib.ABI_VERSION
+        cfg.world, cfg.rank = self.world, self.rank
+        cfg.capacity_tokens, cfg.hidden_size, cfg.top_k = capacity_tokens, hidden_size, top_k
+        cfg.experts_per_rank = experts_per_rank
+        handle = ctypes.c_void_p()
+        _lib.check(lib.fnmoe_ep_create(ctypes.byref(cfg), ctypes.byref(handle)), "ep_create")
+        self.handle = handle
+        ipc = (ctypes.c_char * _lib.EP_IPC_BYTES)()
+        _lib.check(lib.fnmoe_ep_ipc_handle(handle, ipc), "ep_ipc_handle")
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, bytes(ipc), group=group)
+        blob = b"".join(gathered)
+        _lib.check(lib.fnmoe_ep_open_peers(handle, blob), "ep_open_peers")
+        dist.barrier(group=group)
+        self.window = _lib.FnEpWindow()
+        _lib.check(lib.fnmoe_ep_window(handle, ctypes.byref(self.window)), "ep_window")
+        self.capacity_tokens = capacity_tokens
+        self.top_k = top_k
+        self.hidden_size = hidden_size
+
+    def dispatch(self, x, inds) -> None:
+        lib = _lib.ensure_device()
+        _lib.check(lib.fnmoe_ep_dispatch(self.handle, x.data_ptr(), inds.data_ptr(), x.shape[0], _stream()),
+                   "ep_dispatch")
+
+    def return_combine(self, scores, shared_gate, out) -> None:
+        lib = _lib.ensure_device()
+        _lib.check(lib.fnmoe_ep_return_combine(self.handle, scores.data_ptr(), shared_gate.data_ptr(), out.shape[0],
+                                               out.data_ptr(), _stream()), "ep_return_combine")
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        if self.handle is None:
+            return
+        dist.barrier(group=self.group)  # no peer writes into this window any more
+        _lib.check(_lib.ensure_device().fnmoe_ep_destroy(self.handle), "ep_destroy")
+        self.handle = None
+
+
 class ExpertParallelMoE:
-    """One sparse-MoE layer with experts sharded over the ranks of `group`."""
+    """One sparse-MoE layer with experts sharded over the ranks of `group`.
+
+    ``capacity_tokens`` bounds the tokens a rank routes per call.  With it
+    given, a CUDA backend exchanges over NVLink peer memory (``PeerExchange``,
+    graph-capturable); otherwise, or with ``peer=False``, the protocol runs
+    over ``all_to_all_single`` with the capacity agreed per call.  Outside
+    graph capture the ranks first agree on the largest token count, so a call
+    that exceeds the capacity raises ``ValueError`` on every rank (instead of
+    one rank raising while the others wait in a collective)."""
 
     def __init__(self, backend, *, expert_count: int, hidden_size: int, top_k: int, group=None,
-                 capacity_tokens: int | None = None):
+                 capacity_tokens: int | None = None, peer: bool | None = None):
         import torch.distributed as dist
 
         self.backend = backend
@@ -169,58 +234,85 @@ class ExpertParallelMoE:
         self.per_rank = expert_count // self.world
         self.hidden_size = hidden_size
         self.top_k = top_k
-        # tokens per rank and call that every rank's send buffer can hold; None:
-        # agreed per call with an all-reduce of the ranks' token counts
         self.capacity_tokens = capacity_tokens
+        use_peer = peer if peer is not None else (isinstance(backend, CudaBackend) and capacity_tokens is not None)
+        if use_peer and capacity_tokens is None:
+            raise ValueError("the peer-memory exchange needs capacity_tokens")
+        self.exchange = (PeerExchange(group, capacity_tokens=capacity_tokens, hidden_size=hidden_size, top_k=top_k,
+                                      experts_per_rank=self.per_rank) if use_peer else None)
 
-    def _capacity(self, T, device):
+    def close(self) -> None:
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None
+
+    def _agree(self, T, device):
+        """Largest token count over the ranks (one all-reduce); raises on every
+        rank when it exceeds the fixed capacity."""
         torch = _torch()
         import torch.distributed as dist
 
-        if self.capacity_tokens is not None:
-            if T > self.capacity_tokens:
-                raise ValueError(f"{T} tokens exceed capacity_tokens={self.capacity_tokens}")
-            return self.capacity_tokens
         t = torch.tensor([T], dtype=torch.int64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
-        return int(t.item())
-
-    def _a2a(self, out, inp, out_splits, in_splits):
-        import torch.distributed as dist
-
-        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
-        return out
+        most = int(t.item())
+        if self.capacity_tokens is not None and most > self.capacity_tokens:
+            raise ValueError(f"{most} tokens on some rank exceed capacity_tokens={self.capacity_tokens}")
+        return most
 
     def __call__(self, x):
         torch = _torch()
-        T, H = x.shape
-        k = self.top_k
-        W = self.world
-        dev = x.device
+        T = x.shape[0]
+        if self.capacity_tokens is None or not _capturing():
+            cap = self._agree(T, x.device)
+        else:
+            cap = self.capacity_tokens
         inds, scores, sg = self.backend.route(x)
-        flat = inds.reshape(-1).to(torch.int64)
-        owner = torch.div(flat, self.per_rank, rounding_mode="floor")
-        order = torch.sort(owner, stable=True).indices  # pairs grouped by owner, pair order kept
-        so = owner[order]
-        # pairs per owner (scatter_add into a fixed-size tensor: bincount would read its size back to the host)
-        counts = torch.zeros(W, dtype=torch.int64, device=dev).scatter_add_(0, owner, torch.ones_like(owner))
-        starts = torch.cumsum(counts, 0) - counts
-        pos = torch.arange(T * k, device=dev) - starts[so]  # slot inside the owner's segment
-        cap = self._capacity(T, dev) * k
-        w = H // 2
-        # one payload row per slot: the input row as H/2 int32 words, then the
-        # owner-local expert id (ROUTE_NONE when the slot is empty) and 3 pad words
-        send = torch.zeros((W, cap, w + 4), dtype=torch.int32, device=dev)
-        send[:, :, w] = -1  # ROUTE_NONE as int32
-        send[so, pos, :w] = x.view(torch.int32)[torch.div(order, k, rounding_mode="floor")]
-        send[so, pos, w] = (flat[order] - so * self.per_rank).to(torch.int32)
-        recv = torch.empty_like(send)
-        self._a2a(recv.view(W * cap, w + 4), send.view(W * cap, w + 4), None, None)
-        recv_rows = recv[:, :, :w].reshape(W * cap, w).view(x.dtype)
-        d_recv, shared = self.backend.experts(recv_rows, recv[:, :, w].reshape(-1).contiguous(), x)
-        back = torch.empty((W, cap, H), dtype=d_recv.dtype, device=dev)
-        self._a2a(back.view(W * cap, H).view(torch.int32), d_recv.reshape(W * cap, H).contiguous().view(torch.int32),
-                  None, None)
-        d = torch.empty((T * k, H), dtype=back.dtype, device=dev)
-        d[order] = back[so, pos]
-        return self.backend.combine(d.view(T, k, H), inds, scores, shared, sg)
+        if self.exchange is not None:
+            ex = self.exchange
+            ex.dispatch(x, inds)
+            w = ex.window
+            self.backend.run_experts(w.rows, w.ids, w.row_count, w.slots, w.slot_outputs)
+            out = torch.empty((T, self.hidden_size), dtype=torch.bfloat16, device=x.device)
+            ex.return_combine(scores, sg, out)
+            return out
+        return self._collective(x, inds, scores, sg, self.capacity_tokens or cap)
+
+    # -- the same protocol over all_to_all_single (fixed-size buffers) --------
+
+    def _a2a(self, out, inp):
+        import torch.distributed as dist
+
+        dist.all_to_all_single(out, inp, None, None, group=self.group)
+        return out
+
+    def _collective(self, x, inds, scores, sg, cap):
+        torch = _torch()
+        T, H = x.shape
+        k, W, dev = self.top_k, self.world, x.device
+        cap = max(int(cap), 1)
+        flat = inds.to(torch.int64)
+        owner = torch.div(flat, self.per_rank, rounding_mode="floor")       # [T, k]
+        ranks = torch.arange(W, device=dev)
+        # ids[d, t, s]: owner-local expert id of slot s on rank d, or none; slot k: shared expert on the own rank
+        ids = torch.full((W, cap, k + 1), ROUTE_NONE_I32, dtype=torch.int32, device=dev)
+        local = (flat - owner * self.per_rank).to(torch.int32)
+        mine = owner[None, :, :] == ranks[:, None, None]                      # [W, T, k]
+        ids[:, :T, :k] = torch.where(mine, local[None].expand(W, T, k), torch.full_like(local[None].expand(W, T, k),
+                                                                                       ROUTE_NONE_I32))
+        ids[self.rank, :T, k] = self.per_rank
+        rows = torch.zeros((W, cap, H), dtype=x.dtype, device=dev)
+        rows[:, :T] = x[None]
+        # rows travel as int32 words (pairs of bfloat16), which every backend carries
+        r_rows = self._a2a(torch.empty((W * cap, H // 2), dtype=torch.int32, device=dev),
+                           rows.view(W * cap, H).view(torch.int32)).view(x.dtype)
+        r_ids = self._a2a(torch.empty_like(ids).view(W * cap, k + 1), ids.view(W * cap, k + 1))
+        d = self.backend.experts(r_rows, r_ids)                               # [W*cap, k+1, H]
+        d = d.view(W, cap, k + 1, H)
+        back = self._a2a(torch.empty((W * cap * k, H // 2), dtype=torch.int32, device=dev),
+                         d[:, :, :k].contiguous().view(W * cap * k, H).view(torch.int32)).view(d.dtype)
+        back = back.view(W, cap, k, H)                                        # [owner, t, slot, H]
+        tok = torch.arange(T, device=dev)[:, None].expand(T, k)
+        slot = torch.arange(k, device=dev)[None, :].expand(T, k)
+        d_slots = back[owner, tok, slot]                                      # [T, k, H]
+        shared = d[self.rank, :T, k]                                          # [T, H]
+        return self.backend.combine(d_slots.contiguous(), inds, scores, shared.contiguous(), sg)

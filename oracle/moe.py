@@ -132,6 +132,22 @@ def swiglu_bf16(gate, up) -> np.ndarray:
 # --------------------------------------------------------------------------
 
 
+def swiglu_f32(gate, up) -> np.ndarray:
+    """The fused up-SwiGLU sequence with float32 activations (the reference's
+    Metal kernel instantiated with T = float, metal_runtime.py:267-285):
+    |g| -> exp -> 1+e -> 1/d -> select -> g*sigma -> *u, each op rounded to
+    float32; exp correctly rounded (float64 exp, one rounding)."""
+    g = np.asarray(gate, dtype=np.float32)
+    u = np.asarray(up, dtype=np.float32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        mag = np.abs(g)
+        ex = np.exp(mag.astype(np.float64)).astype(np.float32)
+        den = (np.float32(1.0) + ex).astype(np.float32)
+        small = (np.float32(1.0) / den).astype(np.float32)
+        sig = np.where(g < 0, small, (np.float32(1.0) - small).astype(np.float32)).astype(np.float32)
+        return ((g * sig).astype(np.float32) * u).astype(np.float32)
+
+
 def fixed_point_rows(x):
     """Row fixed point of the inputs.
 
@@ -254,12 +270,15 @@ def _project_pairs(rows, expert_of_row, part, group_size):
 
 
 def executor(x, routes, gate, up, down, *, scores=None, shared_y=None,
-             shared=None, shared_gate=None, group_size=32, return_all=False):
+             shared=None, shared_gate=None, group_size=32, return_all=False, f32=False):
     """Gate -> up -> SwiGLU -> down -> slot-ordered combine (+ shared).
 
     ``gate``/``up``/``down`` are ``(words, scales, biases)`` with expert-major
     arrays (words uint32 [E, O, K/8]; scales/biases bfloat16-valued float32).
-    ``routes`` [T, S] expert indices.  Returns bfloat16-valued float32 arrays:
+    ``routes`` [T, S] expert indices.  ``f32``: float32 activations (the
+    reference's kernels instantiated with T = float): the same sequence of
+    operations with every result rounded to float32 instead of bfloat16,
+    float32 outputs.  Otherwise returns bfloat16-valued float32 arrays:
     ``(gate [T,S,I], up [T,S,I], down [T,S,H])`` for ``return_all``; the
     per-slot down outputs [T,S,H] when ``scores`` is None; else the combined
     [T,H] output with the requested shared epilogue
@@ -276,10 +295,11 @@ def executor(x, routes, gate, up, down, *, scores=None, shared_y=None,
     dp = expert_parts(*down)
     flat_e = routes.reshape(-1)
     xrows = np.repeat(x, slots, axis=0)
-    g = bf16.round_f32(_project_pairs(xrows, flat_e, gp, group_size))
-    u = bf16.round_f32(_project_pairs(xrows, flat_e, upp, group_size))
-    act = swiglu_bf16(g, u)
-    d = bf16.round_f32(_project_pairs(act, flat_e, dp, group_size))
+    rnd = (lambda a: np.asarray(a, np.float32)) if f32 else bf16.round_f32
+    g = rnd(_project_pairs(xrows, flat_e, gp, group_size))
+    u = rnd(_project_pairs(xrows, flat_e, upp, group_size))
+    act = swiglu_f32(g, u) if f32 else swiglu_bf16(g, u)
+    d = rnd(_project_pairs(act, flat_e, dp, group_size))
     inter = g.shape[-1]
     hidden = d.shape[-1]
     g = g.reshape(t, slots, inter)
@@ -289,11 +309,14 @@ def executor(x, routes, gate, up, down, *, scores=None, shared_y=None,
         return g, u, d
     if scores is None:
         return d
-    return combine(d, scores, shared_y=shared_y, shared=shared, shared_gate=shared_gate)
+    return combine(d, scores, shared_y=shared_y, shared=shared, shared_gate=shared_gate, f32=f32)
 
 
-def combine(d, scores, *, shared_y=None, shared=None, shared_gate=None):
-    """Slot-ordered combine of bfloat16 per-slot outputs (metal_runtime.py:301-333)."""
+def combine(d, scores, *, shared_y=None, shared=None, shared_gate=None, f32=False):
+    """Slot-ordered combine of per-slot outputs (metal_runtime.py:301-333):
+    float32 products added in slot order (no fused multiply-add), then the
+    shared add; every result rounded to bfloat16, or (``f32``) kept float32."""
+    rnd = (lambda a: np.asarray(a, np.float32)) if f32 else bf16.round_f32
     d = np.asarray(d, np.float32)
     sc = np.asarray(scores, np.float32)
     t, slots, hidden = d.shape
@@ -301,13 +324,13 @@ def combine(d, scores, *, shared_y=None, shared=None, shared_gate=None):
     with np.errstate(all="ignore"):
         for s in range(slots):
             acc = acc + (d[:, s, :] * sc[:, s][:, None])
-    routed = bf16.round_f32(acc)
-    if shared_y is not None:
-        return bf16.round_f32(routed + np.asarray(shared_y, np.float32).reshape(t, hidden))
-    if shared is not None:
-        comp = bf16.round_f32(np.asarray(shared, np.float32).reshape(t, hidden)
-                              * np.asarray(shared_gate, np.float32).reshape(t, 1))
-        return bf16.round_f32(routed + comp)
+        routed = rnd(acc)
+        if shared_y is not None:
+            return rnd(routed + np.asarray(shared_y, np.float32).reshape(t, hidden))
+        if shared is not None:
+            comp = rnd(np.asarray(shared, np.float32).reshape(t, hidden)
+                       * np.asarray(shared_gate, np.float32).reshape(t, 1))
+            return rnd(routed + comp)
     return routed
 
 

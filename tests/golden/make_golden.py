@@ -13,7 +13,8 @@ inputs whose values are exactly representable in bfloat16:
   (metal_runtime.py:955-987);
 * ``MetalMoEExecutor(..., backend="reference").execute`` outputs: combined,
   per-slot and ``return_all`` forms, plus the ``shared_y`` and shared-parts
-  adds (metal_runtime.py:764-941);
+  adds (metal_runtime.py:764-941), for bfloat16-valued and for float32
+  activations;
 * the ``weighted_combine`` known-answer case of
   ``models/flashnext/tests/unit/test_metal_runtime.py:222-239``;
 * the Q4/G32 and Q4/G64 slab record layouts (slab_pack.py:96-153).
@@ -107,6 +108,27 @@ def main() -> None:
         ("with_shared_parts", with_parts),
     ):
         out[f"exec_{name}"] = np.asarray(val)
+
+    # 2b. the same executor with float32 activations (production Flash-Next
+    # keeps activations float32 with bfloat16 scales/biases,
+    # metal_runtime.py:371-373; tests/unit/test_metal_runtime.py:516-557)
+    xf = rng.normal(0, 1, (2, hidden)).astype(np.float32)
+    sf = rng.dirichlet(np.ones(top_k), size=2).astype(np.float32)
+    syf = rng.normal(0, 0.5, (2, hidden)).astype(np.float32)
+    shf = rng.normal(0, 0.5, (2, hidden)).astype(np.float32)
+    sgf = rng.uniform(0, 1, (2, 1)).astype(np.float32)
+    f_combined = ex.execute(xf, routes, packs, scores=sf)
+    f_per_slot = ex.execute(xf, routes, packs)
+    fg, fu, fd = ex.execute(xf, routes, packs, return_all=True)
+    f_with_y = ex.execute(xf, routes, packs, scores=sf, shared_y=syf)
+    f_with_parts = ex.execute(xf, routes, packs, scores=sf, shared=shf, shared_gate=sgf)
+    for name, val in (
+        ("x", xf), ("scores", sf), ("shared_y", syf), ("shared", shf), ("shared_gate", sgf),
+        ("combined", f_combined), ("per_slot", f_per_slot), ("all_gate", fg), ("all_up", fu), ("all_down", fd),
+        ("with_shared_y", f_with_y), ("with_shared_parts", f_with_parts),
+    ):
+        out[f"exec32_{name}"] = np.asarray(val)
+        assert np.asarray(val).dtype == np.float32
 
     # 3. weighted_combine known answer (test_metal_runtime.py:222-239)
     eo = np.array([[[1.0, 2.0], [10.0, 20.0], [100.0, 200.0]],

@@ -64,17 +64,26 @@ class OracleBackend:
         _, sg, _ = moe.shared_expert(xn, *self.shared, self.wg, G)
         return torch.from_numpy(inds.astype(np.int32)), self._bf(scores), self._bf(sg.reshape(-1))
 
-    def experts(self, rows, local_ids, x):
+    def experts(self, rows, ids):
+        """Per-slot outputs [R, S, H] of received rows; id == experts per rank is the shared expert."""
         from oracle import moe
 
-        ids = local_ids.numpy().astype(np.int64)
-        d = np.zeros((rows.shape[0], H), np.float32)
-        live = ids >= 0  # ROUTE_NONE (-1 as int32) marks an empty slot
-        if live.any():
-            d[live] = moe.executor(rows.float().numpy()[live], ids[live].reshape(-1, 1), self.bank["gate_proj"],
-                                   self.bank["up_proj"], self.bank["down_proj"], group_size=G).reshape(-1, H)
-        sh, _, _ = moe.shared_expert(x.float().numpy(), *self.shared, self.wg, G)
-        return self._bf(d), self._bf(sh)
+        ids = ids.numpy().astype(np.int64)
+        R, S = ids.shape
+        xr = rows.float().numpy()
+        d = np.zeros((R, S, H), np.float32)
+        per = self.bank["gate_proj"][0].shape[0]
+        routed = (ids >= 0) & (ids < per)
+        if routed.any():
+            r, s = np.nonzero(routed)
+            d[r, s] = moe.executor(xr[r], ids[r, s].reshape(-1, 1), self.bank["gate_proj"], self.bank["up_proj"],
+                                   self.bank["down_proj"], group_size=G).reshape(-1, H)
+        shared = ids == per
+        if shared.any():
+            r, s = np.nonzero(shared)
+            sh, _, _ = moe.shared_expert(xr[r], *self.shared, self.wg, G)
+            d[r, s] = sh
+        return self._bf(d)
 
     def combine(self, d, inds, scores, shared, shared_gate):
         from oracle import moe
@@ -111,6 +120,50 @@ def _worker(rank, world, port, result_dir):
         np.save(os.path.join(result_dir, f"r{rank}.npy"), np.array([same]))
     finally:
         dist.destroy_process_group()
+
+
+def _overflow_worker(rank, world, port, result_dir):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (root, os.path.join(root, "macqwen-releases_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    from flashnext_b200.expert_parallel import ExpertParallelMoE
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        bank, shared, w, wg = _model()
+        per = E // world
+        backend = OracleBackend(bank, shared, w, wg, rank * per, (rank + 1) * per)
+        layer = ExpertParallelMoE(backend, expert_count=E, hidden_size=H, top_k=K, capacity_tokens=6)
+        x = _tokens(rank)  # rank 0: 5 tokens (fits), rank 1: 7 tokens (exceeds 6)
+        raised = False
+        try:
+            layer(OracleBackend._bf(x))
+        except ValueError:
+            raised = True
+        # the ranks are still in step: one more collective completes
+        import torch
+        t = torch.ones(1)
+        dist.all_reduce(t)
+        np.save(os.path.join(result_dir, f"o{rank}.npy"), np.array([raised, float(t[0]) == world]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_capacity_overflow_raises_on_every_rank(tmp_path):
+    """One rank routes more tokens than the fixed capacity: every rank raises
+    ValueError before any exchange, and the group stays usable."""
+    import torch.multiprocessing as mp
+
+    mp.spawn(_overflow_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        raised, alive = np.load(tmp_path / f"o{r}.npy")
+        assert raised, f"rank {r} did not raise"
+        assert alive, f"rank {r}: the group hung or broke"
 
 
 def _free_port():

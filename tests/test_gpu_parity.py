@@ -546,3 +546,78 @@ def test_executor_tiny_and_subnormal_activations_bit_exact(cuda_lib):
     assert_bf16_equal(_np(g), og, "gate")
     assert_bf16_equal(_np(u), ou, "up")
     assert_bf16_equal(_np(d), od, "down")
+
+
+# --------------------------------------------------------------------------
+# float32 activations (metal_runtime.py:371-373; test_metal_runtime.py:516-557)
+# --------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("tokens,slots,hidden,inter,experts,group", [
+    (1, 10, 2048, 512, 64, 32),   # batch 1 (4-warp row kernel on the reference-layout arrays)
+    (9, 10, 512, 256, 16, 32),    # 16-warp grouped row kernel (>= 64 pairs)
+    (3, 3, 256, 128, 6, 64),      # group size 64
+])
+def test_executor_float32_activations_bit_exact(cuda_lib, tokens, slots, hidden, inter, experts, group):
+    """float32 x: the executor keeps float32 arithmetic (every intermediate
+    rounded to float32, the float32 SwiGLU sequence) and returns float32,
+    bit for bit equal to the oracle's float32 executor -- combined, per-slot,
+    return_all and both shared epilogues."""
+    import torch
+
+    from flashnext_b200 import MoEExecutor, synthetic
+    bank = synthetic.expert_bank(experts, hidden, inter, group, seed=tokens + 400)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(tokens + 401)
+    x = torch.randn((tokens, hidden), generator=g, device="cuda")  # full float32 mantissas
+    rng = np.random.default_rng(tokens)
+    routes = np.stack([rng.permutation(experts)[:slots] for _ in range(tokens)]).astype(np.int32)
+    scores = rng.dirichlet(np.ones(slots), size=tokens).astype(np.float32)
+    sy = rng.normal(0, 0.5, (tokens, hidden)).astype(np.float32)
+    sh = rng.normal(0, 0.5, (tokens, hidden)).astype(np.float32)
+    sgate = rng.uniform(0, 1, (tokens, 1)).astype(np.float32)
+    ex = MoEExecutor(experts, hidden, slots, group_size=group, max_tokens=max(8, tokens))
+    nb = _bank_np(bank)
+    r = torch.tensor(routes).cuda()
+    xn = x.cpu().numpy()
+    out = ex.execute(x, r, bank, scores=torch.tensor(scores).cuda())
+    assert out.dtype == torch.float32
+    want = moe.executor(xn, routes, nb["gate_proj"], nb["up_proj"], nb["down_proj"], scores=scores,
+                        group_size=group, f32=True)
+    np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    gg, uu, dd = ex.execute(x, r, bank, return_all=True)
+    og, ou, od = moe.executor(xn, routes, nb["gate_proj"], nb["up_proj"], nb["down_proj"], group_size=group,
+                              return_all=True, f32=True)
+    for got, w in ((gg, og), (uu, ou), (dd, od)):
+        np.testing.assert_array_equal(got.cpu().numpy().view(np.uint32), w.view(np.uint32))
+    per_slot = ex.execute(x, r, bank)
+    np.testing.assert_array_equal(per_slot.cpu().numpy().view(np.uint32), od.view(np.uint32))
+    for kw in ({"shared_y": sy}, {"shared": sh, "shared_gate": sgate}):
+        got = ex.execute(x, r, bank, scores=torch.tensor(scores).cuda(), **{k: torch.tensor(v).cuda()
+                                                                             for k, v in kw.items()})
+        w = moe.executor(xn, routes, nb["gate_proj"], nb["up_proj"], nb["down_proj"], scores=scores,
+                         group_size=group, f32=True, **kw)
+        np.testing.assert_array_equal(got.cpu().numpy().view(np.uint32), w.view(np.uint32))
+
+
+def test_executor_float32_reference_unit_case(cuda_lib):
+    """The reference's mixed-precision unit case (test_metal_runtime.py:516-557):
+    float32 x = ((arange(256) % 31) - 15) / 64 with bfloat16 scales/biases,
+    routes [[0, 2, 3]], scores [[0.2, 0.3, 0.5]]: float32 output within the
+    reference's tolerance (rtol 1e-3, atol 1e-4) of its NumPy executor, and
+    bit-exact to the oracle."""
+    import torch
+
+    from flashnext_b200 import MoEExecutor, synthetic
+    H, I, E = 256, 128, 4
+    bank = synthetic.expert_bank(E, H, I, 32, seed=516)
+    x = (((np.arange(H, dtype=np.float32) % 31) - 15) / 64).reshape(1, H).astype(np.float32)
+    routes = np.array([[0, 2, 3]], dtype=np.int32)
+    scores = np.array([[0.2, 0.3, 0.5]], dtype=np.float32)
+    got = MoEExecutor(E, H, 3).execute(x, routes, bank, scores=scores)
+    assert isinstance(got, np.ndarray) and got.dtype == np.float32
+    nb = _bank_np(bank)
+    ref = moe.reference_execute(x, routes, nb["gate_proj"], nb["up_proj"], nb["down_proj"], scores=scores)
+    np.testing.assert_allclose(got, ref, rtol=1e-3, atol=1e-4)
+    want = moe.executor(x, routes, nb["gate_proj"], nb["up_proj"], nb["down_proj"], scores=scores, f32=True)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))

@@ -109,3 +109,58 @@ def test_golden_inputs_are_bfloat16_exact(golden):
     for key in ("exec_x", "exec_gate_s", "exec_gate_b", "proj_g32_x", "proj_g32_s"):
         v = golden[key].astype(np.float32)
         np.testing.assert_array_equal(bf16.round_f32(v), v)
+
+
+def _exec32_inputs(golden):
+    e, gate, up, down = _exec_inputs(golden)
+    f = {k[len("exec32_"):]: v for k, v in golden.items() if k.startswith("exec32_")}
+    return e, f, gate, up, down
+
+
+def test_restated_reference_executor_float32_is_bit_exact(golden):
+    """float32 activations through the reference NumPy executor: the
+    restatement reproduces every output of the reference run bit for bit."""
+    e, f, gate, up, down = _exec32_inputs(golden)
+    x, r = f["x"], e["routes"]
+    np.testing.assert_array_equal(moe.reference_execute(x, r, gate, up, down, scores=f["scores"]), f["combined"])
+    np.testing.assert_array_equal(moe.reference_execute(x, r, gate, up, down), f["per_slot"])
+    g_all, u_all, d_all = moe.reference_execute(x, r, gate, up, down, return_all=True)
+    np.testing.assert_array_equal(g_all, f["all_gate"])
+    np.testing.assert_array_equal(u_all, f["all_up"])
+    np.testing.assert_array_equal(d_all, f["all_down"])
+
+
+def test_canonical_float32_executor_matches_reference_run(golden):
+    """The canonical float32 path (fixed-point projections, the float32
+    SwiGLU sequence, slot-ordered float32 combine) against the reference's
+    float32 run: the two differ only in float32 rounding order (the reference
+    accumulates each projection in float64 and uses u * g / (1 + exp(-g))),
+    so they agree to float32 precision -- relative 1e-5 of each output's scale."""
+    e, f, gate, up, down = _exec32_inputs(golden)
+    x, r = f["x"], e["routes"]
+    cases = [
+        (moe.executor(x, r, gate, up, down, scores=f["scores"], f32=True), f["combined"]),
+        (moe.executor(x, r, gate, up, down, f32=True), f["per_slot"]),
+        (moe.executor(x, r, gate, up, down, scores=f["scores"], shared_y=f["shared_y"], f32=True),
+         f["with_shared_y"]),
+        (moe.executor(x, r, gate, up, down, scores=f["scores"], shared=f["shared"], shared_gate=f["shared_gate"],
+                      f32=True), f["with_shared_parts"]),
+    ]
+    g_all, u_all, d_all = moe.executor(x, r, gate, up, down, return_all=True, f32=True)
+    cases += [(g_all, f["all_gate"]), (u_all, f["all_up"]), (d_all, f["all_down"])]
+    for got, want in cases:
+        assert got.dtype == np.float32 and got.shape == want.shape
+        np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5 * np.abs(want).max())
+
+
+def test_float32_swiglu_sequence():
+    """The float32 SwiGLU sequence against float64 evaluation of g*sigmoid(g)*u:
+    a few float32 ulps; where exp(|g|) overflows float32 the sequence gives
+    sigma = 0 or 1 exactly (an absolute error below 1e-30)."""
+    rng = np.random.default_rng(5)
+    g = np.concatenate([rng.normal(0, 4, 4000), [0.0, -0.0, 90.0, -90.0, 1e-30]]).astype(np.float32)
+    u = rng.normal(0, 1, g.shape).astype(np.float32)
+    got = moe.swiglu_f32(g, u).astype(np.float64)
+    gd, ud = g.astype(np.float64), u.astype(np.float64)
+    want = gd / (1.0 + np.exp(-gd)) * ud
+    assert np.all(np.abs(got - want) <= 4 * np.spacing(np.abs(want).astype(np.float32)).astype(np.float64) + 1e-30)
