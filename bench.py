@@ -467,9 +467,21 @@ def gpu_arm(args):
     layer_bytes = (avg_used + 1) * EXPERT_BYTES + ROUTER_BYTES + HIDDEN * 2 + 2 * tokens * HIDDEN * 2
     step_s = ms / args.steps / 1000.0
 
+    # per-step distribution over 200 more steps (events between steps)
+    distribution = step_distribution(step, 200) if world == 1 else None
+
     batch1 = None
     if world == 1 and args.workload == "c2" and not args.no_batch1:
         batch1 = batch1_numbers(hbm_peak)
+
+    # the other benchmark configs, one GPU (weights of each config are freed before the next)
+    configs = {}
+    if world == 1 and args.workload == "c2" and not args.no_configs:
+        del blocks, xs, outs, host_x, host_out, dev_x
+        torch.cuda.empty_cache()
+        configs["c5"] = c5_numbers(20, 3)
+        configs["c4"] = c4_numbers(5, 3)
+        configs["c3"] = c3_numbers(10)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -504,8 +516,12 @@ def gpu_arm(args):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if distribution is not None:
+            line["step_ms"] = distribution
         if batch1 is not None:
             line["batch1"] = batch1
+        if configs:
+            line["configs"] = configs
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -707,6 +723,23 @@ def _capture_ep_graphs(eps, xs, graphs, gouts):
     torch.cuda.synchronize()
 
 
+def step_distribution(step, n):
+    """Device time of each of n more steps (CUDA events between the steps,
+    after a spin kernel that covers the host enqueue): median, p10, p90 (ms)."""
+    import torch
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(n + 1)]
+    torch.cuda.synchronize()
+    torch.cuda._sleep(CUSHION_CYCLES)
+    ev[0].record()
+    for i in range(n):
+        step(i)
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    ts = [ev[i].elapsed_time(ev[i + 1]) for i in range(n)]
+    return {"steps": n, "median_ms": statistics.median(ts), "p10_ms": _pct(ts, 10), "p90_ms": _pct(ts, 90)}
+
+
 def batch1_numbers(hbm_peak):
     """Batch-1 (config 1) tokens/s over 8 distinct layers via one CUDA graph."""
     import torch
@@ -780,7 +813,7 @@ def _graph(fn):
     return g
 
 
-def c5_arm(args):
+def c5_numbers(steps: int, warmup: int) -> dict:
     """Config 5: paged-KV decode attention, GQA 16/2, D 256, page 64, 16 sequences
     with context ~ U[1k, 32k]; two KV pools (each > L2) alternate per step."""
     import torch
@@ -797,26 +830,37 @@ def c5_arm(args):
         P = sets[i % 2]
         paged_decode(P.q, P.k_cache, P.v_cache, P.block_table, P.context_lens, P.scale, out=outs[i % 2])
 
-    for i in range(max(3, args.warmup)):
+    for i in range(max(3, warmup)):
         step(i)
-    ms = _timed(step, args.steps) / args.steps
+    ms = _timed(step, steps) / steps
     ctx = [int(P.context_lens.sum()) for P in sets]
     kv_bytes = sum(ctx) / 2 * 2048  # K and V, 2 KV heads x 256 x 2 B per context token (mean of the two sets)
     io = 2 * 16 * 16 * 256 * 2
     gbs = (kv_bytes + io) / (ms / 1000.0) / 1e9
-    print(json.dumps({
-        "metric": "paged-KV decode attention GB/s (C5)", "value": gbs, "unit": "GB/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
-        "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "C5: 16 sequences, GQA 16/2, head_dim 256, page 64, ctx U[1k,32k]",
-                   "context_tokens": ctx, "l2": "two KV pools of ~0.5 GB alternate"},
+    del sets, outs
+    torch.cuda.empty_cache()
+    return {
+        "metric": "paged-KV decode attention GB/s (C5)", "value": gbs, "unit": "GB/s", "steps": steps,
+        "ms_per_step": ms, "workload": "C5: 16 sequences, GQA 16/2, head_dim 256, page 64, ctx U[1k,32k]",
+        "context_tokens": ctx, "l2": "two KV pools of ~0.5 GB alternate",
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": gbs / hbm_peak},
+    }
+
+
+def c5_arm(args):
+    r = c5_numbers(args.steps, args.warmup)
+    print(json.dumps({
+        "metric": r["metric"], "value": r["value"], "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": r["ms_per_step"], "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic", "config": {"workload": r["workload"], "context_tokens": r["context_tokens"],
+                                        "l2": r["l2"]},
+        "roofline": r["roofline"],
     }), flush=True)
     return 0
 
 
-def c3_arm(args):
+def c3_numbers(steps: int) -> dict:
     """Config 3: 48-layer stack, hidden 3072, 512 experts of intermediate 640 +
     shared, top-10, Q4/G32; batch-1 and batch-64 decode through all 48 layers
     (CUDA graph replays).  Each layer is generated, tiled and its arrays freed
@@ -850,7 +894,7 @@ def c3_arm(args):
         g = _graph(stack)
         for _ in range(3):
             g.replay()
-        ms = _timed(lambda i: g.replay(), args.steps) / args.steps
+        ms = _timed(lambda i: g.replay(), steps) / steps
         used = [int(torch.unique(b.last_inds).numel()) for b in blocks]
         step_bytes = sum((u + 1) * expert_bytes for u in used) + n_layers * (E * H * 2 + H * 2)
         gbs = step_bytes / (ms / 1000.0) / 1e9
@@ -858,19 +902,28 @@ def c3_arm(args):
                                      "hbm_gbs": gbs, "roofline_frac": gbs / hbm_peak,
                                      "distinct_experts_per_layer": sum(used) / len(used)}
         del g
+    resident = sum(b.tiled.gate_up.numel() + b.tiled.down.numel() for b in blocks) / 1e9
+    del blocks, routers
+    torch.cuda.empty_cache()
+    return {"metric": "48-layer MoE decode tokens/s (C3)", "value": results["batch64"]["tokens_per_s"],
+            "unit": "tokens/s", "steps": steps,
+            "workload": "C3: 48 layers, H3072/I640/E512 top-10 Q4/G32 + shared, Zipf(1.1) routing; "
+                        "value = batch-64 tokens/s, batch1 below",
+            "resident_tiled_gb": resident, "results": results, "peak": hbm_peak, "peak_kind": peak_kind}
+
+
+def c3_arm(args):
+    r = c3_numbers(args.steps)
     print(json.dumps({
-        "metric": "48-layer MoE decode tokens/s (C3)", "value": results["batch64"]["tokens_per_s"],
-        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": 3, "higher_is_better": True,
-        "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "C3: 48 layers, H3072/I640/E512 top-10 Q4/G32 + shared, Zipf(1.1) routing; "
-                               "value = batch-64 tokens/s, batch1 below",
-                   "resident_tiled_gb": sum(b.tiled.gate_up.numel() + b.tiled.down.numel() for b in blocks) / 1e9},
-        "results": results, "peak": hbm_peak, "peak_kind": peak_kind,
+        "metric": r["metric"], "value": r["value"], "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": 3, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": r["workload"], "resident_tiled_gb": r["resident_tiled_gb"]},
+        "results": r["results"], "peak": r["peak"], "peak_kind": r["peak_kind"],
     }), flush=True)
     return 0
 
 
-def c4_arm(args):
+def c4_numbers(steps_arg: int, warmup: int) -> dict:
     """Config 4: 5,000-token prefill chunk through one H2048/I512/E512 top-10
     Q4/G32 layer (+ shared), uniform routing.  The layer picks the tcgen05
     grouped GEMMs (prefill path); value = TFLOP/s of the expert GEMMs
@@ -895,11 +948,11 @@ def c4_arm(args):
     d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = float(d.get("bf16_tflops", 1590.0))
     peak_kind = "measured burst" if "bf16_tflops" in d else "fallback"
-    steps = max(1, min(args.steps, 10))
+    steps = max(1, min(steps_arg, 10))
     res = {}
     for path in ("prefill", "decode"):
         block = SparseMoEBlock(L.router_weight, L.experts, path=path, **kw)
-        for _ in range(max(3, args.warmup)):
+        for _ in range(max(3, warmup)):
             block(L.x, out=out)
         ms = _timed(lambda i: block(L.x, out=out), steps) / steps
         _lib.profile_enable(True)
@@ -920,18 +973,26 @@ def c4_arm(args):
     gu_tf = gu_flops / (gu_us * 1e-6) / 1e12 if gu_us else None
     ms = res["prefill"]["ms_per_step"]
     tflops = res["prefill"]["tflops"]
+    del L
+    torch.cuda.empty_cache()
+    return {"metric": "prefill MoE layer TFLOP/s (C4)", "value": tflops, "unit": "TFLOP/s", "steps": steps,
+            "ms_per_step": ms,
+            "workload": "C4: 5,000 tokens, H2048/I512/E512 top-10 Q4/G32 + shared, uniform routing",
+            "kernel": "tcgen05 grouped GEMM (M128 N256 K16 bf16, fp32 TMEM accumulators), "
+                      "Q4 dequant to bf16 in registers",
+            "roofline": {"bound": "tensor", "kernel": "prefill gate_up", "achieved": gu_tf, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": (gu_tf / peak) if gu_tf else None,
+                         "useful_flops": gu_flops, "avg_launch_us": gu_us},
+            "down_tflops": dn_flops / (dn_us * 1e-6) / 1e12 if dn_us else None, "paths": res}
+
+
+def c4_arm(args):
+    r = c4_numbers(args.steps, args.warmup)
     print(json.dumps({
-        "metric": "prefill MoE layer TFLOP/s (C4)", "value": tflops, "unit": "TFLOP/s", "n_gpus": 1,
-        "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
-        "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "C4: 5,000 tokens, H2048/I512/E512 top-10 Q4/G32 + shared, uniform routing",
-                   "kernel": "tcgen05 grouped GEMM (M128 N256 K16 bf16, fp32 TMEM accumulators), "
-                             "Q4 dequant to bf16 in registers"},
-        "roofline": {"bound": "tensor", "kernel": "prefill gate_up", "achieved": gu_tf, "peak": peak,
-                     "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": (gu_tf / peak) if gu_tf else None,
-                     "useful_flops": gu_flops, "avg_launch_us": gu_us},
-        "down_tflops": dn_flops / (dn_us * 1e-6) / 1e12 if dn_us else None,
-        "paths": res,
+        "metric": r["metric"], "value": r["value"], "unit": "TFLOP/s", "n_gpus": 1, "steps": r["steps"],
+        "warmup": max(3, args.warmup), "ms_per_step": r["ms_per_step"], "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic", "config": {"workload": r["workload"], "kernel": r["kernel"]},
+        "roofline": r["roofline"], "down_tflops": r["down_tflops"], "paths": r["paths"],
     }), flush=True)
     return 0
 
@@ -947,6 +1008,8 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS, help="distinct layers rotated per step")
     ap.add_argument("--no-batch1", action="store_true", help="skip the batch-1 CUDA-graph sub-measure")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the C3/C4/C5 sub-measures of the default one-GPU line")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return reference_arm(args)
