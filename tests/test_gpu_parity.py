@@ -555,7 +555,7 @@ def test_executor_tiny_and_subnormal_activations_bit_exact(cuda_lib):
 
 @pytest.mark.parametrize("tokens,slots,hidden,inter,experts,group", [
     (1, 10, 2048, 512, 64, 32),   # batch 1 (4-warp row kernel on the reference-layout arrays)
-    (9, 10, 512, 256, 16, 32),    # 16-warp grouped row kernel (>= 64 pairs)
+    (8, 10, 512, 256, 16, 32),    # 16-warp grouped row kernel (>= 64 pairs)
     (3, 3, 256, 128, 6, 64),      # group size 64
 ])
 def test_executor_float32_activations_bit_exact(cuda_lib, tokens, slots, hidden, inter, experts, group):
@@ -576,7 +576,7 @@ def test_executor_float32_activations_bit_exact(cuda_lib, tokens, slots, hidden,
     sy = rng.normal(0, 0.5, (tokens, hidden)).astype(np.float32)
     sh = rng.normal(0, 0.5, (tokens, hidden)).astype(np.float32)
     sgate = rng.uniform(0, 1, (tokens, 1)).astype(np.float32)
-    ex = MoEExecutor(experts, hidden, slots, group_size=group, max_tokens=max(8, tokens))
+    ex = MoEExecutor(experts, hidden, slots, group_size=group)
     nb = _bank_np(bank)
     r = torch.tensor(routes).cuda()
     xn = x.cpu().numpy()
