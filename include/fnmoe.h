@@ -267,6 +267,29 @@ typedef struct FnPagedArgs {
   uint64_t workspace_bytes;
 } FnPagedArgs;
 
+/* Quantized embedding / n-gram row lookup (fnmoe_rows_dequantize).  The
+ * table -- every shard of a sharded table, concatenated in shard order -- is
+ * resident on the device: weight [table_rows][dims * bits / 32] uint32 (value
+ * j of a word in bits [j*bits, (j+1)*bits), MLX affine packing), scales and
+ * biases [table_rows][dims / group_size] bf16.  out[i, k] = bf16(s*q + b),
+ * rounded once, of row r(i): indices[i] when it lies in [0, table_rows),
+ * else shard 0's row clamp(indices[i], 0, first_shard_rows - 1) (the sharded
+ * lookup's clamping, ngram.py:106-119).  count == 0 is a no-op. */
+typedef struct FnRowsArgs {
+  uint32_t abi_version;
+  uint32_t dims;               /* values per row, a multiple of group_size */
+  uint32_t bits;               /* 2, 4 or 8 */
+  uint32_t group_size;         /* 32, 64 or 128 */
+  uint64_t table_rows;         /* rows of the whole (concatenated) table */
+  uint64_t first_shard_rows;   /* rows of shard 0 (table_rows for one table) */
+  uint64_t count;              /* rows to look up */
+  const uint32_t *weight;      /* 8-byte aligned */
+  const void *scales;          /* bf16 */
+  const void *biases;          /* bf16 */
+  const int64_t *indices;      /* [count] device */
+  void *out;                   /* [count, dims] bf16, 16-byte aligned */
+} FnRowsArgs;
+
 /* 1 when an sm_100 device is current and the library initialised, else 0.
  * Replaces flashnext_native_available (metal_runtime_native.mm:196-201). */
 FNMOE_API int fnmoe_available(void);
@@ -382,6 +405,13 @@ FNMOE_API int fnmoe_swiglu(const void *gate, const void *up, void *out, uint64_t
 
 FNMOE_API int fnmoe_paged_decode_workspace_size(const FnPagedArgs *args, uint64_t *bytes);
 FNMOE_API int fnmoe_paged_decode(const FnPagedArgs *args, void *stream);
+
+/* Gather and dequantise table rows (see FnRowsArgs) on `stream`.  Replaces
+ * StreamingQuantizedEmbedding.__call__ (ngram.py:62-69, rows read by
+ * store.rows then mx.dequantize, ngram.py:49-60) and
+ * StreamingShardedEmbedding._direct_rows (ngram.py:160-185); the input
+ * embedding's streamed rows use the same class (loader.py:266-283). */
+FNMOE_API int fnmoe_rows_dequantize(const FnRowsArgs *args, void *stream);
 
 /* ---- Expert-parallel exchange over NVLink peer memory ----
  * No reference counterpart: the reference runs on one device.  One process

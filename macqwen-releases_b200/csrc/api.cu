@@ -17,6 +17,7 @@
 
 #include "../../include/fnmoe.h"
 #include "attention.cuh"
+#include "rows.cuh"
 #include "common.cuh"
 #include "moe_kernels.cuh"
 
@@ -982,6 +983,10 @@ int fnmoe_paged_decode_workspace_size(const FnPagedArgs *args, uint64_t *bytes) 
 
 int fnmoe_paged_decode(const FnPagedArgs *args, void *stream) {
   return paged_decode(args, static_cast<cudaStream_t>(stream), g_last_error);
+}
+
+int fnmoe_rows_dequantize(const FnRowsArgs *args, void *stream) {
+  return rows_dequant(args, static_cast<cudaStream_t>(stream), g_last_error);
 }
 
 int fnmoe_tiled_record_bytes(uint32_t hidden_size, uint32_t inter_size, uint32_t group_size,

@@ -132,6 +132,14 @@ class FnPagedArgs(ctypes.Structure):
     ]
 
 
+class FnRowsArgs(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", _u32), ("dims", _u32), ("bits", _u32), ("group_size", _u32),
+        ("table_rows", _u64), ("first_shard_rows", _u64), ("count", _u64),
+        ("weight", _vp), ("scales", _vp), ("biases", _vp), ("indices", _vp), ("out", _vp),
+    ]
+
+
 EP_IPC_BYTES = 64
 
 
@@ -173,6 +181,7 @@ SIGNATURES = {
     "fnmoe_swiglu": ([_vp, _vp, _vp, _u64, _vp], ctypes.c_int),
     "fnmoe_paged_decode_workspace_size": ([ctypes.POINTER(FnPagedArgs), ctypes.POINTER(_u64)], ctypes.c_int),
     "fnmoe_paged_decode": ([ctypes.POINTER(FnPagedArgs), _vp], ctypes.c_int),
+    "fnmoe_rows_dequantize": ([ctypes.POINTER(FnRowsArgs), _vp], ctypes.c_int),
     "fnmoe_read_device_errors": ([ctypes.POINTER(_u32), ctypes.c_int], ctypes.c_int),
     "fnmoe_profile_enable": ([ctypes.c_int], ctypes.c_int),
     "fnmoe_ep_create": ([ctypes.POINTER(FnEpConfig), ctypes.POINTER(_vp)], ctypes.c_int),

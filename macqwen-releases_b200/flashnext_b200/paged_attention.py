@@ -4,10 +4,11 @@ Replaces the decode branch (L == 1) of ``paged_attention(queries, cache,
 scale, mask)`` (``models/qwen27b/paged_kv.py:417-495``): per-page partial
 softmax statistics in float32 merged online, output ``o / l`` in the query
 dtype.  Here the cache is HBM-resident pages addressed through a block table
-(the layout of ``BASELINE`` config 5: bfloat16 K/V pages of ``page_size``
-tokens, ``[pages, page_size, kv_heads, head_dim]``), and the merge is a
-split-K flash decode: warps own ``split_tokens`` contiguous tokens, a second
-kernel merges the splits of a sequence in order.
+(bfloat16 K/V pages of ``page_size`` tokens, ``[pages, page_size, kv_heads,
+head_dim]``), and the merge is a split-K flash decode: one CTA streams the
+K/V rows of ``split_tokens`` contiguous tokens of one (sequence, kv head)
+through a TMA ring into tensor-core MMAs, a second kernel merges the splits
+of a sequence.
 """
 from __future__ import annotations
 
@@ -25,9 +26,24 @@ def _torch():
     return torch
 
 
+def auto_split(batch: int, kv_heads: int, capacity_tokens: int, sms: int = 148) -> int:
+    """Tokens per split-K chunk: the longest power of two in [64, 2048]
+    whose (sequence, kv head, split) work items -- counted at full capacity
+    -- still give every SM three CTAs (1.5 waves of the two resident per
+    SM).  Longer splits mean fewer CTA start-ups and partials to merge;
+    enough items keep every SM streaming."""
+    split = 2048
+    while split > 64 and batch * kv_heads * -(-capacity_tokens // split) < 3 * sms:
+        split //= 2
+    return split
+
+
 def paged_decode(q, k_cache, v_cache, block_table, context_lens, scale: float,
-                 split_tokens: int = 256, out=None, workspace=None):
-    """q [B, Hq, D] bf16 -> out [B, Hq, D] bf16 (one query token per sequence)."""
+                 split_tokens: int | None = None, out=None, workspace=None):
+    """q [B, Hq, D] bf16 -> out [B, Hq, D] bf16 (one query token per sequence).
+
+    ``split_tokens`` defaults to :func:`auto_split` of the batch, kv heads
+    and block-table capacity."""
     torch = _torch()
     lib = _lib.ensure_device()
     qt = _bf16(q, "q")
@@ -48,6 +64,9 @@ def paged_decode(q, k_cache, v_cache, block_table, context_lens, scale: float,
     a.batch, a.q_heads, a.kv_heads, a.head_dim = batch, q_heads, kv_heads, head_dim
     a.page_size, a.max_pages, a.num_pages = page_size, int(bt.shape[1]), num_pages
     a.scale = float(scale)
+    if split_tokens is None:
+        split_tokens = auto_split(batch, kv_heads, int(bt.shape[1]) * page_size,
+                                  torch.cuda.get_device_properties(qt.device).multi_processor_count)
     a.split_tokens = int(split_tokens)
     a.q, a.k_cache, a.v_cache = qt.data_ptr(), kt.data_ptr(), vt.data_ptr()
     a.block_table, a.context_lens = bt.data_ptr(), cl.data_ptr()

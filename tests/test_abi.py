@@ -92,6 +92,8 @@ int main(void) {
          offsetof(FnTileArgs, tiled));
   printf("LayerTiled %zu\n", offsetof(FnMoELayerArgs, tiled));
   printf("LayerKeep %zu %zu\n", offsetof(FnMoELayerArgs, keep_threshold), offsetof(FnMoELayerArgs, min_keep));
+  printf("FnRowsArgs %zu %zu %zu\n", sizeof(FnRowsArgs), offsetof(FnRowsArgs, table_rows),
+         offsetof(FnRowsArgs, weight));
   return 0;
 }
 """
@@ -121,6 +123,30 @@ def test_struct_layout_matches_c_compiler(tmp_path):
     assert int(lines["LayerTiled"]) == _lib.FnMoELayerArgs.tiled.offset
     got = [int(v) for v in lines["LayerKeep"].split()]
     assert got == [_lib.FnMoELayerArgs.keep_threshold.offset, _lib.FnMoELayerArgs.min_keep.offset]
+    got = [int(v) for v in lines["FnRowsArgs"].split()]
+    assert got == [s(_lib.FnRowsArgs), _lib.FnRowsArgs.table_rows.offset, _lib.FnRowsArgs.weight.offset]
+
+
+def test_rows_dequantize_validates_before_any_device_call():
+    """Argument checks of the row lookup run on the host: a bad bit width,
+    group size, shape or alignment is an error code, never a launch."""
+    lib = _lib.load()
+    a = _lib.FnRowsArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.dims, a.bits, a.group_size = 256, 4, 32
+    a.table_rows, a.first_shard_rows, a.count = 10, 10, 3
+    a.weight, a.scales, a.biases, a.indices, a.out = 0x1000, 0x2000, 0x3000, 0x4000, 0x5000
+    for field, value, code in (("bits", 3, _lib.ERR_UNSUPPORTED), ("group_size", 16, _lib.ERR_UNSUPPORTED),
+                               ("dims", 48, _lib.ERR_SHAPE), ("first_shard_rows", 11, _lib.ERR_SHAPE),
+                               ("out", 0x5008, _lib.ERR_VALUE), ("indices", None, _lib.ERR_NULL)):
+        b = _lib.FnRowsArgs.from_buffer_copy(a)
+        setattr(b, field, value)
+        assert lib.fnmoe_rows_dequantize(ctypes.byref(b), None) == code, field
+    b = _lib.FnRowsArgs.from_buffer_copy(a)
+    b.count = 0
+    assert lib.fnmoe_rows_dequantize(ctypes.byref(b), None) == _lib.OK  # nothing to do
+    b.abi_version = 3
+    assert lib.fnmoe_rows_dequantize(ctypes.byref(b), None) == _lib.ERR_ABI
 
 
 def test_tiled_record_bytes_without_gpu():

@@ -128,6 +128,24 @@ def test_c5_split_sizes_agree(cuda_lib, split):
     _check_attention(_np(out), P)
 
 
+@pytest.mark.parametrize("batch,hq,hkv,d,page,ctx,split", [
+    (5, 6, 2, 128, 48, (1, 200), 80),     # 3 query heads per kv head, page 48, splits not a stage multiple
+    (3, 8, 1, 256, 16, (31, 33), 16),     # stages partly filled at both ends of a split
+    (2, 16, 2, 256, 64, (4096, 4096), 4096),  # one split per sequence, every stage full
+    (6, 4, 4, 64, 32, (1, 3000), 256),
+])
+def test_paged_decode_ring_edges(cuda_lib, batch, hq, hkv, d, page, ctx, split):
+    """Geometry edges of the staged ring: grouped-query widths below 8, page
+    sizes that do not divide a stage, splits shorter than a stage or not a
+    multiple of it, one-token contexts and contexts that end a stage
+    exactly."""
+    from flashnext_b200 import synthetic
+    from flashnext_b200.paged_attention import paged_decode
+    P = synthetic.paged_decode_inputs(batch, hq, hkv, d, page, ctx, seed=batch * 31 + page)
+    out = paged_decode(P.q, P.k_cache, P.v_cache, P.block_table, P.context_lens, P.scale, split_tokens=split)
+    _check_attention(_np(out), P)
+
+
 def test_paged_attention_api_with_cache_append(cuda_lib):
     """paged_attention(queries, cache, scale) over a PagedKVCache filled by
     append() in uneven pieces (page-crossing appends, three sequences of
