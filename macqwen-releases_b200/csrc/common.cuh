@@ -85,6 +85,24 @@ __device__ __forceinline__ float swiglu_bf16(const uint16_t *tab, float g, float
   return bmul(bmul(g, sigmoid_bf16(tab, g)), u);
 }
 
+// The same two sequences with exp computed in registers instead of read from
+// the table: the table holds exactly f64_to_bf16_once(exp(double(v))) for
+// every bfloat16 v, so the bits are identical; used where a table lookup (an
+// L2 round trip) would sit on a latency-critical path.
+__device__ __forceinline__ float exp_bf16_direct(float v) {
+  return bf16_to_f32(f64_to_bf16_once(exp(static_cast<double>(round_bf16(v)))));
+}
+__device__ __forceinline__ float sigmoid_bf16_direct(float g) {
+  const float mag = fabsf(g);
+  const float ex = exp_bf16_direct(mag);
+  const float den = badd(1.0f, ex);
+  const float small = bdiv(1.0f, den);
+  return (g < 0.0f) ? small : bsub(1.0f, small);
+}
+__device__ __forceinline__ float swiglu_bf16_direct(float g, float u) {
+  return bmul(bmul(g, sigmoid_bf16_direct(g)), u);
+}
+
 // The same sequence with float32 activations (the reference's kernel with
 // T = float): every op rounded to float32, exp correctly rounded (float64
 // exp, one rounding).

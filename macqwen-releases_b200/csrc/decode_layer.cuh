@@ -39,12 +39,18 @@ constexpr int kFusedThreads = 512;
 constexpr int kFusedWarps = kFusedThreads / 32;
 constexpr int kFusedMaxSlots = 16;              // gate/up items per CTA
 constexpr int kFusedRowsPerGroup = 5;           // activation rows per fixed-point thread group (I <= 1024)
-constexpr uint32_t kGridSpinLimit = 1u << 22;   // barrier polls (with a 64 ns back-off): ~0.3-0.5 s
+constexpr uint32_t kGridSpinLimit = 1u << 24;   // barrier polls (one L2 round trip each): ~1-2 s
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+__device__ __forceinline__ uint32_t atom_add_release_gpu(uint32_t *p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;\n" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
 // Grid barrier over co-resident CTAs (one call per CTA per barrier).  The
@@ -53,15 +59,17 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
 // 2^31 and each CTA waits until the top bit differs from the value its own
 // add returned.  The low 31 bits are back to zero after every complete
 // barrier, so a counter that starts at zero needs no reset between launches.
-// Writes before the barrier are visible to L2-coherent (ld.cg / acquire)
-// reads after it.  Returns false (and flags kErrTimeout) if it gave up; the
+// Ordering: the CTA barrier orders the CTA's writes before thread 0's
+// release add; a waiter's acquire load that sees the flip, then its CTA
+// barrier, orders them before every later read of its CTA (L2-coherent:
+// ld.cg / acquire).  The spin has no back-off: the wake-up latency is one
+// L2 round trip.  Returns false (and flags kErrTimeout) if it gave up; the
 // counter is then left mid-barrier (fnmoe_read_device_errors clears it).
 __device__ __forceinline__ bool grid_sync(uint32_t *bar, uint32_t *err, int *s_flag) {
   __syncthreads();
   if (threadIdx.x == 0) {
     const uint32_t inc = blockIdx.x == 0 ? 0x80000000u - (gridDim.x - 1u) : 1u;
-    __threadfence();
-    const uint32_t old = atomicAdd(bar, inc);
+    const uint32_t old = atom_add_release_gpu(bar, inc);
     int ok = 1;
     uint32_t spins = 0;
     while (((old ^ ld_acquire_gpu(bar)) & 0x80000000u) == 0u) {
@@ -70,9 +78,7 @@ __device__ __forceinline__ bool grid_sync(uint32_t *bar, uint32_t *err, int *s_f
         set_error(err, kErrTimeout);
         break;
       }
-      __nanosleep(32);
     }
-    __threadfence();
     *s_flag = ok;
   }
   __syncthreads();
@@ -463,8 +469,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_layer(FusedLayer p,
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xFFFFFFFFu, lmax, off));
   if (lane == 0) s_red[warp] = lmax;
-  if (warp == 1 && lane == 0)
-    s_sg = has_sh ? sigmoid_bf16(g_exp_bf16, bf16_to_f32(__ldcg(p.shared_logit))) : 0.0f;
   __syncthreads();
   float M = s_red[0];
 #pragma unroll
@@ -549,10 +553,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_layer(FusedLayer p,
     }
     if (lane == 0) {
       s_keep = keep;
-      if (cta == 0) {
-        p.mass[0] = f32_to_bf16(topm);
-        if (has_sh) p.shared_gate[0] = f32_to_bf16(s_sg);
-      }
+      if (cta == 0) p.mass[0] = f32_to_bf16(topm);
     }
   }
   __syncthreads();
@@ -570,6 +571,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_layer(FusedLayer p,
     if (lane == 0) s_armed |= armed;
   } else if (warp == 1) {
     if (has_dg && !p.alias) issue_down(cta, n_units);
+    // the shared expert's sigmoid gate, needed only by the combine: its
+    // loads overlap the expert data's arrival instead of the routing
+    if (lane == 0) {
+      s_sg = has_sh ? sigmoid_bf16_direct(bf16_to_f32(__ldcg(p.shared_logit))) : 0.0f;
+      if (cta == 0 && has_sh) p.shared_gate[0] = f32_to_bf16(s_sg);
+    }
   } else if (warp == 2) {
     // down rows of this CTA's row groups that are not staged yet: into L2
     const int first = p.alias ? cta : cta + NB;
@@ -616,7 +623,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_layer(FusedLayer p,
     const int q = j / n_rg, rg = j - q * n_rg;
     uint32_t mag = 0u;
     if (live && mrow < 8) {
-      const uint16_t a = f32_to_bf16(swiglu_bf16(g_exp_bf16, y, other));
+      const uint16_t a = f32_to_bf16(swiglu_bf16_direct(y, other));
       p.act[static_cast<size_t>(unit_row(q)) * I + rg * 8 + mrow] = a;
       mag = a & 0x7FFFu;
       if (mag >= 0x7F80u) {
