@@ -652,6 +652,8 @@ struct LayerLayout {
   int *ghist;          // prefill: per-chunk bin counts of the multi-CTA grouping
   uint64_t ghist_bytes;
   uint32_t *amax;      // batch-1 persistent kernel: activation row maxima
+  RouterScratch rs;    // many-token router: fixed-point byte planes
+  bool has_rs = false;
 };
 
 // Carves the layer workspace from `base` (null: a size probe).  Returns the
@@ -682,6 +684,18 @@ uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL, uint6
   LL.ghist_bytes = layer_prefill(a) ? static_cast<uint64_t>((n_total + 4095) / 4096) * n_bins * sizeof(int) : 0;
   LL.ghist = LL.ghist_bytes ? cv.take<int>(LL.ghist_bytes / sizeof(int)) : nullptr;
   LL.amax = cv.take<uint32_t>(32);
+  {
+    // many-token router: byte planes of the fixed points and row exponents
+    const int R = E + (shared ? 1 : 0);
+    if (router_scratch_bytes(T, R, a->hidden_size) > 0) {
+      const uint64_t TH = static_cast<uint64_t>(T) * a->hidden_size;
+      LL.rs.xq = cv.take<uint8_t>(3 * TH);
+      LL.rs.wq = cv.take<uint8_t>(2ull * R * a->hidden_size);
+      LL.rs.ex = cv.take<int32_t>(T);
+      LL.rs.ew = cv.take<int32_t>(R);
+      LL.has_rs = true;
+    }
+  }
   if (used != nullptr) *used = cv.used();
   return cv.off + kWorkspaceSlack;
 }
@@ -803,7 +817,7 @@ int fnmoe_moe_layer(const FnMoELayerArgs *a, void *stream) {
     e = launch_router_logits(static_cast<const uint16_t *>(a->x), static_cast<const uint16_t *>(a->router_weight),
                              T, H, E, shared ? static_cast<const uint16_t *>(a->shared_expert_gate) : nullptr,
                              logits, LL.shared_logit, s, prefill ? nullptr : L.xl, prefill ? nullptr : L.xm, G,
-                             &prep_done);
+                             &prep_done, LL.has_rs ? &LL.rs : nullptr);
   }
   if (e != cudaSuccess) return cuda_fail(e, "router logits");
   if (!prefill && !prep_done) {

@@ -15,7 +15,8 @@
 //
 //  A  row fixed point of x (shared memory), bulk copies of this CTA's
 //     shared-expert gate/up row groups (routing-independent), the router
-//     GEMV rows of this CTA (one row per warp, the canonical 32-lane chain),
+//     GEMV rows of this CTA (one row per warp, the exact integer dot product
+//     of the row fixed points),
 //     logits to global.                                          barrier 1
 //  B  softmax / top-k / keep / renorm of the 512 logits, recomputed by
 //     every CTA (identical arithmetic, so identical results -- no third
@@ -431,7 +432,25 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_layer(FusedLayer p,
     else
       fixed_point_group<G, 2>(xs, false, H, tr, 256, reinterpret_cast<uint16_t *>(xl), xm, err, 1, s_mx[0]);
   } else if (router_warp) {
-    float a = -0.0f;
+    // exact integer dot product of the row fixed points (k_router_logits'
+    // arithmetic): exponents of the router row and of x from warp maxima
+    bool bad = false;
+    uint32_t mw = 0, mxx = 0;
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      const int cidx = lane + 32 * m;
+      if (cidx < nchunks) {
+        mw = max(mw, max_mag8(wv[m], bad));
+        mxx = max(mxx, max_mag8(reinterpret_cast<const uint4 *>(xs)[cidx], bad));
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      mw = max(mw, __shfl_xor_sync(0xFFFFFFFFu, mw, off));
+      mxx = max(mxx, __shfl_xor_sync(0xFFFFFFFFu, mxx, off));
+    }
+    const int ew = row_exponent(mw), ex = row_exponent(mxx);
+    long long a = 0;
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
       const int cidx = lane + 32 * m;
@@ -440,17 +459,19 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_layer(FusedLayer p,
         const uint32_t wu[4] = {wv[m].x, wv[m].y, wv[m].z, wv[m].w};
         const uint32_t xu[4] = {xv4.x, xv4.y, xv4.z, xv4.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          a = __fmaf_rn(__uint_as_float(wu[i] << 16), __uint_as_float(xu[i] << 16), a);
-          a = __fmaf_rn(__uint_as_float(wu[i] & 0xFFFF0000u), __uint_as_float(xu[i] & 0xFFFF0000u), a);
+        for (int i = 0; i < 8; ++i) {
+          const int wq = fixed_q((wu[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, ew, kRouterWBits);
+          const int xq = fixed_q((xu[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, ex, kRouterXBits);
+          a += static_cast<long long>(wq) * xq;
         }
       }
     }
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xFFFFFFFFu, a, off));
+    for (int off = 16; off >= 1; off >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, off);
     if (lane == 0) {
-      if (row < E) p.logits[row] = f32_to_bf16(a);
-      else p.shared_logit[0] = f32_to_bf16(a);
+      const uint16_t bits = router_logit_bits(a, ex, ew);
+      if (row < E) p.logits[row] = bits;
+      else p.shared_logit[0] = bits;
     }
   }
   if (!grid_sync(p.bar, err, &s_flag)) {

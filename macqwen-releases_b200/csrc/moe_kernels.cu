@@ -144,6 +144,43 @@ __device__ __forceinline__ int fixed_x(uint32_t h, int E) {
   return (h & 0x8000u) ? -static_cast<int>(mag) : static_cast<int>(mag);
 }
 
+// Router fixed points (see k_router_prep): token rows keep 22 fraction bits
+// below the row's top exponent, router rows 14; a logit is the exact integer
+// dot product scaled by 2^(Ex - 22 + Ew - 14), rounded once to bfloat16.
+constexpr int kRouterXBits = 22, kRouterWBits = 14;
+
+// floor(log2) of a row's largest finite magnitude from its bfloat16
+// magnitude bits (magnitudes order like their bit patterns); 0 for a zero row.
+__device__ __forceinline__ int row_exponent(uint32_t mx) {
+  if (mx == 0) return 0;
+  return (mx >> 7) ? static_cast<int>(mx >> 7) - 127 : (31 - __clz(static_cast<int>(mx))) - 133;
+}
+// trunc(h * 2^(bits - E)) of one bfloat16 input; fixed_x is bits = 22.
+__device__ __forceinline__ int fixed_q(uint32_t h, int E, int bits) {
+  const uint32_t ef = (h >> 7) & 0xFFu, mf = h & 0x7Fu;
+  if ((h & 0x7FFFu) == 0 || ef == 255u) return 0;
+  const uint32_t M = ef ? (mf | 0x80u) : mf;
+  const int sh = ef ? (static_cast<int>(ef) - 134 + bits - E) : (-133 + bits - E);
+  const uint32_t mag = sh >= 0 ? (M << sh) : ((-sh >= 31) ? 0u : (M >> (-sh)));
+  return (h & 0x8000u) ? -static_cast<int>(mag) : static_cast<int>(mag);
+}
+// Largest finite magnitude bits of 8 bfloat16 values; `bad` when one is not finite.
+__device__ __forceinline__ uint32_t max_mag8(const uint4 v, bool &bad) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t mx = 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const uint32_t a = (w[e >> 1] >> (16 * (e & 1))) & 0x7FFFu;
+    if (a >= 0x7F80u) bad = true;
+    else mx = max(mx, a);
+  }
+  return mx;
+}
+// Router logit bits from the exact dot product S of the fixed points.
+__device__ __forceinline__ uint16_t router_logit_bits(long long S, int ex, int ew) {
+  return f64_to_bf16_once(ldexp(static_cast<double>(S), ex + ew - kRouterXBits - kRouterWBits));
+}
+
 // The same for one float32 input (bits), E the row exponent.
 __device__ __forceinline__ int fixed_x32(uint32_t bits, int E) {
   const uint32_t ef = (bits >> 23) & 0xFFu, mf = bits & 0x7FFFFFu;
@@ -2028,15 +2065,17 @@ cudaError_t launch_combine_f32(const float *d, const uint32_t *routes, const voi
 // ---------------------------------------------------------------------------
 
 
-// Grid (row groups, token blocks).  Each warp keeps kRouterRW router rows in
-// registers (RW = 2 up to hidden 3072, else 1) for blocks of kRouterTok tokens.
-// Each warp keeps kRouterRW router rows in
-// registers (lane j owns 8-element chunks j, j+32, ... of each) and runs the
-// canonical per-lane chain for every (row, token) of the block, reading each
-// staged input element once for both rows; then the xor butterfly.
+// Router logits as exact integer dot products (GEMV form).  Grid (row
+// groups, token blocks).  Each warp keeps kRouterRW router rows in registers
+// as their 14-bit fixed points (row exponent from a warp reduction; lane j
+// owns 8-element chunks j, j+32, ...); the CTA stages its token block as
+// 22-bit fixed points in shared memory (token exponents from shared-memory
+// maxima).  Every (row, token) sum is an exact int64 over the lane's
+// elements plus an xor butterfly -- exact in any order -- scaled and rounded
+// once to bfloat16 (router_logit_bits): the same bits as the tensor-core path.
 // With prep_limbs set, CTAs from router_ctas on (one per token row, blockDim
-// threads per row) compute the row fixed point of x instead (prep_rows_body),
-// which saves small batches a launch.
+// threads per row) compute the projection's row fixed point of x instead
+// (prep_rows_body), which saves small batches a launch.
 template <int CH, int kRouterRW, int kRouterTok, int kRouterWarps>
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
     const uint16_t *x, const uint16_t *__restrict__ W, int T, int H, int E,
@@ -2052,57 +2091,73 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
     else prep_rows_body<64, SPT>(x, T, H, blockDim.x, prep_limbs, prep_meta, err, block);
     return;
   }
-  extern __shared__ __align__(16) float xs[];  // [kRouterTok][H] float32
+  extern __shared__ __align__(16) int xq[];  // [kRouterTok][H] token fixed points
+  __shared__ uint32_t s_mx[kRouterTok];
+  __shared__ int s_ex[kRouterTok];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = (blockIdx.x * kRouterWarps + warp) * kRouterRW;
   const int rows = E + (wsg != nullptr ? 1 : 0);
   const int nchunks = H / 8;
   const int t0 = blockIdx.y * kRouterTok;
   const int tb = min(kRouterTok, T - t0);
-  float w[kRouterRW][CH * 8];
+  int w[kRouterRW][CH * 8];
+  int ew[kRouterRW];
   bool live[kRouterRW];
+  bool bad = false;
 #pragma unroll
   for (int q = 0; q < kRouterRW; ++q) {
     const int row = row0 + q;
     const uint16_t *wrow = row < E ? W + static_cast<size_t>(row) * H : (row < rows ? wsg : nullptr);
     live[q] = wrow != nullptr;
+    uint4 wv[CH];
+    uint32_t mx = 0;
 #pragma unroll
     for (int m = 0; m < CH; ++m) {
       const int cidx = lane + 32 * m;
-      if (wrow != nullptr && cidx < nchunks) {
-        const uint4 v = ldg_u128(reinterpret_cast<const uint4 *>(wrow + cidx * 8));
-        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+      wv[m] = (wrow != nullptr && cidx < nchunks) ? ldg_u128(reinterpret_cast<const uint4 *>(wrow + cidx * 8))
+                                                  : make_uint4(0u, 0u, 0u, 0u);
+      mx = max(mx, max_mag8(wv[m], bad));
+    }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          w[q][m * 8 + 2 * i] = __uint_as_float(u[i] << 16);
-          w[q][m * 8 + 2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
-        }
-      } else {
+    for (int off = 16; off >= 1; off >>= 1) mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+    ew[q] = row_exponent(mx);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) w[q][m * 8 + i] = 0.0f;
-      }
+    for (int m = 0; m < CH; ++m) {
+      const uint32_t u[4] = {wv[m].x, wv[m].y, wv[m].z, wv[m].w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[q][m * 8 + i] = fixed_q((u[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, ew[q], kRouterWBits);
     }
   }
   // the router rows are constant: their loads above overlap the previous kernel
   pdl_wait();
   pdl_trigger();
-  // stage the token block as float32 (8 bf16 per 16-byte load)
+  // token block: exponents from the rows' largest magnitudes, then fixed points
+  if (threadIdx.x < kRouterTok) s_mx[threadIdx.x] = 0u;
+  __syncthreads();
   const uint4 *xsrc = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t0) * H);
-  float4 *xdst = reinterpret_cast<float4 *>(xs);
+  for (int idx = threadIdx.x; idx < tb * nchunks; idx += blockDim.x)
+    atomicMax(&s_mx[idx / nchunks], max_mag8(xsrc[idx], bad));
+  __syncthreads();
+  if (threadIdx.x < tb) s_ex[threadIdx.x] = row_exponent(s_mx[threadIdx.x]);
+  __syncthreads();
   for (int idx = threadIdx.x; idx < tb * nchunks; idx += blockDim.x) {
     const uint4 v = xsrc[idx];
-    xdst[2 * idx] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
-                                __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
-    xdst[2 * idx + 1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
-                                    __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
+    const int ex = s_ex[idx / nchunks];
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    int q8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q8[i] = fixed_q((u[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, ex, kRouterXBits);
+    reinterpret_cast<int4 *>(xq)[2 * idx] = make_int4(q8[0], q8[1], q8[2], q8[3]);
+    reinterpret_cast<int4 *>(xq)[2 * idx + 1] = make_int4(q8[4], q8[5], q8[6], q8[7]);
   }
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) set_error(err, kErrNonFinite);
   __syncthreads();
   if (!live[0]) return;
-  float acc[kRouterRW][kRouterTok];
+  long long acc[kRouterRW][kRouterTok];
 #pragma unroll
   for (int q = 0; q < kRouterRW; ++q)
 #pragma unroll
-    for (int tt = 0; tt < kRouterTok; ++tt) acc[q][tt] = -0.0f;
+    for (int tt = 0; tt < kRouterTok; ++tt) acc[q][tt] = 0;
 #pragma unroll
   for (int m = 0; m < CH; ++m) {
     const int cidx = lane + 32 * m;
@@ -2110,145 +2165,218 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
 #pragma unroll
       for (int tt = 0; tt < kRouterTok; ++tt) {
         // rows past tb hold stale data; their results are never stored
-        const float4 *xp = reinterpret_cast<const float4 *>(xs + tt * H + cidx * 8);
-        const float4 p0 = xp[0], p1 = xp[1];
-        const float xv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const int4 *xp = reinterpret_cast<const int4 *>(xq + tt * H + cidx * 8);
+        const int4 p0 = xp[0], p1 = xp[1];
+        const int xv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
         for (int q = 0; q < kRouterRW; ++q) {
-          float a = acc[q][tt];
+          long long a = acc[q][tt];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) a = __fmaf_rn(w[q][m * 8 + i], xv[i], a);
+          for (int i = 0; i < 8; ++i) a += static_cast<long long>(w[q][m * 8 + i]) * xv[i];
           acc[q][tt] = a;
         }
       }
     }
   }
 #pragma unroll
-  for (int q = 0; q < kRouterRW; ++q) {
+  for (int q = 0; q < kRouterRW; ++q)
 #pragma unroll
-    for (int tt = 0; tt < kRouterTok; ++tt) {
+    for (int tt = 0; tt < kRouterTok; ++tt)
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1)
-        acc[q][tt] = __fadd_rn(acc[q][tt], __shfl_xor_sync(0xFFFFFFFFu, acc[q][tt], off));
-    }
-  }
+      for (int off = 16; off >= 1; off >>= 1) acc[q][tt] += __shfl_xor_sync(0xFFFFFFFFu, acc[q][tt], off);
 #pragma unroll
   for (int q = 0; q < kRouterRW; ++q) {
     const int row = row0 + q;
     if (!live[q] || lane >= tb) continue;
-    float v = acc[q][0];
+    long long v = acc[q][0];
 #pragma unroll
     for (int tt = 1; tt < kRouterTok; ++tt)
       if (lane == tt) v = acc[q][tt];
-    if (row < E) logits[static_cast<size_t>(t0 + lane) * E + row] = f32_to_bf16(v);
-    else shared_logit[t0 + lane] = f32_to_bf16(v);
+    const uint16_t bits = router_logit_bits(v, s_ex[lane], ew[q]);
+    if (row < E) logits[static_cast<size_t>(t0 + lane) * E + row] = bits;
+    else shared_logit[t0 + lane] = bits;
   }
 }
 
-// Router logits for many tokens: a CTA tile of RC (32 or 16) router rows x 16
-// tokens, H streamed in 256-wide rounds through double-buffered bf16 shared
-// memory (cp.async, coherent L2 loads).  Each warp owns 8 rows x 8 tokens
-// (RC/8 warps per 8-token half); lane j runs the canonical chains of those
-// 8 x 8 (row, token) pairs -- chunk 32*round + j, elements in increasing h,
-// from -0.0 -- then the same xor butterfly as k_router_logits, so logits are
-// bit-identical.
-constexpr int kRtTok = 16, kRtRound = 256;
+// Router logits for many tokens on integer tensor cores.
+//
+// k_router_prep: one warp per row -- every token row (22 fraction bits) and
+// every router row (14 bits; row E is the shared gate) -- finds the row
+// exponent and writes the fixed point as byte planes: token X = X0 + 2^8 X1 +
+// 2^16 X2 (X0, X1 unsigned, X2 signed: |X| < 2^23), router W = W0 + 2^8 W1
+// (W0 unsigned, W1 signed: |W| < 2^15).
+//
+// k_router_mma: CTA tile 64 tokens x 64 router rows, 8 warps of 16 tokens x
+// 32 rows; K in 128-byte chunks through a double-buffered cp.async ring
+// (rows padded to 144 bytes: the eight rows of an ldmatrix phase fall in
+// distinct bank groups).  Per 32-byte k-step a warp loads its A fragments
+// (three token planes) and B fragments (two router planes) with ldmatrix and
+// issues mma.sync.m16n8k32 with s32 accumulation for the six limb pairs,
+// summed per power of two (2^0, 2^8, 2^16, 2^24: every partial sum stays
+// below 2^31 for H <= 8192).  The epilogue forms the exact int64 dot
+// product, scales it by 2^(Ex - 22 + Ew - 14) and rounds once to bfloat16:
+// the GEMV kernels' bits.
+constexpr int kRmTok = 64, kRmRows = 64, kRmK = 128, kRmPitch = kRmK + 16;
+constexpr int kRmStage = (3 * kRmTok + 2 * kRmRows) * kRmPitch;  // bytes per ring stage
+constexpr int kRmSmem = 2 * kRmStage;
 
-__device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float (&f)[8]) {
-  f[0] = __uint_as_float(u.x << 16);
-  f[1] = __uint_as_float(u.x & 0xFFFF0000u);
-  f[2] = __uint_as_float(u.y << 16);
-  f[3] = __uint_as_float(u.y & 0xFFFF0000u);
-  f[4] = __uint_as_float(u.z << 16);
-  f[5] = __uint_as_float(u.z & 0xFFFF0000u);
-  f[6] = __uint_as_float(u.w << 16);
-  f[7] = __uint_as_float(u.w & 0xFFFF0000u);
-}
-
-template <int RC, int WT>
-__global__ void __launch_bounds__(RC / 8 * (kRtTok / WT) * 32) k_router_tiled(const uint16_t *x, const uint16_t *__restrict__ W,
-                                                                            int T, int H, int E,
-                                                                            const uint16_t *__restrict__ wsg,
-                                                                            uint16_t *logits, uint16_t *shared_logit) {
-  constexpr int kRtRows = RC, kRowWarps = RC / 8, kThreads = kRowWarps * (kRtTok / WT) * 32;
-  __shared__ __align__(16) uint16_t sw[2][kRtRows][kRtRound];
-  __shared__ __align__(16) uint16_t sx[2][kRtTok][kRtRound];
+__global__ void __launch_bounds__(256) k_router_prep(const uint16_t *x, int T, const uint16_t *__restrict__ W,
+                                                     const uint16_t *__restrict__ wsg, int E, int H,
+                                                     RouterScratch rs, uint32_t *err) {
   pdl_wait();
   pdl_trigger();
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int rows = E + (wsg != nullptr ? 1 : 0);
-  const int r0 = blockIdx.x * kRtRows, t0 = blockIdx.y * kRtTok;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int R = E + (wsg != nullptr ? 1 : 0);
+  if (warp >= T + R) return;
+  const bool tok = warp < T;
+  const int row = tok ? warp : warp - T;
+  const uint16_t *src = tok ? x + static_cast<size_t>(row) * H : (row < E ? W + static_cast<size_t>(row) * H : wsg);
   const int nchunks = H / 8;
-  const int nrounds = (nchunks + 31) / 32;
-  const int wr = 8 * (warp % kRowWarps), wt = WT * (warp / kRowWarps);
-  auto stage = [&](int m, int b) {
-    // RC rows x 32 chunks of W and 16 tokens x 32 chunks of x, 16 bytes each
-    for (int i = tid; i < (kRtRows + kRtTok) * 32; i += kThreads) {
-      const int rr = i >> 5, c = i & 31;
-      const int h = (32 * m + c) * 8;
-      const uint16_t *src = nullptr;
-      uint16_t *dst;
-      if (rr < kRtRows) {
-        const int row = r0 + rr;
-        src = row < E ? W + static_cast<size_t>(row) * H : (row < rows ? wsg : nullptr);
-        dst = &sw[b][rr][c * 8];
+  bool bad = false;
+  uint32_t mx = 0;
+  for (int c = lane; c < nchunks; c += 32) mx = max(mx, max_mag8(reinterpret_cast<const uint4 *>(src)[c], bad));
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) set_error(err, kErrNonFinite);
+  const int ex = row_exponent(mx);
+  const int bits = tok ? kRouterXBits : kRouterWBits;
+  const size_t plane = tok ? static_cast<size_t>(T) * H : static_cast<size_t>(R) * H;
+  uint8_t *dst = (tok ? rs.xq : rs.wq) + static_cast<size_t>(row) * H;
+  for (int c = lane; c < nchunks; c += 32) {
+    const uint4 v = reinterpret_cast<const uint4 *>(src)[c];
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    uint32_t b0[2] = {0u, 0u}, b1[2] = {0u, 0u}, b2[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int q = fixed_q((u[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, ex, bits);
+      const int sh = 8 * (i & 3);
+      b0[i >> 2] |= (static_cast<uint32_t>(q) & 0xFFu) << sh;
+      b1[i >> 2] |= (static_cast<uint32_t>(q >> 8) & 0xFFu) << sh;
+      b2[i >> 2] |= (static_cast<uint32_t>(q >> 16) & 0xFFu) << sh;
+    }
+    reinterpret_cast<uint2 *>(dst)[c] = make_uint2(b0[0], b0[1]);
+    reinterpret_cast<uint2 *>(dst + plane)[c] = make_uint2(b1[0], b1[1]);
+    if (tok) reinterpret_cast<uint2 *>(dst + 2 * plane)[c] = make_uint2(b2[0], b2[1]);
+  }
+  if (lane == 0) (tok ? rs.ex : rs.ew)[row] = ex;
+}
+
+template <bool AS, bool BS>  // signedness of A (token plane) and B (router plane)
+__device__ __forceinline__ void imma(int c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  if (!AS && !BS)
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+                 : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else if (!AS && BS)
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+                 : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else if (AS && !BS)
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+                 : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+                 : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t r[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(256) k_router_mma(RouterScratch rs, int T, int E, int R, int H,
+                                                    uint16_t *logits, uint16_t *shared_logit) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(128) uint8_t rsm[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int t0 = blockIdx.x * kRmTok, r0 = blockIdx.y * kRmRows;
+  const int wt = 16 * (warp & 3), wr = 32 * (warp >> 2);
+  const size_t xplane = static_cast<size_t>(T) * H, wplane = static_cast<size_t>(R) * H;
+  const int nk = H / kRmK;
+  // stage: 3 token planes x 64 rows, then 2 router planes x 64 rows; 8 x 16 B per row
+  auto stage = [&](int kc, int buf) {
+    uint8_t *base = rsm + buf * kRmStage;
+    for (int i = tid; i < (3 * kRmTok + 2 * kRmRows) * 8; i += 256) {
+      const int rr = i >> 3, c = i & 7;
+      const uint8_t *src = nullptr;
+      if (rr < 3 * kRmTok) {
+        const int pl = rr / kRmTok, row = t0 + rr - pl * kRmTok;
+        if (row < T) src = rs.xq + pl * xplane + static_cast<size_t>(row) * H;
       } else {
-        const int t = t0 + rr - kRtRows;
-        src = t < T ? x + static_cast<size_t>(t) * H : nullptr;
-        dst = &sx[b][rr - kRtRows][c * 8];
+        const int q = rr - 3 * kRmTok, pl = q / kRmRows, row = r0 + q - pl * kRmRows;
+        if (row < R) src = rs.wq + pl * wplane + static_cast<size_t>(row) * H;
       }
-      if (src != nullptr && h < H) cp_async16(dst, src + h);
+      if (src != nullptr) cp_async16(base + rr * kRmPitch + c * 16, src + kc * kRmK + c * 16);
     }
     cp_async_commit();
   };
-  float acc[8][WT];
+  int acc[4][4][4];  // [2^(8s)][n-tile][fragment]
 #pragma unroll
-  for (int r = 0; r < 8; ++r)
+  for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int t = 0; t < WT; ++t) acc[r][t] = -0.0f;
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[a][n][e] = 0;
+  // ldmatrix addressing: lane i serves row (i & 7) of matrix (i >> 3)
+  const int mi = lane >> 3, ri = lane & 7;
+  const uint32_t a_off = static_cast<uint32_t>((wt + (mi & 1) * 8 + ri) * kRmPitch + (mi >> 1) * 16);
+  const uint32_t b_off = static_cast<uint32_t>((3 * kRmTok + wr + (mi & 1) * 8 + ri) * kRmPitch + (mi >> 1) * 16);
   stage(0, 0);
-  for (int m = 0; m < nrounds; ++m) {
-    if (m + 1 < nrounds) stage(m + 1, (m + 1) & 1);
+  for (int kc = 0; kc < nk; ++kc) {
+    if (kc + 1 < nk) stage(kc + 1, (kc + 1) & 1);
     else cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    const int b = m & 1;
-    if (32 * m + lane < nchunks) {
-      // this lane's chunk of the warp's tokens as float32, then per router
-      // row its chunk and 8 x WT FMAs: every (row, token) chain takes the
-      // chunk's 8 elements in increasing h
-      float xf[WT][8];
+    const uint32_t sb = smem_u32(rsm + (kc & 1) * kRmStage);
 #pragma unroll
-      for (int t = 0; t < WT; ++t) bf16x8_to_f32(*reinterpret_cast<const uint4 *>(&sx[b][wt + t][lane * 8]), xf[t]);
+    for (int ks = 0; ks < kRmK / 32; ++ks) {
+      uint32_t A[3][4], B[2][4][2];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        float wf[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4 *>(&sw[b][wr + r][lane * 8]), wf);
+      for (int pl = 0; pl < 3; ++pl) ldsm4(sb + a_off + pl * kRmTok * kRmPitch + ks * 32, A[pl]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+      for (int pl = 0; pl < 2; ++pl)
 #pragma unroll
-          for (int t = 0; t < WT; ++t) acc[r][t] = __fmaf_rn(wf[i], xf[t][i], acc[r][t]);
+        for (int np = 0; np < 2; ++np) {
+          uint32_t r4[4];  // n-tiles 2np and 2np + 1: b0 of each, then b1 of each
+          ldsm4(sb + b_off + (pl * kRmRows + 16 * np) * kRmPitch + ks * 32, r4);
+          B[pl][2 * np][0] = r4[0];
+          B[pl][2 * np + 1][0] = r4[1];
+          B[pl][2 * np][1] = r4[2];
+          B[pl][2 * np + 1][1] = r4[3];
+        }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        imma<false, false>(acc[0][n], A[0], B[0][n][0], B[0][n][1]);
+        imma<false, false>(acc[1][n], A[1], B[0][n][0], B[0][n][1]);
+        imma<false, true>(acc[1][n], A[0], B[1][n][0], B[1][n][1]);
+        imma<true, false>(acc[2][n], A[2], B[0][n][0], B[0][n][1]);
+        imma<false, true>(acc[2][n], A[1], B[1][n][0], B[1][n][1]);
+        imma<true, true>(acc[3][n], A[2], B[1][n][0], B[1][n][1]);
       }
     }
     __syncthreads();
   }
+  // fragment e: token g (e < 2) or g + 8, router row 2t + (e & 1) of the n-tile
 #pragma unroll
-  for (int r = 0; r < 8; ++r)
+  for (int e = 0; e < 4; ++e) {
+    const int tok = t0 + wt + g + (e >> 1) * 8;
+    if (tok >= T) continue;
+    const int ex = rs.ex[tok];
 #pragma unroll
-    for (int t = 0; t < WT; ++t)
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) acc[r][t] = __fadd_rn(acc[r][t], __shfl_xor_sync(0xFFFFFFFFu, acc[r][t], off));
-  // every lane holds every sum; spread the stores over the lanes
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int row = r0 + wr + r;
-#pragma unroll
-    for (int t = 0; t < WT; ++t) {
-      const int tok = t0 + wt + t;
-      if (lane == ((r * WT + t) & 31) && row < rows && tok < T) {
-        if (row < E) logits[static_cast<size_t>(tok) * E + row] = f32_to_bf16(acc[r][t]);
-        else shared_logit[tok] = f32_to_bf16(acc[r][t]);
-      }
+    for (int n = 0; n < 4; ++n) {
+      const int row = r0 + wr + 8 * n + 2 * t + (e & 1);
+      if (row >= R) continue;
+      const long long S = static_cast<long long>(acc[0][n][e]) + (static_cast<long long>(acc[1][n][e]) << 8) +
+                          (static_cast<long long>(acc[2][n][e]) << 16) + (static_cast<long long>(acc[3][n][e]) << 24);
+      const uint16_t bits = router_logit_bits(S, ex, rs.ew[row]);
+      if (row < E) logits[static_cast<size_t>(tok) * E + row] = bits;
+      else shared_logit[tok] = bits;
     }
   }
 }
@@ -2278,19 +2406,30 @@ cudaError_t launch_router_cfg(const uint16_t *x, const uint16_t *W, int T, int H
   return e;
 }
 
+uint64_t router_scratch_bytes(int T, int R, int H) {
+  if (T < 64 || H % kRmK != 0 || H > 8192) return 0;
+  auto up = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
+  return up(3ull * T * H) + up(2ull * R * H) + up(4ull * T) + up(4ull * R);
+}
+
 cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, int H, int E,
                                  const uint16_t *w_shared_gate, uint16_t *logits,
                                  uint16_t *shared_logit, cudaStream_t s, uint16_t *prep_limbs, float *prep_meta,
-                                 int prep_G, bool *prep_done) {
+                                 int prep_G, bool *prep_done, const RouterScratch *rs) {
   const int ch = (H / 8 + 31) / 32;
   if (prep_done != nullptr) *prep_done = false;
-  if (T >= 64 && H % 8 == 0) {
-    const int rows = E + (w_shared_gate ? 1 : 0);
-    const int tok_tiles = (T + kRtTok - 1) / kRtTok;
-    // 16-row tiles: at ~156 registers per thread three 4-warp CTAs fit per SM
-    // (one 8-warp CTA with 32-row tiles), which hides more of the staging latency
-    cudaError_t e = launch_pdl(k_router_tiled<16, 4>, dim3((rows + 15) / 16, tok_tiles), 256, 0, s, x, W, T, H, E,
-                               w_shared_gate, logits, shared_logit);
+  const int rows = E + (w_shared_gate ? 1 : 0);
+  if (rs != nullptr && router_scratch_bytes(T, rows, H) > 0) {
+    // many tokens: byte planes, then the integer tensor-core GEMM
+    const int warps = T + rows;
+    cudaError_t e = launch_pdl(k_router_prep, (warps + 7) / 8, 256, 0, s, x, T, W, w_shared_gate, E, H, *rs,
+                               device_error_word());
+    if (e != cudaSuccess) return e;
+    static const cudaError_t attr =
+        cudaFuncSetAttribute(k_router_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, kRmSmem);
+    if (attr != cudaSuccess) return attr;
+    e = launch_pdl(k_router_mma, dim3((T + kRmTok - 1) / kRmTok, (rows + kRmRows - 1) / kRmRows), 256, kRmSmem, s,
+                   *rs, T, E, rows, H, logits, shared_logit);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }
@@ -2308,9 +2447,9 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
 #undef FNMOE_ROUTER_SMALL
     return cudaErrorInvalidValue;
   }
-  if (ch <= 4) return launch_router_cfg<4, 2, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
-  if (ch <= 8) return launch_router_cfg<8, 2, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
-  if (ch <= 12) return launch_router_cfg<12, 2, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
+  if (ch <= 4) return launch_router_cfg<4, 1, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
+  if (ch <= 8) return launch_router_cfg<8, 1, 16>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
+  if (ch <= 12) return launch_router_cfg<12, 1, 8>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
   if (ch <= 16) return launch_router_cfg<16, 1, 8>(x, W, T, H, E, w_shared_gate, logits, shared_logit, s);
   return cudaErrorInvalidValue;
 }

@@ -148,12 +148,26 @@ cudaError_t launch_combine_f32(const float *d, const uint32_t *routes, const voi
 // With prep_limbs / prep_meta set, batches of <= 4 tokens also compute the
 // row fixed point of x (launch_prep_rows' output) in extra CTAs of the same
 // launch; *prep_done tells whether that happened (else call launch_prep_rows).
+// Scratch of the many-token router: the byte-limb planes of the token rows'
+// and router rows' fixed points and their row exponents (router_scratch_bytes).
+struct RouterScratch {
+  uint8_t *xq;  // [3][T][H]: bytes 0 and 1 (unsigned) and 2 (signed) of X
+  uint8_t *wq;  // [2][R][H]: byte 0 (unsigned) and 1 (signed) of W
+  int32_t *ex;  // [T]
+  int32_t *ew;  // [R]
+};
+// Bytes of RouterScratch for T tokens and R router rows (0 when the tensor-
+// core path does not apply: fewer than 64 tokens or H not a multiple of 128).
+uint64_t router_scratch_bytes(int T, int R, int H);
+
+// Router logits.  With `rs` (sized by router_scratch_bytes) and at least 64
+// tokens, the integer tensor-core path; otherwise the exact integer GEMV.
 cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T,
                                  int H, int E, const uint16_t *w_shared_gate,
                                  uint16_t *logits, uint16_t *shared_logit,
                                  cudaStream_t s, uint16_t *prep_limbs = nullptr,
                                  float *prep_meta = nullptr, int prep_G = 32,
-                                 bool *prep_done = nullptr);
+                                 bool *prep_done = nullptr, const RouterScratch *rs = nullptr);
 cudaError_t launch_softmax_topk(const uint16_t *logits, int T, int E, int k,
                                 float blend, const uint32_t *route_map,
                                 int table_routes, uint32_t *inds,

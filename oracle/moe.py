@@ -37,8 +37,9 @@ one input row ``x`` of K values and one projection row with packed codes
 ``fl`` is float32 round-to-nearest-even and ``fma`` a float32 fused
 multiply-add (one rounding).
 
-Router dot products (bfloat16 weights) are exact per product and summed in a
-fixed 32-lane order (see ``router_logits``).  ``exp`` is correctly rounded:
+Router dot products are exact integer sums of the token row's and the router
+row's fixed points, scaled by a power of two and rounded once to bfloat16
+(see ``router_dot``): independent of any summation order.  ``exp`` is correctly rounded:
 to float32 in the softmax, to bfloat16 in the sigmoid.
 """
 from __future__ import annotations
@@ -428,44 +429,47 @@ def reference_execute(x, routes, gate, up, down, *, scores=None, shared_y=None,
 # Router (adaptive_topk.py:53-64, compiled.py:61-71)
 # --------------------------------------------------------------------------
 
-ROUTER_LANES = 32
-ROUTER_CHUNK = 8
+ROUTER_LANES = 32  # lanes of the softmax's canonical float32 sum
+ROUTER_X_BITS = 22  # token rows: X = trunc(x * 2**(22 - Ex)), |X| < 2**23 (the projection's fixed point)
+ROUTER_W_BITS = 14  # router rows: W = trunc(w * 2**(14 - Ew)), |W| < 2**15
 
 
-def lane_dot(x, w) -> np.ndarray:
-    """Canonical float32 dot products of bfloat16 rows: x [T,H], w [R,H] -> [T,R].
+def fixed_point_bits(x, bits: int):
+    """Row fixed point with ``bits`` fraction bits below the row's top
+    exponent: ``(E, X)`` with ``X = trunc(x * 2**(bits - E))`` (float64,
+    exact, |X| < 2**(bits + 1)); ``fixed_point_rows`` is the case bits = 22."""
+    x = np.asarray(x, dtype=np.float64)
+    nz = x != 0
+    _, e = np.frexp(np.abs(x))
+    e = np.where(nz, e - 1, -(1 << 20))
+    emax = e.max(axis=-1)
+    emax = np.where(nz.any(axis=-1), emax, 0).astype(np.int64)
+    X = np.trunc(np.ldexp(x, (bits - emax)[..., None].astype(np.int32)))
+    return emax, X
 
-    Each product of two bfloat16 values is exact in float32.  Lane j of 32
-    owns the 8-element chunks c = j, j+32, ... (h = 8c..8c+7) and adds their
-    products in increasing h from -0.0; the 32 lane sums are then combined
-    pairwise (j with j+16, then j+8, 4, 2, 1).
+
+def router_dot(x, w) -> np.ndarray:
+    """Canonical router dot products of bfloat16 rows: x [T,H], w [R,H] -> [T,R].
+
+    The exact value of ``sum_h X[h] * W[h] * 2**(Ex - 22 + Ew - 14)`` with
+    ``X``, ``W`` the row fixed points of the token row (22 fraction bits below
+    its top exponent ``Ex``) and of the router row (14 bits below ``Ew``).
+    The integer sum is exact in any order (|X*W| < 2**38, every partial sum
+    below 2**49), so tensor-core integer MMAs on byte limbs, CUDA-core
+    integer dot products and this float64 matrix product all give the same
+    number; the power-of-two scale is exact.  Truncation drops only input bits
+    below 2**-22 (tokens) / 2**-14 (router rows) of the row maximum.
     """
-    x = np.asarray(x, np.float32)
-    w = np.asarray(w, np.float32)
-    t, h = x.shape
-    r = w.shape[0]
-    chunks = h // ROUTER_CHUNK
-    m_count = -(-chunks // ROUTER_LANES)
-    lanes = np.full((t, r, ROUTER_LANES), -0.0, dtype=np.float32)
-    with np.errstate(all="ignore"):
-        for m in range(m_count):
-            c0 = m * ROUTER_LANES
-            nl = min(ROUTER_LANES, chunks - c0)
-            for i in range(ROUTER_CHUNK):
-                hs = (c0 + np.arange(nl)) * ROUTER_CHUNK + i
-                prod = x[:, hs][:, None, :] * w[:, hs][None, :, :]
-                lanes[:, :, :nl] = lanes[:, :, :nl] + prod
-        v = lanes
-        off = ROUTER_LANES // 2
-        while off >= 1:
-            v = v[..., :off] + v[..., off:2 * off]
-            off //= 2
-    return v[..., 0]
+    ex, X = fixed_point_bits(x, ROUTER_X_BITS)
+    ew, W = fixed_point_bits(w, ROUTER_W_BITS)
+    S = np.asarray(X, np.float64) @ np.asarray(W, np.float64).T
+    return np.ldexp(S, (ex[:, None] - ROUTER_X_BITS + ew[None, :] - ROUTER_W_BITS).astype(np.int32))
 
 
 def router_logits(x, router_weight) -> np.ndarray:
-    """BF16 router linear ``self.gate(x)`` (adaptive_topk.py:59,61): bf16 logits."""
-    return bf16.round_f32(lane_dot(x, router_weight))
+    """BF16 router linear ``self.gate(x)`` (adaptive_topk.py:59,61): bf16
+    logits, each the canonical dot product rounded once to bfloat16."""
+    return bf16.bits_to_f32(bf16.f64_to_bits(router_dot(x, router_weight)))
 
 
 def softmax_bf16(logits) -> np.ndarray:
@@ -587,7 +591,7 @@ def shared_expert(x, gate, up, down, gate_weight, group_size=32):
     u = bf16.round_f32(qmv(x, unpack_q4(uw), us, ub, group_size))
     act = swiglu_bf16(g, u)
     sh = bf16.round_f32(qmv(act, unpack_q4(dw), ds, db, group_size))
-    logit = bf16.round_f32(lane_dot(x, np.asarray(gate_weight, np.float32).reshape(1, -1)))
+    logit = router_logits(x, np.asarray(gate_weight, np.float32).reshape(1, -1))
     sg = sigmoid_bf16(logit)
     sy = bf16.op(np.multiply, sg, sh)
     return sh, sg, sy

@@ -100,13 +100,28 @@ def test_swiglu_contract_exhaustive(up_bits):
     assert np.count_nonzero((bf16.f32_to_bits(fp32) != bf16.f32_to_bits(ours)) & finite) > 0
 
 
-def test_router_lane_dot_matches_float64():
+def test_router_dot_matches_float64():
+    """The canonical router dot product differs from the exact float64 one
+    only by the truncation of input bits below 2**-22 / 2**-14 of each row's
+    maximum; its integer sum is exact, so byte-limb decompositions agree."""
     rng = np.random.default_rng(5)
     x = _bf(rng, (4, 2048))
     w = _bf(rng, (64, 2048), 0.02)
-    got = moe.lane_dot(x, w)
+    got = moe.router_dot(x, w)
     ref = x.astype(np.float64) @ w.T.astype(np.float64)
-    np.testing.assert_allclose(got, ref, rtol=0, atol=1e-6 * np.abs(ref).max())
+    bound = 2048 * (np.abs(x).max() * np.abs(w).max() * 2.0 ** -13)
+    assert np.abs(got - ref).max() < bound
+    np.testing.assert_allclose(got, ref, rtol=0, atol=2e-4 * np.abs(ref).max())
+    # the same integers through 3 x 2 byte limbs (the tensor-core form)
+    ex, X = moe.fixed_point_bits(x, moe.ROUTER_X_BITS)
+    ew, W = moe.fixed_point_bits(w, moe.ROUTER_W_BITS)
+    Xi, Wi = X.astype(np.int64), W.astype(np.int64)
+    xl = [Xi & 255, (Xi >> 8) & 255, Xi >> 16]
+    wl = [Wi & 255, Wi >> 8]
+    S = sum((xl[i] @ wl[j].T) << (8 * (i + j)) for i in range(3) for j in range(2))
+    np.testing.assert_array_equal(S, Xi @ Wi.T)
+    np.testing.assert_array_equal(np.ldexp(S.astype(np.float64), (ex[:, None] - 22 + ew[None, :] - 14).astype(np.int32)),
+                                  got)
 
 
 def test_topk_orders_by_probability_then_lower_index():
