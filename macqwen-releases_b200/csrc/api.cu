@@ -693,6 +693,11 @@ uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL, uint6
       LL.rs.wq = cv.take<uint8_t>(2ull * R * a->hidden_size);
       LL.rs.ex = cv.take<int32_t>(T);
       LL.rs.ew = cv.take<int32_t>(R);
+      LL.rs.ksplit = router_ksplit(T, R, a->hidden_size);
+      if (LL.rs.ksplit > 1) {
+        LL.rs.acc = cv.take<unsigned long long>(static_cast<uint64_t>(T) * R);
+        LL.rs.tickets = cv.take<int32_t>(static_cast<uint64_t>(router_tiles(T, R)));
+      }
       LL.has_rs = true;
     }
   }

@@ -297,6 +297,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_layer(FusedLayer p,
   __shared__ float s_score[kCombineMaxSlots];
   __shared__ float s_red[kFusedWarps];
   __shared__ uint32_t s_mx[8][8];
+  __shared__ uint32_t s_rmx[8];     // router row half maxima (warps 0-7)
+  __shared__ uint32_t s_xmx[8];     // maxima of x by eighths (warps 0-7)
+  __shared__ long long s_rsum[8];   // router row half sums (warps 0-7)
   __shared__ int s_keep;
   __shared__ float s_sg;
   __shared__ uint32_t s_armed;    // ring slots armed (bit i)
@@ -317,6 +320,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_layer(FusedLayer p,
   const XStage xsi = xstage_geom(I, G);
 
   uint16_t *xs = reinterpret_cast<uint16_t *>(fsm + p.off_x);
+  int *xqs = reinterpret_cast<int *>(fsm + p.off_xq);
   uint8_t *xl = fsm + p.off_xl;
   float *xm = reinterpret_cast<float *>(fsm + p.off_xm);
   float *soft = reinterpret_cast<float *>(fsm + p.off_soft);
@@ -401,19 +405,30 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_layer(FusedLayer p,
                            static_cast<size_t>(dg) * dn_item,
                        dn_item);
   }
-  // router rows: warps 0-7, row = cta + NB * warp (E + 1 <= 8 * nCTA); row E
-  // is the shared gate row
+  // Router rows: warps 0-7 in pairs, pair q = warp / 2 owns row cta + NB * q
+  // (E + 1 <= 4 * nCTA; row E is the shared gate row), each warp of a pair
+  // half of the row's 8-element chunks.  Integer sums combine exactly, so
+  // the halves add in shared memory.
   const int nchunks = H / 8;
-  const int row = cta + NB * warp;
+  const int hc = (nchunks + 1) / 2;             // chunks per half (<= 256: H <= 4096)
+  const int half = warp & 1;
+  const int row = cta + NB * (warp >> 1);
   const bool router_warp = warp < 8 && row < E + (has_sh ? 1 : 0);
-  uint4 wv[16];
+  const int c_end = min(nchunks, (half + 1) * hc);
+  uint4 wv[8];
   if (router_warp) {
     const uint16_t *wrow = row < E ? p.W + static_cast<size_t>(row) * H : p.wsg;
+    bool bad = false;
+    uint32_t mw = 0;
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const int cidx = lane + 32 * m;
-      wv[m] = (cidx < nchunks) ? ldg_u128(reinterpret_cast<const uint4 *>(wrow + cidx * 8)) : make_uint4(0, 0, 0, 0);
+    for (int m = 0; m < 8; ++m) {
+      const int cidx = half * hc + lane + 32 * m;
+      wv[m] = (cidx < c_end) ? ldg_u128(reinterpret_cast<const uint4 *>(wrow + cidx * 8)) : make_uint4(0, 0, 0, 0);
+      mw = max(mw, max_mag8(wv[m], bad));
     }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mw = max(mw, __shfl_xor_sync(0xFFFFFFFFu, mw, off));
+    if (lane == 0) s_rmx[warp] = mw;  // the router row's half maximum (constant data: before the wait)
   }
   pdl_trigger();
   pdl_wait();
@@ -431,47 +446,64 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_layer(FusedLayer p,
       fixed_point_group<G, 1>(xs, false, H, tr, 256, reinterpret_cast<uint16_t *>(xl), xm, err, 1, s_mx[0]);
     else
       fixed_point_group<G, 2>(xs, false, H, tr, 256, reinterpret_cast<uint16_t *>(xl), xm, err, 1, s_mx[0]);
-  } else if (router_warp) {
+  } else {
     // exact integer dot product of the row fixed points (k_router_logits'
-    // arithmetic): exponents of the router row and of x from warp maxima
+    // arithmetic).  x's maximum: each of warps 0-7 takes an eighth of x
+    // (named barrier 2 over the 256 router-warp threads).
     bool bad = false;
-    uint32_t mw = 0, mxx = 0;
+    uint32_t mxx = 0;
+    for (int c = warp * 32 + lane; c < nchunks; c += 256)
+      mxx = max(mxx, max_mag8(reinterpret_cast<const uint4 *>(xs)[c], bad));
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const int cidx = lane + 32 * m;
-      if (cidx < nchunks) {
-        mw = max(mw, max_mag8(wv[m], bad));
-        mxx = max(mxx, max_mag8(reinterpret_cast<const uint4 *>(xs)[cidx], bad));
+    for (int off = 16; off >= 1; off >>= 1) mxx = max(mxx, __shfl_xor_sync(0xFFFFFFFFu, mxx, off));
+    if (lane == 0) s_xmx[warp] = mxx;
+    named_sync(2, 256);
+    uint32_t mx_all = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) mx_all = max(mx_all, s_xmx[w]);
+    const int ex = row_exponent(mx_all);
+    // x's fixed point, once per CTA: each of warps 0-7 converts an eighth
+    {
+      const FixScale sx = fix_scale(ex, kRouterXBits);
+      for (int c = warp * 32 + lane; c < nchunks; c += 256) {
+        const uint4 v = reinterpret_cast<const uint4 *>(xs)[c];
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+        int q8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q8[i] = fixed_qf((u[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, sx);
+        reinterpret_cast<int4 *>(xqs)[2 * c] = make_int4(q8[0], q8[1], q8[2], q8[3]);
+        reinterpret_cast<int4 *>(xqs)[2 * c + 1] = make_int4(q8[4], q8[5], q8[6], q8[7]);
       }
     }
+    named_sync(2, 256);
+    if (router_warp) {
+      const int ew = row_exponent(max(s_rmx[warp & ~1], s_rmx[warp | 1]));
+      const FixScale sw = fix_scale(ew, kRouterWBits);
+      long long a = 0;
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-      mw = max(mw, __shfl_xor_sync(0xFFFFFFFFu, mw, off));
-      mxx = max(mxx, __shfl_xor_sync(0xFFFFFFFFu, mxx, off));
-    }
-    const int ew = row_exponent(mw), ex = row_exponent(mxx);
-    long long a = 0;
+      for (int m = 0; m < 8; ++m) {
+        const int cidx = half * hc + lane + 32 * m;
+        if (cidx < c_end) {
+          const int4 x0 = reinterpret_cast<const int4 *>(xqs)[2 * cidx];
+          const int4 x1 = reinterpret_cast<const int4 *>(xqs)[2 * cidx + 1];
+          const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+          const uint32_t wu[4] = {wv[m].x, wv[m].y, wv[m].z, wv[m].w};
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const int cidx = lane + 32 * m;
-      if (cidx < nchunks) {
-        const uint4 xv4 = reinterpret_cast<const uint4 *>(xs)[cidx];
-        const uint32_t wu[4] = {wv[m].x, wv[m].y, wv[m].z, wv[m].w};
-        const uint32_t xu[4] = {xv4.x, xv4.y, xv4.z, xv4.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int wq = fixed_q((wu[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, ew, kRouterWBits);
-          const int xq = fixed_q((xu[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, ex, kRouterXBits);
-          a += static_cast<long long>(wq) * xq;
+          for (int i = 0; i < 8; ++i)
+            a += static_cast<long long>(fixed_qf((wu[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, sw)) * xv[i];
         }
       }
-    }
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, off);
-    if (lane == 0) {
-      const uint16_t bits = router_logit_bits(a, ex, ew);
-      if (row < E) p.logits[row] = bits;
-      else p.shared_logit[0] = bits;
+      for (int off = 16; off >= 1; off >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, off);
+      if (lane == 0) s_rsum[warp] = a;
+      __syncwarp();
+      // the pair's halves meet: a barrier over just the pair's 64 threads
+      asm volatile("bar.sync %0, 64;\n" ::"r"(3 + (warp >> 1)) : "memory");
+      if (half == 0 && lane == 0) {
+        const uint16_t bits = router_logit_bits(s_rsum[warp] + s_rsum[warp + 1], ex, ew);
+        if (row < E) p.logits[row] = bits;
+        else p.shared_logit[0] = bits;
+      }
     }
   }
   if (!grid_sync(p.bar, err, &s_flag)) {
@@ -796,11 +828,13 @@ inline bool fused_layer_geometry(FusedLayer &p, int sms, int G, size_t limit, si
   const size_t dn_item = static_cast<size_t>(nblk_i) * kTileChunk;
   const XStage xsh = xstage_geom(H, G), xsi = xstage_geom(I, G);
   const int nslot = (units * n_rg + sms - 1) / sms;
-  if (nslot > kFusedMaxSlots || E + 1 > 8 * sms) return false;
+  if (nslot > kFusedMaxSlots || E + 1 > 4 * sms) return false;
   auto up = [](size_t v) { return (v + 127) & ~static_cast<size_t>(127); };
   size_t off = 0;
   p.off_x = static_cast<int>(off);
   off = up(off + static_cast<size_t>(H) * 2);
+  p.off_xq = static_cast<int>(off);  // x's router fixed point (int32)
+  off = up(off + static_cast<size_t>(H) * 4);
   p.off_xl = static_cast<int>(off);
   off = up(off + static_cast<size_t>(xsh.Xrow));
   p.off_xm = static_cast<int>(off);

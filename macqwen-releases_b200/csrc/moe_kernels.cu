@@ -13,6 +13,7 @@
 // tensor cores (m16n8k16 fp16 -> fp32).  Every operand and partial sum is an
 // integer below 2^21, so the accumulation is exact and order-free; the
 // epilogue rounds exactly where the CPU oracle does (oracle/moe.py).
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -155,15 +156,25 @@ __device__ __forceinline__ int row_exponent(uint32_t mx) {
   if (mx == 0) return 0;
   return (mx >> 7) ? static_cast<int>(mx >> 7) - 127 : (31 - __clz(static_cast<int>(mx))) - 133;
 }
-// trunc(h * 2^(bits - E)) of one bfloat16 input; fixed_x is bits = 22.
-__device__ __forceinline__ int fixed_q(uint32_t h, int E, int bits) {
-  const uint32_t ef = (h >> 7) & 0xFFu, mf = h & 0x7Fu;
-  if ((h & 0x7FFFu) == 0 || ef == 255u) return 0;
-  const uint32_t M = ef ? (mf | 0x80u) : mf;
-  const int sh = ef ? (static_cast<int>(ef) - 134 + bits - E) : (-133 + bits - E);
-  const uint32_t mag = sh >= 0 ? (M << sh) : ((-sh >= 31) ? 0u : (M >> (-sh)));
-  return (h & 0x8000u) ? -static_cast<int>(mag) : static_cast<int>(mag);
+// trunc(x * 2^(bits - E)) of one bfloat16 input x (bits h), E the row
+// exponent (fixed_x is the integer form for bits = 22), through float32: the
+// scale 2^(bits - E) = s1 * s2 (each a power of two), the product exact
+// (|x * 2^(bits - E)| < 2^(bits + 1); a product that would drop below
+// 2^-126 truncates to 0 either way), cvt.rzi truncates.  Non-finite inputs
+// give 0.
+struct FixScale {
+  float s1, s2;
+};
+__device__ __forceinline__ FixScale fix_scale(int E, int bits) {
+  const int k = bits - E;  // >= -113 for bfloat16 rows
+  const int k1 = min(k, 127);
+  return FixScale{__int_as_float((k1 + 127) << 23), __int_as_float((k - k1 + 127) << 23)};
 }
+__device__ __forceinline__ int fixed_qf(uint32_t h, FixScale sc) {
+  if ((h & 0x7F80u) == 0x7F80u) return 0;
+  return __float2int_rz(__fmul_rn(__fmul_rn(__uint_as_float(h << 16), sc.s1), sc.s2));
+}
+
 // Largest finite magnitude bits of 8 bfloat16 values; `bad` when one is not finite.
 __device__ __forceinline__ uint32_t max_mag8(const uint4 v, bool &bad) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -2121,11 +2132,12 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
     ew[q] = row_exponent(mx);
+    const FixScale sw = fix_scale(ew[q], kRouterWBits);
 #pragma unroll
     for (int m = 0; m < CH; ++m) {
       const uint32_t u[4] = {wv[m].x, wv[m].y, wv[m].z, wv[m].w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w[q][m * 8 + i] = fixed_q((u[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, ew[q], kRouterWBits);
+      for (int i = 0; i < 8; ++i) w[q][m * 8 + i] = fixed_qf((u[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, sw);
     }
   }
   // the router rows are constant: their loads above overlap the previous kernel
@@ -2142,11 +2154,11 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
   __syncthreads();
   for (int idx = threadIdx.x; idx < tb * nchunks; idx += blockDim.x) {
     const uint4 v = xsrc[idx];
-    const int ex = s_ex[idx / nchunks];
+    const FixScale sx = fix_scale(s_ex[idx / nchunks], kRouterXBits);
     const uint32_t u[4] = {v.x, v.y, v.z, v.w};
     int q8[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q8[i] = fixed_q((u[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, ex, kRouterXBits);
+    for (int i = 0; i < 8; ++i) q8[i] = fixed_qf((u[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, sx);
     reinterpret_cast<int4 *>(xq)[2 * idx] = make_int4(q8[0], q8[1], q8[2], q8[3]);
     reinterpret_cast<int4 *>(xq)[2 * idx + 1] = make_int4(q8[4], q8[5], q8[6], q8[7]);
   }
@@ -2206,19 +2218,24 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_logits(
 // 2^16 X2 (X0, X1 unsigned, X2 signed: |X| < 2^23), router W = W0 + 2^8 W1
 // (W0 unsigned, W1 signed: |W| < 2^15).
 //
-// k_router_mma: CTA tile 64 tokens x 64 router rows, 8 warps of 16 tokens x
-// 32 rows; K in 128-byte chunks through a double-buffered cp.async ring
-// (rows padded to 144 bytes: the eight rows of an ldmatrix phase fall in
-// distinct bank groups).  Per 32-byte k-step a warp loads its A fragments
+// k_router_mma: CTA tile 64 tokens x 32 router rows, 4 warps of 16 tokens x
+// 32 rows; K in 128-byte chunks through a 3-stage TMA ring: per chunk one 2D
+// box (128 bytes x 64 rows) per token plane and one (128 x 32) per router
+// plane, 128-byte swizzle (16-byte chunk j of box row r at j ^ (r & 7), so
+// the eight rows of an ldmatrix phase fall in distinct bank groups); thread 0
+// refills a stage once all four warps have released it.  Per 32-byte k-step a warp loads its A fragments
 // (three token planes) and B fragments (two router planes) with ldmatrix and
 // issues mma.sync.m16n8k32 with s32 accumulation for the six limb pairs,
 // summed per power of two (2^0, 2^8, 2^16, 2^24: every partial sum stays
 // below 2^31 for H <= 8192).  The epilogue forms the exact int64 dot
 // product, scales it by 2^(Ex - 22 + Ew - 14) and rounds once to bfloat16:
 // the GEMV kernels' bits.
-constexpr int kRmTok = 64, kRmRows = 64, kRmK = 128, kRmPitch = kRmK + 16;
-constexpr int kRmStage = (3 * kRmTok + 2 * kRmRows) * kRmPitch;  // bytes per ring stage
-constexpr int kRmSmem = 2 * kRmStage;
+constexpr int kRmTok = 64, kRmRows = 32, kRmK = 128, kRmThreads = 128, kRmStages = 3;
+constexpr int kRmTokBox = kRmTok * kRmK, kRmRowBox = kRmRows * kRmK;  // box bytes
+constexpr int kRmStage = 3 * kRmTokBox + 2 * kRmRowBox;               // bytes per ring stage
+constexpr int kRmBarOff = kRmStages * kRmStage;
+constexpr int kRmSmem = kRmBarOff + 16 * kRmStages + 1024;            // + barriers + 1 KiB alignment
+constexpr uint32_t kRmSpin = 1u << 22;                                // mbarrier polls before giving up
 
 __global__ void __launch_bounds__(256) k_router_prep(const uint16_t *x, int T, const uint16_t *__restrict__ W,
                                                      const uint16_t *__restrict__ wsg, int E, int H,
@@ -2227,6 +2244,14 @@ __global__ void __launch_bounds__(256) k_router_prep(const uint16_t *x, int T, c
   pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int R = E + (wsg != nullptr ? 1 : 0);
+  if (rs.ksplit > 1) {  // split-K: zero the partial sums and the tile tickets
+    const size_t n = static_cast<size_t>(T) * R;
+    const size_t tiles = static_cast<size_t>((T + kRmTok - 1) / kRmTok) * ((R + kRmRows - 1) / kRmRows);
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) rs.acc[i] = 0ull;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < tiles; i += stride)
+      rs.tickets[i] = 0;
+  }
   if (warp >= T + R) return;
   const bool tok = warp < T;
   const int row = tok ? warp : warp - T;
@@ -2239,7 +2264,7 @@ __global__ void __launch_bounds__(256) k_router_prep(const uint16_t *x, int T, c
   for (int off = 16; off >= 1; off >>= 1) mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
   if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) set_error(err, kErrNonFinite);
   const int ex = row_exponent(mx);
-  const int bits = tok ? kRouterXBits : kRouterWBits;
+  const FixScale sc = fix_scale(ex, tok ? kRouterXBits : kRouterWBits);
   const size_t plane = tok ? static_cast<size_t>(T) * H : static_cast<size_t>(R) * H;
   uint8_t *dst = (tok ? rs.xq : rs.wq) + static_cast<size_t>(row) * H;
   for (int c = lane; c < nchunks; c += 32) {
@@ -2248,7 +2273,7 @@ __global__ void __launch_bounds__(256) k_router_prep(const uint16_t *x, int T, c
     uint32_t b0[2] = {0u, 0u}, b1[2] = {0u, 0u}, b2[2] = {0u, 0u};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int q = fixed_q((u[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, ex, bits);
+      const int q = fixed_qf((u[i >> 1] >> (16 * (i & 1))) & 0xFFFFu, sc);
       const int sh = 8 * (i & 3);
       b0[i >> 2] |= (static_cast<uint32_t>(q) & 0xFFu) << sh;
       b1[i >> 2] |= (static_cast<uint32_t>(q >> 8) & 0xFFu) << sh;
@@ -2288,34 +2313,69 @@ __device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t r[4]) {
                : "memory");
 }
 
-__global__ void __launch_bounds__(256) k_router_mma(RouterScratch rs, int T, int E, int R, int H,
-                                                    uint16_t *logits, uint16_t *shared_logit) {
+// 2D TMA load of one box (no multicast) completing on mbarrier `bar`.
+__device__ __forceinline__ void rm_tma(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool rm_wait(uint64_t *bar, unsigned parity, uint32_t *err) {
+  uint32_t spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if (++spins >= kRmSpin) {
+      set_error(err, kErrTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Byte offset of 16-byte chunk j of row r in a 128-byte-swizzled box.
+__device__ __forceinline__ uint32_t rm_swz(int r, int j) { return r * 128 + (((j ^ r) & 7) << 4); }
+
+__global__ void __launch_bounds__(kRmThreads) k_router_mma(const __grid_constant__ CUtensorMap xmap,
+                                                           const __grid_constant__ CUtensorMap wmap,
+                                                           RouterScratch rs, int T, int E, int R, int H,
+                                                           uint16_t *logits, uint16_t *shared_logit, uint32_t *err) {
   pdl_wait();
   pdl_trigger();
-  extern __shared__ __align__(128) uint8_t rsm[];
+  extern __shared__ __align__(128) uint8_t rsm_raw[];
+  uint8_t *rsm = rsm_raw + ((1024u - (smem_u32(rsm_raw) & 1023u)) & 1023u);
+  uint64_t *full = reinterpret_cast<uint64_t *>(rsm + kRmBarOff);
+  uint64_t *empty = full + kRmStages;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const int t0 = blockIdx.x * kRmTok, r0 = blockIdx.y * kRmRows;
-  const int wt = 16 * (warp & 3), wr = 32 * (warp >> 2);
-  const size_t xplane = static_cast<size_t>(T) * H, wplane = static_cast<size_t>(R) * H;
-  const int nk = H / kRmK;
-  // stage: 3 token planes x 64 rows, then 2 router planes x 64 rows; 8 x 16 B per row
-  auto stage = [&](int kc, int buf) {
-    uint8_t *base = rsm + buf * kRmStage;
-    for (int i = tid; i < (3 * kRmTok + 2 * kRmRows) * 8; i += 256) {
-      const int rr = i >> 3, c = i & 7;
-      const uint8_t *src = nullptr;
-      if (rr < 3 * kRmTok) {
-        const int pl = rr / kRmTok, row = t0 + rr - pl * kRmTok;
-        if (row < T) src = rs.xq + pl * xplane + static_cast<size_t>(row) * H;
-      } else {
-        const int q = rr - 3 * kRmTok, pl = q / kRmRows, row = r0 + q - pl * kRmRows;
-        if (row < R) src = rs.wq + pl * wplane + static_cast<size_t>(row) * H;
-      }
-      if (src != nullptr) cp_async16(base + rr * kRmPitch + c * 16, src + kc * kRmK + c * 16);
+  const int wt = 16 * warp, wr = 0;
+  // this CTA's k-chunks: slice blockIdx.z of rs.ksplit
+  const int nk_all = H / kRmK;
+  const int per = (nk_all + rs.ksplit - 1) / rs.ksplit;
+  const int kc0 = min(nk_all, static_cast<int>(blockIdx.z) * per);
+  const int nk = min(nk_all, kc0 + per) - kc0;
+  if (tid == 0) {
+    for (int i = 0; i < kRmStages; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, kRmThreads / 32);
     }
-    cp_async_commit();
+    mbar_init_fence();
+  }
+  __syncthreads();
+  // stage: 3 token-plane boxes (plane p rows p*T + t0 ..), 2 router-plane boxes
+  auto issue = [&](int kc, int slot) {
+    uint8_t *base = rsm + slot * kRmStage;
+    mbar_expect_tx(full + slot, kRmStage);
+    const int x = (kc0 + kc) * kRmK;
+#pragma unroll
+    for (int p = 0; p < 3; ++p) rm_tma(smem_u32(base + p * kRmTokBox), &xmap, x, p * T + t0, full + slot);
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+      rm_tma(smem_u32(base + 3 * kRmTokBox + p * kRmRowBox), &wmap, x, p * R + r0, full + slot);
   };
+  bool dead = false;
+  if (tid == 0)
+    for (int i = 0; i < kRmStages - 1 && i < nk; ++i) issue(i, i);
   int acc[4][4][4];  // [2^(8s)][n-tile][fragment]
 #pragma unroll
   for (int a = 0; a < 4; ++a)
@@ -2325,60 +2385,92 @@ __global__ void __launch_bounds__(256) k_router_mma(RouterScratch rs, int T, int
       for (int e = 0; e < 4; ++e) acc[a][n][e] = 0;
   // ldmatrix addressing: lane i serves row (i & 7) of matrix (i >> 3)
   const int mi = lane >> 3, ri = lane & 7;
-  const uint32_t a_off = static_cast<uint32_t>((wt + (mi & 1) * 8 + ri) * kRmPitch + (mi >> 1) * 16);
-  const uint32_t b_off = static_cast<uint32_t>((3 * kRmTok + wr + (mi & 1) * 8 + ri) * kRmPitch + (mi >> 1) * 16);
-  stage(0, 0);
+  const int a_row = wt + (mi & 1) * 8 + ri, b_row = wr + (mi & 1) * 8 + ri;
   for (int kc = 0; kc < nk; ++kc) {
-    if (kc + 1 < nk) stage(kc + 1, (kc + 1) & 1);
-    else cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const uint32_t sb = smem_u32(rsm + (kc & 1) * kRmStage);
+    const int slot = kc % kRmStages;
+    if (tid == 0 && kc + kRmStages - 1 < nk) {
+      // refill the slot chunk kc - 1 used, once every warp has released it
+      const int nxt = kc + kRmStages - 1, ns = nxt % kRmStages;
+      if (nxt >= kRmStages && !dead) dead = !rm_wait(empty + ns, ((nxt / kRmStages) - 1) & 1, err);
+      if (!dead) issue(nxt, ns);
+    }
+    __syncwarp();
+    if (!rm_wait(full + slot, (kc / kRmStages) & 1, err)) break;
+    const uint32_t sb = smem_u32(rsm + slot * kRmStage);
 #pragma unroll
     for (int ks = 0; ks < kRmK / 32; ++ks) {
-      uint32_t A[3][4], B[2][4][2];
+      const int jc = 2 * ks + (mi >> 1);  // 16-byte chunk of this lane's matrix row
+      uint32_t A[3][4];
 #pragma unroll
-      for (int pl = 0; pl < 3; ++pl) ldsm4(sb + a_off + pl * kRmTok * kRmPitch + ks * 32, A[pl]);
+      for (int pl = 0; pl < 3; ++pl) ldsm4(sb + pl * kRmTokBox + rm_swz(a_row, jc), A[pl]);
 #pragma unroll
-      for (int pl = 0; pl < 2; ++pl)
+      for (int np = 0; np < 2; ++np) {
+        // n-tiles 2np and 2np + 1 of both router planes: b0 of each, then b1 of each
+        uint32_t B0[4], B1[4];
+        ldsm4(sb + 3 * kRmTokBox + rm_swz(b_row + 16 * np, jc), B0);
+        ldsm4(sb + 3 * kRmTokBox + kRmRowBox + rm_swz(b_row + 16 * np, jc), B1);
 #pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          uint32_t r4[4];  // n-tiles 2np and 2np + 1: b0 of each, then b1 of each
-          ldsm4(sb + b_off + (pl * kRmRows + 16 * np) * kRmPitch + ks * 32, r4);
-          B[pl][2 * np][0] = r4[0];
-          B[pl][2 * np + 1][0] = r4[1];
-          B[pl][2 * np][1] = r4[2];
-          B[pl][2 * np + 1][1] = r4[3];
+        for (int nn = 0; nn < 2; ++nn) {
+          const int n = 2 * np + nn;
+          imma<false, false>(acc[0][n], A[0], B0[nn], B0[2 + nn]);
+          imma<false, false>(acc[1][n], A[1], B0[nn], B0[2 + nn]);
+          imma<false, true>(acc[1][n], A[0], B1[nn], B1[2 + nn]);
+          imma<true, false>(acc[2][n], A[2], B0[nn], B0[2 + nn]);
+          imma<false, true>(acc[2][n], A[1], B1[nn], B1[2 + nn]);
+          imma<true, true>(acc[3][n], A[2], B1[nn], B1[2 + nn]);
         }
-#pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        imma<false, false>(acc[0][n], A[0], B[0][n][0], B[0][n][1]);
-        imma<false, false>(acc[1][n], A[1], B[0][n][0], B[0][n][1]);
-        imma<false, true>(acc[1][n], A[0], B[1][n][0], B[1][n][1]);
-        imma<true, false>(acc[2][n], A[2], B[0][n][0], B[0][n][1]);
-        imma<false, true>(acc[2][n], A[1], B[1][n][0], B[1][n][1]);
-        imma<true, true>(acc[3][n], A[2], B[1][n][0], B[1][n][1]);
       }
     }
-    __syncthreads();
+    __syncwarp();
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(empty + slot)) : "memory");
   }
+  // every box issued lands before the CTA exits
+  if (tid == 0)
+    for (int kc = max(0, nk - kRmStages); kc < nk; ++kc) rm_wait(full + kc % kRmStages, (kc / kRmStages) & 1, err);
   // fragment e: token g (e < 2) or g + 8, router row 2t + (e & 1) of the n-tile
+  const bool split = rs.ksplit > 1;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const int tok = t0 + wt + g + (e >> 1) * 8;
     if (tok >= T) continue;
-    const int ex = rs.ex[tok];
+    const int ex = split ? 0 : rs.ex[tok];
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
       const int row = r0 + wr + 8 * n + 2 * t + (e & 1);
       if (row >= R) continue;
       const long long S = static_cast<long long>(acc[0][n][e]) + (static_cast<long long>(acc[1][n][e]) << 8) +
                           (static_cast<long long>(acc[2][n][e]) << 16) + (static_cast<long long>(acc[3][n][e]) << 24);
+      if (split) {
+        // integer sums are exact in any order: slices add into the tile's partial sums
+        atomicAdd(rs.acc + static_cast<size_t>(tok) * R + row, static_cast<unsigned long long>(S));
+        continue;
+      }
       const uint16_t bits = router_logit_bits(S, ex, rs.ew[row]);
       if (row < E) logits[static_cast<size_t>(tok) * E + row] = bits;
       else shared_logit[tok] = bits;
     }
   }
+  if (!split) return;
+  // the tile's last slice to finish converts its sums (and clears them)
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+  if (tid == 0) s_last = atomicAdd(rs.tickets + tile, 1) == rs.ksplit - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = tid; i < kRmTok * kRmRows; i += kRmThreads) {
+    const int tok = t0 + i / kRmRows, row = r0 + i % kRmRows;
+    if (tok >= T || row >= R) continue;
+    unsigned long long *p = rs.acc + static_cast<size_t>(tok) * R + row;
+    const long long S = static_cast<long long>(__ldcg(p));
+    *p = 0ull;
+    const uint16_t bits = router_logit_bits(S, rs.ex[tok], rs.ew[row]);
+    if (row < E) logits[static_cast<size_t>(tok) * E + row] = bits;
+    else shared_logit[tok] = bits;
+  }
+  if (tid == 0) rs.tickets[tile] = 0;
 }
 
 template <int CH, int RW, int TOK, int NW = 8>
@@ -2406,10 +2498,58 @@ cudaError_t launch_router_cfg(const uint16_t *x, const uint16_t *W, int T, int H
   return e;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+namespace {
+EncodeTiledFn router_encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+}  // namespace
+
+// A byte matrix [rows][cols] (row pitch cols, a multiple of 128) as a tensor
+// map with 128-byte x box_rows boxes, 128-byte swizzle; rows past the end
+// read as zero.
+bool make_u8_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, int box_rows) {
+  EncodeTiledFn fn = router_encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRmK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int router_tiles(int T, int R) { return ((T + kRmTok - 1) / kRmTok) * ((R + kRmRows - 1) / kRmRows); }
+
+int router_ksplit(int T, int R, int H) {
+  const long long tiles = router_tiles(T, R);
+  const int nk = H / kRmK;
+  const long long want = (3LL * device_info().sms + tiles - 1) / tiles;  // three CTAs per SM
+  return static_cast<int>(std::max(1LL, std::min<long long>(nk, want)));
+}
+
 uint64_t router_scratch_bytes(int T, int R, int H) {
   if (T < 64 || H % kRmK != 0 || H > 8192) return 0;
   auto up = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
-  return up(3ull * T * H) + up(2ull * R * H) + up(4ull * T) + up(4ull * R);
+  uint64_t b = up(3ull * T * H) + up(2ull * R * H) + up(4ull * T) + up(4ull * R);
+  if (router_ksplit(T, R, H) > 1) {
+    b += up(8ull * T * R) + up(4ull * router_tiles(T, R));
+  }
+  return b;
 }
 
 cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, int H, int E,
@@ -2428,8 +2568,12 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
     static const cudaError_t attr =
         cudaFuncSetAttribute(k_router_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, kRmSmem);
     if (attr != cudaSuccess) return attr;
-    e = launch_pdl(k_router_mma, dim3((T + kRmTok - 1) / kRmTok, (rows + kRmRows - 1) / kRmRows), 256, kRmSmem, s,
-                   *rs, T, E, rows, H, logits, shared_logit);
+    CUtensorMap xmap{}, wmap{};
+    if (!make_u8_map(&xmap, rs->xq, 3ull * T, H, kRmTok) || !make_u8_map(&wmap, rs->wq, 2ull * rows, H, kRmRows))
+      return cudaErrorInvalidValue;
+    e = launch_pdl(k_router_mma, dim3((T + kRmTok - 1) / kRmTok, (rows + kRmRows - 1) / kRmRows, rs->ksplit),
+                   kRmThreads, kRmSmem, s, xmap, wmap, *rs, T, E, rows, H, logits, shared_logit,
+                   device_error_word());
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }

@@ -155,7 +155,15 @@ struct RouterScratch {
   uint8_t *wq;  // [2][R][H]: byte 0 (unsigned) and 1 (signed) of W
   int32_t *ex;  // [T]
   int32_t *ew;  // [R]
+  unsigned long long *acc;  // [T][R] int64 partial sums (split-K only)
+  int32_t *tickets;         // per 64 x 64 tile (split-K only)
+  int ksplit;               // K slices per tile (router_ksplit)
 };
+// K slices of the tensor-core router for these sizes: enough (sequence of
+// 128-byte k-chunks split evenly) that small token counts still fill the SMs.
+int router_ksplit(int T, int R, int H);
+// Output tiles of the tensor-core router (split-K tickets).
+int router_tiles(int T, int R);
 // Bytes of RouterScratch for T tokens and R router rows (0 when the tensor-
 // core path does not apply: fewer than 64 tokens or H not a multiple of 128).
 uint64_t router_scratch_bytes(int T, int R, int H);
@@ -225,7 +233,7 @@ struct FusedLayer {
   // shared-memory carve (byte offsets into the dynamic allocation)
   int nslot;                // ring slots = most gate/up items a CTA can get
   int alias;                // 1: the down stage and activation limbs reuse the ring
-  int off_x, off_xl, off_xm, off_soft, off_d, off_ring, off_down, off_al, off_am;
+  int off_x, off_xq, off_xl, off_xm, off_soft, off_d, off_ring, off_down, off_al, off_am;
 };
 
 // cudaErrorNotSupported when the sizes do not fit the fused kernel (the
