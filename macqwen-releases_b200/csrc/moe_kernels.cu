@@ -25,6 +25,7 @@
 
 #include "async.cuh"
 #include "common.cuh"
+#include "umma.cuh"
 #include "moe_kernels.cuh"
 
 namespace fnmoe {
@@ -2473,6 +2474,227 @@ __global__ void __launch_bounds__(kRmThreads) k_router_mma(const __grid_constant
   if (tid == 0) rs.tickets[tile] = 0;
 }
 
+// Router logits for prefill-sized batches on tcgen05, from the byte planes of
+// k_router_prep.  A tile is 128 tokens (MMA M: TMEM lanes) x 64 router rows
+// (MMA N).  Per 32-byte k-step six tcgen05.mma.kind::i8 (M128 N64 K32, s32 in
+// TMEM) add the limb products into four 64-column accumulators, one per
+// power of two: 2^0 X0 W0; 2^8 X1 W0 + X0 W1; 2^16 X2 W0 + X1 W1; 2^24 X2 W1
+// (X2 and W1 signed; every partial sum stays below 2^31 for H <= 8192).
+// Persistent CTAs, one per SM, walk the tiles; two 256-column accumulator
+// sets let the epilogue of one tile overlap the MMAs of the next.
+//   warp 0     TMA producer: per 128-byte k-chunk three 128-row token boxes
+//              and two 64-row router boxes (128-byte swizzle, the K-major
+//              SW128 operand layout), 3-stage ring;
+//   warp 1     TMEM allocation and the MMA issuer (one thread);
+//   warps 2-5  epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (its 32
+//              tokens), forms the exact int64 sums, scales them by
+//              2^(Ex - 22 + Ew - 14) and rounds once to bfloat16 -- the GEMV
+//              kernels' bits.
+// Every wait is bounded; a timeout sets kErrTimeout, marks the CTA dead
+// (later waits return at once) and every role runs to the teardown.
+constexpr int kRuTok = 128, kRuRows = 64, kRuStages = 3, kRuThreads = 192;
+constexpr int kRuTokBox = kRuTok * kRmK, kRuRowBox = kRuRows * kRmK;  // box bytes
+constexpr int kRuStage = 3 * kRuTokBox + 2 * kRuRowBox;               // 64 KB per ring stage
+constexpr int kRuBarOff = kRuStages * kRuStage;
+constexpr int kRuFull = 0, kRuEmpty = kRuStages, kRuAccFull = 2 * kRuStages, kRuAccEmpty = kRuAccFull + 2,
+              kRuBars = kRuAccEmpty + 2;
+constexpr int kRuSmem = kRuBarOff + 8 * kRuBars + 16 + 1024;  // + tmem slot, dead flag, 1 KiB alignment
+constexpr uint32_t kRuTmemCols = 512;                         // two sets of four 64-column accumulators
+static_assert(kRuSmem <= 227 * 1024, "router tcgen05 shared memory");
+
+// Instruction descriptor of kind::i8: s32 D, A/B signedness, K-major A and B, N 64, M 128.
+__host__ __device__ constexpr uint32_t ru_idesc(bool a_signed, bool b_signed) {
+  return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | ((b_signed ? 1u : 0u) << 10) |
+         (static_cast<uint32_t>(kRuRows >> 3) << 17) | (static_cast<uint32_t>(kRuTok >> 4) << 24);
+}
+
+template <bool AS, bool BS>
+__device__ __forceinline__ void umma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(ru_idesc(AS, BS)), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ bool ru_wait(uint32_t bar, uint32_t parity, volatile uint32_t *dead, uint32_t *err) {
+  uint32_t spins = 0;
+  while (!mbar_try_wait_u32(bar, parity)) {
+    if (*dead) return false;
+    if (++spins >= kRmSpin) {
+      *dead = 1u;
+      set_error(err, kErrTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(kRuThreads, 1) k_router_umma(const __grid_constant__ CUtensorMap xmap,
+                                                               const __grid_constant__ CUtensorMap wmap,
+                                                               RouterScratch rs, int T, int E, int R, int H,
+                                                               uint16_t *logits, uint16_t *shared_logit,
+                                                               uint32_t *err) {
+  extern __shared__ __align__(128) uint8_t rsm_raw[];
+  uint8_t *rsm = rsm_raw + ((1024u - (smem_u32(rsm_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(rsm);
+  const uint32_t bars = sbase + kRuBarOff;
+  auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(rsm + kRuBarOff + 8 * kRuBars);
+  volatile uint32_t *dead = tmem_slot + 1;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_rt = (R + kRuRows - 1) / kRuRows;
+  const int n_items = ((T + kRuTok - 1) / kRuTok) * n_rt;
+  const int nk = H / kRmK;
+  if (tid == 0) {
+    for (int i = 0; i < kRuBars; ++i) {
+      const uint32_t count = (i >= kRuAccEmpty) ? 4u : 1u;  // acc_empty: the four epilogue warps
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar(i)), "r"(count));
+    }
+    *dead = 0u;
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kRuTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+  }
+  pdl_wait();  // the byte planes and exponents come from k_router_prep
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      uint32_t st = 0, ph = 0;
+      bool live = true;
+      for (int item = blockIdx.x; item < n_items && live; item += gridDim.x) {
+        const int t0 = (item / n_rt) * kRuTok, r0 = (item % n_rt) * kRuRows;
+        for (int kc = 0; kc < nk; ++kc) {
+          live = ru_wait(bar(kRuEmpty + st), ph ^ 1u, dead, err);
+          if (!live) break;
+          mbar_expect_tx_u32(bar(kRuFull + st), kRuStage);
+          const uint32_t base = sbase + st * kRuStage;
+#pragma unroll
+          for (int p = 0; p < 3; ++p) tma_box2d(base + p * kRuTokBox, &xmap, kc * kRmK, p * T + t0, bar(kRuFull + st));
+#pragma unroll
+          for (int p = 0; p < 2; ++p)
+            tma_box2d(base + 3 * kRuTokBox + p * kRuRowBox, &wmap, kc * kRmK, p * R + r0, bar(kRuFull + st));
+          if (++st == kRuStages) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t st = 0, ph = 0;
+      int n = 0;
+      bool live = true;
+      for (int item = blockIdx.x; item < n_items && live; item += gridDim.x) {
+        const uint32_t b = n & 1, bph = (n >> 1) & 1;
+        ++n;
+        live = ru_wait(bar(kRuAccEmpty + b), bph ^ 1u, dead, err);
+        if (!live) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * 256;
+        for (int kc = 0; kc < nk; ++kc) {
+          live = ru_wait(bar(kRuFull + st), ph, dead, err);
+          if (!live) break;
+          tc_fence_after();
+          const uint32_t base = sbase + st * kRuStage;
+          const uint64_t a0 = sw128_desc(base), a1 = sw128_desc(base + kRuTokBox),
+                         a2 = sw128_desc(base + 2 * kRuTokBox);
+          const uint64_t b0 = sw128_desc(base + 3 * kRuTokBox), b1 = sw128_desc(base + 3 * kRuTokBox + kRuRowBox);
+#pragma unroll
+          for (int kk = 0; kk < kRmK / 32; ++kk) {
+            const uint32_t acc = (kc | kk) != 0 ? 1u : 0u;
+            const uint64_t o = 2ull * kk;  // 32 bytes along the swizzled row
+            umma_i8<false, false>(d, a0 + o, b0 + o, acc);
+            umma_i8<false, false>(d + 64, a1 + o, b0 + o, acc);
+            umma_i8<false, true>(d + 64, a0 + o, b1 + o, 1u);
+            umma_i8<true, false>(d + 128, a2 + o, b0 + o, acc);
+            umma_i8<false, true>(d + 128, a1 + o, b1 + o, 1u);
+            umma_i8<true, true>(d + 192, a2 + o, b1 + o, acc);
+          }
+          umma_commit(bar(kRuEmpty + st));
+          if (++st == kRuStages) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+        if (live) umma_commit(bar(kRuAccFull + b));
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int quarter = warp & 3;  // TMEM lanes 32 * quarter .. + 31
+    const bool vec = (E % 8) == 0;
+    int n = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+      const uint32_t b = n & 1, bph = (n >> 1) & 1;
+      ++n;
+      if (!ru_wait(bar(kRuAccFull + b), bph, dead, err)) break;
+      tc_fence_after();
+      const int t0 = (item / n_rt) * kRuTok, r0 = (item % n_rt) * kRuRows;
+      const int tok = t0 + 32 * quarter + lane;
+      const bool valid = tok < T;
+      const int ex = valid ? rs.ex[tok] : 0;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + b * 256;
+#pragma unroll 1
+      for (int c = 0; c < kRuRows / 16; ++c) {
+        uint32_t v0[16], v1[16], v2[16], v3[16];
+        tmem_ld16_nowait(taddr + 16 * c, v0);
+        tmem_ld16_nowait(taddr + 64 + 16 * c, v1);
+        tmem_ld16_nowait(taddr + 128 + 16 * c, v2);
+        tmem_ld16_nowait(taddr + 192 + 16 * c, v3);
+        tmem_wait_ld();
+        if (!valid) continue;
+        const int row0 = r0 + 16 * c;
+        uint32_t o[8];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int row = row0 + j;
+          const long long S = static_cast<long long>(static_cast<int>(v0[j])) +
+                              static_cast<long long>(static_cast<int>(v1[j])) * 256LL +
+                              static_cast<long long>(static_cast<int>(v2[j])) * 65536LL +
+                              static_cast<long long>(static_cast<int>(v3[j])) * 16777216LL;
+          const uint32_t bits = row < R ? router_logit_bits(S, ex, __ldg(rs.ew + row)) : 0u;
+          if (j & 1) o[j >> 1] |= bits << 16;
+          else o[j >> 1] = bits;
+        }
+        if (vec && row0 + 16 <= E) {
+          uint4 *dst = reinterpret_cast<uint4 *>(logits + static_cast<size_t>(tok) * E + row0);
+          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int row = row0 + j;
+            const uint16_t bits = static_cast<uint16_t>(o[j >> 1] >> (16 * (j & 1)));
+            if (row < E) logits[static_cast<size_t>(tok) * E + row] = bits;
+            else if (row < R) shared_logit[tok] = bits;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kRuAccEmpty + b));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kRuTmemCols));
+  }
+}
+
 template <int CH, int RW, int TOK, int NW = 8>
 cudaError_t launch_router_cfg(const uint16_t *x, const uint16_t *W, int T, int H, int E,
                               const uint16_t *w_shared_gate, uint16_t *logits, uint16_t *shared_logit,
@@ -2565,10 +2787,24 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
     cudaError_t e = launch_pdl(k_router_prep, (warps + 7) / 8, 256, 0, s, x, T, W, w_shared_gate, E, H, *rs,
                                device_error_word());
     if (e != cudaSuccess) return e;
+    CUtensorMap xmap{}, wmap{};
+    const int sms = device_info().sms;
+    const int u_items = ((T + kRuTok - 1) / kRuTok) * ((rows + kRuRows - 1) / kRuRows);
+    if (u_items >= sms) {
+      // enough 128-token x 64-row tiles to fill the SMs: tcgen05
+      static const cudaError_t uattr =
+          cudaFuncSetAttribute(k_router_umma, cudaFuncAttributeMaxDynamicSharedMemorySize, kRuSmem);
+      if (uattr != cudaSuccess) return uattr;
+      if (!make_u8_map(&xmap, rs->xq, 3ull * T, H, kRuTok) || !make_u8_map(&wmap, rs->wq, 2ull * rows, H, kRuRows))
+        return cudaErrorInvalidValue;
+      e = launch_pdl(k_router_umma, std::min(u_items, sms), kRuThreads, kRuSmem, s, xmap, wmap, *rs, T, E, rows, H,
+                     logits, shared_logit, device_error_word());
+      if (e != cudaSuccess) return e;
+      return cudaGetLastError();
+    }
     static const cudaError_t attr =
         cudaFuncSetAttribute(k_router_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, kRmSmem);
     if (attr != cudaSuccess) return attr;
-    CUtensorMap xmap{}, wmap{};
     if (!make_u8_map(&xmap, rs->xq, 3ull * T, H, kRmTok) || !make_u8_map(&wmap, rs->wq, 2ull * rows, H, kRmRows))
       return cudaErrorInvalidValue;
     e = launch_pdl(k_router_mma, dim3((T + kRmTok - 1) / kRmTok, (rows + kRmRows - 1) / kRmRows, rs->ksplit),

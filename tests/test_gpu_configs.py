@@ -5,6 +5,8 @@
   within the north-star tolerance of the exact decode path (itself bit-exact
   to the oracle), and a seeded sample of tokens against the oracle layer
   directly (a token's result does not depend on the rest of its batch).
+* The tensor-core router on ragged tiles (tokens, rows and the shared gate
+  row off the tile grid), bit for bit against the oracle router.
 * C5: paged decode attention at the benchmark shape (16 sequences, context
   uniform in [1k, 32k], GQA 16/2, head_dim 256, page 64, a random permutation
   block table) against the attention oracle and float64 truth, at the
@@ -60,6 +62,7 @@ def test_c4_prefill_layer_5000_tokens(cuda_lib):
     pre = SparseMoEBlock(L.router_weight, L.experts, path="prefill", **kw)
     out_p = pre(L.x).clone()
     inds_p = _np(pre.last_inds).copy()
+    logits_p = _np(pre.last_logits).copy()
     del pre
     dec = SparseMoEBlock(L.router_weight, L.experts, path="decode", **kw)
     out_d = dec(L.x).clone()
@@ -71,7 +74,8 @@ def test_c4_prefill_layer_5000_tokens(cuda_lib):
     # routing: all 5,000 tokens against the oracle router
     x = _np(L.x)
     w = _np(L.router_weight)
-    want_inds, _, _, _ = moe.router(x, w, 10)
+    want_inds, _, _, want_logits = moe.router(x, w, 10)
+    np.testing.assert_array_equal(bf16.f32_to_bits(logits_p), bf16.f32_to_bits(want_logits))
     np.testing.assert_array_equal(inds_p, want_inds)
     np.testing.assert_array_equal(inds_d, want_inds)
     # every token of the tensor-core path against the exact decode path
@@ -85,6 +89,33 @@ def test_c4_prefill_layer_5000_tokens(cuda_lib):
                         _np(L.shared_expert_gate))
     np.testing.assert_array_equal(bf16.f32_to_bits(_np(out_d)[sample]), bf16.f32_to_bits(ref["out"]))
     assert_north_star(_np(out_p)[sample], ref["out"], "prefill path vs oracle sample")
+
+
+def test_router_tensor_core_ragged_tiles(cuda_lib):
+    """The tcgen05 router on ragged tiles: 3,900 tokens (not a multiple of the
+    128-token tile), 300 experts + the shared gate row (301 rows: the last
+    64-row tile one-thirteenth full, rows not a multiple of 8), H 1,024.
+    Logits and top-8 bit for bit against the oracle router on every token;
+    a seeded sample of tokens' outputs (which go through the shared gate's
+    logit) bit for bit against the oracle layer."""
+    from flashnext_b200 import synthetic
+    from flashnext_b200.moe_block import SparseMoEBlock
+    tokens, hidden, inter, experts, k = 3900, 1024, 64, 300, 8
+    L = synthetic.moe_layer(tokens, hidden, inter, experts, k, 32, zipf=None, seed=77)
+    blk = SparseMoEBlock(L.router_weight, L.experts, path="decode", top_k=k, shared=L.shared,
+                         shared_expert_gate=L.shared_expert_gate)
+    out = _np(blk(L.x))
+    x, w = _np(L.x), _np(L.router_weight)
+    want_inds, _, _, want_logits = moe.router(x, w, k)
+    np.testing.assert_array_equal(bf16.f32_to_bits(_np(blk.last_logits)), bf16.f32_to_bits(want_logits))
+    np.testing.assert_array_equal(_np(blk.last_inds), want_inds)
+    rng = np.random.default_rng(77)
+    sample = np.sort(np.concatenate([rng.choice(tokens - 60, 40, replace=False), np.arange(tokens - 60, tokens)]))
+    bank = {n: tuple(_np(t) for t in v) for n, v in L.experts.items()}
+    sh = tuple(tuple(_np(t) for t in L.shared[n]) for n in ("gate_proj", "up_proj", "down_proj"))
+    ref = moe.moe_block(x[sample], w, k, bank["gate_proj"], bank["up_proj"], bank["down_proj"], sh,
+                        _np(L.shared_expert_gate))
+    np.testing.assert_array_equal(bf16.f32_to_bits(out[sample]), bf16.f32_to_bits(ref["out"]))
 
 
 def _check_attention(got, P):
