@@ -2238,17 +2238,38 @@ constexpr int kRmBarOff = kRmStages * kRmStage;
 constexpr int kRmSmem = kRmBarOff + 16 * kRmStages + 1024;            // + barriers + 1 KiB alignment
 constexpr uint32_t kRmSpin = 1u << 22;                                // mbarrier polls before giving up
 
+//
+// With prep_limbs set, CTAs from prep_base on compute the projection's row
+// fixed point of x (prep_rows_body, prep_tpr threads per row), which saves
+// decode batches the separate launch.
 __global__ void __launch_bounds__(256) k_router_prep(const uint16_t *x, int T, const uint16_t *__restrict__ W,
                                                      const uint16_t *__restrict__ wsg, int E, int H,
-                                                     RouterScratch rs, uint32_t *err) {
+                                                     RouterScratch rs, uint16_t *prep_limbs, float *prep_meta,
+                                                     int prep_G, int prep_tpr, int prep_base, uint32_t *err) {
   pdl_wait();
   pdl_trigger();
+  if (prep_limbs != nullptr && static_cast<int>(blockIdx.x) >= prep_base) {
+    const int block = blockIdx.x - prep_base;
+    const int spt = (H / 8 + prep_tpr - 1) / prep_tpr;
+    if (prep_G == 32) {
+      if (spt == 1) prep_rows_body<32, 1>(x, T, H, prep_tpr, prep_limbs, prep_meta, err, block);
+      else if (spt == 2) prep_rows_body<32, 2>(x, T, H, prep_tpr, prep_limbs, prep_meta, err, block);
+      else prep_rows_body<32, 4>(x, T, H, prep_tpr, prep_limbs, prep_meta, err, block);
+    } else {
+      if (spt == 1) prep_rows_body<64, 1>(x, T, H, prep_tpr, prep_limbs, prep_meta, err, block);
+      else if (spt == 2) prep_rows_body<64, 2>(x, T, H, prep_tpr, prep_limbs, prep_meta, err, block);
+      else prep_rows_body<64, 4>(x, T, H, prep_tpr, prep_limbs, prep_meta, err, block);
+    }
+    return;
+  }
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int R = E + (wsg != nullptr ? 1 : 0);
   if (rs.ksplit > 1) {  // split-K: zero the partial sums and the tile tickets
     const size_t n = static_cast<size_t>(T) * R;
     const size_t tiles = static_cast<size_t>((T + kRmTok - 1) / kRmTok) * ((R + kRmRows - 1) / kRmRows);
-    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    // the router CTAs only (the row fixed point CTAs after them have returned)
+    const int ctas = prep_limbs != nullptr ? prep_base : static_cast<int>(gridDim.x);
+    const size_t stride = static_cast<size_t>(ctas) * blockDim.x;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) rs.acc[i] = 0ull;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < tiles; i += stride)
       rs.tickets[i] = 0;
@@ -2784,8 +2805,16 @@ cudaError_t launch_router_logits(const uint16_t *x, const uint16_t *W, int T, in
   if (rs != nullptr && router_scratch_bytes(T, rows, H) > 0) {
     // many tokens: byte planes, then the integer tensor-core GEMM
     const int warps = T + rows;
-    cudaError_t e = launch_pdl(k_router_prep, (warps + 7) / 8, 256, 0, s, x, T, W, w_shared_gate, E, H, *rs,
-                               device_error_word());
+    const int base = (warps + 7) / 8;
+    // decode batches: the row fixed point of x in extra CTAs of the same
+    // launch when its threads per row divide the 256-thread CTA
+    const int slices = H / 8;
+    const int tpr = std::min(256, ((slices + 31) / 32) * 32);
+    const bool prep = prep_limbs != nullptr && 256 % tpr == 0 && slices <= 4 * tpr && (prep_G == 32 || prep_G == 64);
+    const int prep_ctas = prep ? (T + 256 / tpr - 1) / (256 / tpr) : 0;
+    cudaError_t e = launch_pdl(k_router_prep, base + prep_ctas, 256, 0, s, x, T, W, w_shared_gate, E, H, *rs,
+                               prep ? prep_limbs : nullptr, prep_meta, prep_G, tpr, base, device_error_word());
+    if (e == cudaSuccess && prep_done != nullptr) *prep_done = prep;
     if (e != cudaSuccess) return e;
     CUtensorMap xmap{}, wmap{};
     const int sms = device_info().sms;
