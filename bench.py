@@ -20,8 +20,9 @@ time, CUDA events, max over ranks).  ``e2e`` = the same through the public
 API with the batch copied from pinned host memory and the output copied back
 inside the timed region.  N > 1 (torchrun) runs the layer expert-parallel:
 512/N experts per GPU, router and shared expert replicated, each GPU routing
-its own 64 tokens (weak scaling) with NCCL all-to-all dispatch and return of
-the per-slot outputs; device time is the max over ranks.
+its own 64 tokens (weak scaling), dispatch and return of the per-slot outputs
+by the library's kernels over NVLink peer memory; device time is the max over
+ranks.
 
 ``--workload c3|c4|c5`` print one line each for the other benchmark configs
 (48-layer stack, 5k-token prefill, paged attention).
@@ -533,8 +534,10 @@ def gpu_arm(args):
 
 def ep_arm(args):
     """N > 1: the C2 layer expert-parallel over N GPUs (experts 512/N per rank,
-    router and shared expert replicated, 64 tokens routed by each rank, NCCL
-    all-to-all dispatch and return of the per-slot outputs)."""
+    router and shared expert replicated, 64 tokens routed by each rank;
+    dispatch of the x rows and return of the per-slot outputs by the
+    library's own kernels over NVLink peer memory, ``fnmoe_ep_*``; NCCL only
+    for set-up and the parity check)."""
     import datetime
 
     import torch
@@ -582,8 +585,8 @@ def ep_arm(args):
     for i in range(warm):
         eager_step(i)
     torch.cuda.synchronize()
-    # One CUDA graph per layer (NCCL all-to-alls included: with a fixed
-    # capacity the step reads nothing back to the host).  Every rank must
+    # One CUDA graph per layer (the peer-memory exchange kernels included:
+    # with a fixed capacity the step reads nothing back to the host).  Every rank must
     # agree that capture worked before any graph is replayed.
     graphs, gouts = [], []  # the only references to the graphs: cleared before the process group goes
     ok = 1
