@@ -22,10 +22,13 @@ inside the timed region.  N > 1 (torchrun) runs the layer expert-parallel:
 512/N experts per GPU, router and shared expert replicated, each GPU routing
 its own 64 tokens (weak scaling), dispatch and return of the per-slot outputs
 by the library's kernels over NVLink peer memory; device time is the max over
-ranks.
+ranks.  That line also carries ``configs.c3``: the 48-layer C3 stack
+expert-parallel over the same ranks (batch 64 and 1 per GPU), with its own
+bit-identity check.
 
 ``--workload c3|c4|c5`` print one line each for the other benchmark configs
-(48-layer stack, 5k-token prefill, paged attention).
+(48-layer stack -- expert-parallel under torchrun --, 5k-token prefill, paged
+attention).
 
 ``--impl reference`` times the reference-semantics CPU implementation (the
 NumPy oracle port; MLX, the reference's own runtime, is not installable
@@ -670,6 +673,8 @@ def ep_arm(args):
         return 1000.0 * t / max(1, c)
 
     exchange_us = {"dispatch": avg_us("ep_dispatch"), "return_combine": avg_us("ep_return_combine")}
+    # the 48-layer C3 stack expert-parallel over the same ranks (collective)
+    c3 = None if args.no_configs else c3_ep_numbers(10)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -695,6 +700,8 @@ def ep_arm(args):
             "gpu_launches": int(round(launches_per_step * args.steps)),
             "clocks": clocks, "cpu_baseline": None,
         }
+        if c3 is not None:
+            line["configs"] = {"c3": c3}
         print(json.dumps(line), flush=True)
     dist.barrier()
     torch.cuda.synchronize()
@@ -926,6 +933,122 @@ def c3_arm(args):
     return 0
 
 
+def c3_ep_numbers(steps: int) -> dict:
+    """Config 3 expert-parallel over the ranks of the initialised process
+    group: the 48-layer stack, H3072/I640/E512 top-10 Q4/G32 + shared,
+    512/N experts of every layer per rank (tiled), router and shared expert
+    replicated, the library's NVLink peer-memory exchange in every layer.
+    Each rank routes its own batch (64 tokens, then 1: weak scaling); one CUDA
+    graph per layer, the 48 replayed in order per step; device time max over
+    ranks.  Layer 0 is checked bit for bit against all 512 experts on one
+    GPU, on every rank.  Collective: every rank calls it."""
+    import gc
+
+    import torch
+    import torch.distributed as dist
+
+    from flashnext_b200 import synthetic
+    from flashnext_b200.expert_parallel import CudaBackend, ExpertParallelMoE
+    from flashnext_b200.moe_block import SparseMoEBlock
+
+    world, rank, _ = _dist()
+    H, I, E, K, n_layers, cap = 3072, 640, 512, 10, 48, 64
+    per = E // world
+    eps, xs = [], []
+    parity = False
+    for l in range(n_layers):
+        L = synthetic.moe_layer(cap * world, H, I, E, K, 32, zipf=1.1, seed=7000 + 31 * l)
+        local_bank = {n: tuple(t[rank * per:(rank + 1) * per].contiguous() for t in v) for n, v in L.experts.items()}
+        backend = CudaBackend(L.router_weight, local_bank, L.shared, L.shared_expert_gate, top_k=K)
+        eps.append(ExpertParallelMoE(backend, expert_count=E, hidden_size=H, top_k=K, capacity_tokens=cap))
+        xs.append(L.x[cap * rank:cap * (rank + 1)].contiguous())
+        if l == 0:  # every rank takes this collective step at the same point
+            ref = SparseMoEBlock(L.router_weight, L.experts, top_k=K, shared=L.shared,
+                                 shared_expert_gate=L.shared_expert_gate)
+            parity = torch.equal(eps[0](xs[0]).view(torch.int16), ref(xs[0]).view(torch.int16))
+            del ref
+        del L, local_bank, backend
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    flag = torch.tensor([1 if parity else 0], dtype=torch.int32, device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    parity = bool(flag.item())
+    stream = torch.cuda.current_stream()
+    results = {}
+    for batch in (64, 1):
+        bx = [x[:batch].contiguous() for x in xs]
+        for ep, x in zip(eps, bx):  # eager warm-up of every layer at this batch
+            ep(x)
+        torch.cuda.synchronize()
+        graphs, gouts = [], []
+        _capture_ep_graphs(eps, bx, graphs, gouts)
+        for _ in range(3):
+            for g in graphs:
+                g.replay()
+        torch.cuda.synchronize()
+        _barrier(world)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(CUSHION_CYCLES)
+        start.record(stream)
+        for _ in range(steps):
+            for g in graphs:
+                g.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        _barrier(world)
+        ms = _max_over_ranks(start.elapsed_time(end), world) / steps
+        results[f"batch{batch}"] = {"tokens_per_s": batch * world / (ms / 1000.0), "ms_per_token_step": ms,
+                                    "tokens_per_gpu": batch}
+        graphs.clear()  # the graphs go before the exchange windows and the process group
+        gouts.clear()
+        gc.collect()
+        torch.cuda.synchronize()
+    for ep in eps:
+        ep.close()
+    del eps, xs
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return {"metric": "48-layer MoE decode tokens/s (C3)", "value": results["batch64"]["tokens_per_s"],
+            "unit": "tokens/s", "n_gpus": world, "steps": steps, "scaling": "weak", "parity_vs_1gpu": parity,
+            "workload": "C3: 48 layers, H3072/I640/E512 top-10 Q4/G32 + shared, Zipf(1.1) routing, "
+                        f"experts sharded {per}/GPU, router + shared expert replicated; value = batch-64-per-GPU "
+                        "tokens/s of the whole job, batch1 below",
+            "parallelism": f"ep{world}", "results": results}
+
+
+def c3_ep_arm(args):
+    """``--workload c3`` under torchrun (N > 1): the expert-parallel 48-layer
+    stack as its own line (c3_ep_numbers)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    from flashnext_b200 import _lib
+
+    _lib.ensure_device()
+    hbm_peak, peak_kind = _peaks()
+    r = c3_ep_numbers(args.steps)
+    if rank == 0:
+        print(json.dumps({
+            "metric": r["metric"], "value": r["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": 3, "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic",
+            "parity_vs_1gpu": r["parity_vs_1gpu"],
+            "config": {"workload": r["workload"], "parallelism": r["parallelism"], "cuda_graph": True,
+                       "exchange": "NVLink peer stores into CUDA-IPC windows (the library's kernels)",
+                       "parity": "layer 0, every rank: bit-identical to all 512 experts on one GPU"},
+            "results": r["results"], "peak": hbm_peak, "peak_kind": peak_kind,
+        }), flush=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    dist.destroy_process_group()
+    return 0
+
+
 def c4_numbers(steps_arg: int, warmup: int) -> dict:
     """Config 4: 5,000-token prefill chunk through one H2048/I512/E512 top-10
     Q4/G32 layer (+ shared), uniform routing.  The layer picks the tcgen05
@@ -1012,14 +1135,15 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=LAYERS, help="distinct layers rotated per step")
     ap.add_argument("--no-batch1", action="store_true", help="skip the batch-1 CUDA-graph sub-measure")
     ap.add_argument("--no-configs", action="store_true",
-                    help="skip the C3/C4/C5 sub-measures of the default one-GPU line")
+                    help="skip the C3/C4/C5 sub-measures of the default line (one GPU), "
+                         "or its expert-parallel C3 sub-measure (N > 1)")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return reference_arm(args)
     if args.workload == "c5":
         return c5_arm(args)
     if args.workload == "c3":
-        return c3_arm(args)
+        return c3_ep_arm(args) if _dist()[0] > 1 else c3_arm(args)
     if args.workload == "c4":
         return c4_arm(args)
     if _dist()[0] > 1:

@@ -354,6 +354,23 @@ FNMOE_API int fnmoe_router_topk_shared(const void *x, const void *router_weight,
                                        void *mass, void *logits, void *shared_logit,
                                        void *shared_gate, void *stream);
 
+/* fnmoe_router_topk_shared with a caller workspace (adaptive_topk.py:59-64,
+ * 263-264, the same outputs): from 64 tokens the logits come from the integer
+ * tensor-core GEMM on byte planes of the fixed points, which the workspace
+ * holds; fewer tokens take the GEMV path and need none.
+ * fnmoe_router_workspace_size reports the bytes (0 when none are needed);
+ * a smaller workspace is FNMOE_ERR_WORKSPACE.  Used by the expert-parallel
+ * layer, which routes each rank's decode batch. */
+FNMOE_API int fnmoe_router_workspace_size(uint32_t tokens, uint32_t hidden, uint32_t experts,
+                                          uint32_t with_shared_gate, uint64_t *bytes);
+FNMOE_API int fnmoe_router_topk_shared_ws(const void *x, const void *router_weight,
+                                          const void *shared_gate_weight, uint32_t tokens,
+                                          uint32_t hidden, uint32_t experts, uint32_t top_k,
+                                          float renorm_blend, uint32_t *inds, void *scores,
+                                          void *mass, void *logits, void *shared_logit,
+                                          void *shared_gate, void *workspace,
+                                          uint64_t workspace_bytes, void *stream);
+
 /* Slot-ordered combine of per-slot expert outputs (metal_runtime.py:301-333):
  * out[t] = bf16(sum_s float(slot_outputs[t,s]) * score[t,s]) in slot order
  * (float32, no fused multiply-add; slots whose route is >= expert_count are

@@ -95,6 +95,26 @@ struct Carver {
   uint64_t used() const { return shift + off; }
 };
 
+// The many-token router's scratch (byte planes of the fixed points, row
+// exponents, split-K partial sums and tile tickets) carved from `cv`; false
+// when T tokens x R rows take the GEMV path, which needs none.
+bool carve_router(Carver &cv, int T, int R, int H, RouterScratch &rs) {
+  if (router_scratch_bytes(T, R, H) == 0) return false;
+  const uint64_t TH = static_cast<uint64_t>(T) * H;
+  rs.xq = cv.take<uint8_t>(3 * TH);
+  rs.wq = cv.take<uint8_t>(2ull * R * H);
+  rs.ex = cv.take<int32_t>(T);
+  rs.ew = cv.take<int32_t>(R);
+  rs.ksplit = router_ksplit(T, R, H);
+  rs.acc = nullptr;
+  rs.tickets = nullptr;
+  if (rs.ksplit > 1) {
+    rs.acc = cv.take<unsigned long long>(static_cast<uint64_t>(T) * R);
+    rs.tickets = cv.take<int32_t>(static_cast<uint64_t>(router_tiles(T, R)));
+  }
+  return true;
+}
+
 bool device_ok(std::string &why) {
   int n = 0;
   cudaError_t e = cudaGetDeviceCount(&n);
@@ -523,6 +543,57 @@ int fnmoe_router_topk_shared(const void *x, const void *router_weight, const voi
   return e == cudaSuccess ? FNMOE_OK : cuda_fail(e, "softmax_topk");
 }
 
+int fnmoe_router_workspace_size(uint32_t tokens, uint32_t hidden, uint32_t experts, uint32_t with_shared_gate,
+                                uint64_t *bytes) {
+  if (!bytes) return fail(FNMOE_ERR_NULL, "bytes is required");
+  if (tokens == 0 || hidden == 0 || hidden % 8 || hidden > 4096)
+    return fail(FNMOE_ERR_SHAPE, "tokens must be positive, hidden a multiple of 8 up to 4096");
+  if (experts == 0 || experts > 1024) return fail(FNMOE_ERR_SHAPE, "experts must be in 1..1024");
+  Carver cv(nullptr);
+  RouterScratch rs{};
+  const bool need = carve_router(cv, static_cast<int>(tokens), static_cast<int>(experts + (with_shared_gate ? 1 : 0)),
+                                 static_cast<int>(hidden), rs);
+  *bytes = need ? cv.off + kWorkspaceSlack : 0;
+  return FNMOE_OK;
+}
+
+int fnmoe_router_topk_shared_ws(const void *x, const void *router_weight, const void *shared_gate_weight,
+                                uint32_t tokens, uint32_t hidden, uint32_t experts, uint32_t top_k,
+                                float renorm_blend, uint32_t *inds, void *scores, void *mass, void *logits,
+                                void *shared_logit, void *shared_gate, void *workspace, uint64_t workspace_bytes,
+                                void *stream) {
+  if (!x || !router_weight || !shared_gate_weight || !inds || !scores || !logits || !shared_logit || !shared_gate)
+    return fail(FNMOE_ERR_NULL,
+                "x, router_weight, shared_gate_weight, inds, scores, logits, shared_logit and shared_gate are required");
+  if (tokens == 0 || hidden == 0 || hidden % 8) return fail(FNMOE_ERR_SHAPE, "hidden must be a positive multiple of 8");
+  if (hidden > 4096) return fail(FNMOE_ERR_SHAPE, "hidden must be <= 4096");
+  if (experts == 0 || experts > 1024) return fail(FNMOE_ERR_SHAPE, "experts must be in 1..1024");
+  if (top_k == 0 || top_k > kMaxTopK || top_k > experts) return fail(FNMOE_ERR_VALUE, "top_k out of range");
+  uint64_t need = 0;
+  int rc = fnmoe_router_workspace_size(tokens, hidden, experts, 1, &need);
+  if (rc != FNMOE_OK) return rc;
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return fail(FNMOE_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes");
+  RouterScratch rs{};
+  bool has_rs = false;
+  if (need > 0) {
+    Carver cv(workspace);
+    has_rs = carve_router(cv, static_cast<int>(tokens), static_cast<int>(experts) + 1, static_cast<int>(hidden), rs);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = ensure_exp_table(s);
+  if (e != cudaSuccess) return cuda_fail(e, "exp table");
+  e = launch_router_logits(static_cast<const uint16_t *>(x), static_cast<const uint16_t *>(router_weight), tokens,
+                           hidden, experts, static_cast<const uint16_t *>(shared_gate_weight),
+                           static_cast<uint16_t *>(logits), static_cast<uint16_t *>(shared_logit), s, nullptr,
+                           nullptr, 32, nullptr, has_rs ? &rs : nullptr);
+  if (e != cudaSuccess) return cuda_fail(e, "router logits");
+  e = launch_softmax_topk(static_cast<const uint16_t *>(logits), tokens, experts, top_k, renorm_blend, nullptr, 0,
+                          inds, inds, nullptr, static_cast<uint16_t *>(scores), static_cast<uint16_t *>(mass),
+                          static_cast<const uint16_t *>(shared_logit), static_cast<uint16_t *>(shared_gate), s);
+  return e == cudaSuccess ? FNMOE_OK : cuda_fail(e, "softmax_topk");
+}
+
 int fnmoe_combine(const void *slot_outputs, const uint32_t *routes, const void *scores, uint32_t scores_dtype,
                   uint32_t tokens, uint32_t slots, uint32_t hidden, uint32_t expert_count, const void *shared_y,
                   const void *shared, const void *shared_gate, void *out, void *stream) {
@@ -687,19 +758,7 @@ uint64_t carve_layer(const FnMoELayerArgs *a, void *base, LayerLayout &LL, uint6
   {
     // many-token router: byte planes of the fixed points and row exponents
     const int R = E + (shared ? 1 : 0);
-    if (router_scratch_bytes(T, R, a->hidden_size) > 0) {
-      const uint64_t TH = static_cast<uint64_t>(T) * a->hidden_size;
-      LL.rs.xq = cv.take<uint8_t>(3 * TH);
-      LL.rs.wq = cv.take<uint8_t>(2ull * R * a->hidden_size);
-      LL.rs.ex = cv.take<int32_t>(T);
-      LL.rs.ew = cv.take<int32_t>(R);
-      LL.rs.ksplit = router_ksplit(T, R, a->hidden_size);
-      if (LL.rs.ksplit > 1) {
-        LL.rs.acc = cv.take<unsigned long long>(static_cast<uint64_t>(T) * R);
-        LL.rs.tickets = cv.take<int32_t>(static_cast<uint64_t>(router_tiles(T, R)));
-      }
-      LL.has_rs = true;
-    }
+    LL.has_rs = carve_router(cv, T, R, static_cast<int>(a->hidden_size), LL.rs);
   }
   if (used != nullptr) *used = cv.used();
   return cv.off + kWorkspaceSlack;

@@ -170,6 +170,9 @@ SIGNATURES = {
                           ctypes.c_int),
     "fnmoe_router_topk_shared": ([_vp, _vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_float, _vp, _vp, _vp, _vp, _vp,
                                   _vp, _vp], ctypes.c_int),
+    "fnmoe_router_workspace_size": ([_u32, _u32, _u32, _u32, ctypes.POINTER(_u64)], ctypes.c_int),
+    "fnmoe_router_topk_shared_ws": ([_vp, _vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_float, _vp, _vp, _vp, _vp,
+                                     _vp, _vp, _vp, _u64, _vp], ctypes.c_int),
     "fnmoe_combine": ([_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "fnmoe_softmax_topk": ([_vp, _u32, _u32, _u32, ctypes.c_float, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "fnmoe_group_tokens": ([_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _u64, _vp], ctypes.c_int),

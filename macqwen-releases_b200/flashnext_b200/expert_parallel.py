@@ -94,6 +94,7 @@ class CudaBackend:
         self.inter_size = self.local.inter_size
         self.shared_gate_weight = _bf16(shared_expert_gate, "shared_expert_gate").reshape(-1)
         self._ws = _Workspace()
+        self._rws = _Workspace()  # the router's: byte planes of the fixed points from 64 tokens
 
     def route(self, x):
         torch = _torch()
@@ -106,11 +107,16 @@ class CudaBackend:
         sl = torch.empty((T,), dtype=torch.bfloat16, device="cuda")
         sg = torch.empty((T,), dtype=torch.bfloat16, device="cuda")
         if T:
-            _lib.check(lib.fnmoe_router_topk_shared(
+            need = ctypes.c_uint64(0)
+            _lib.check(lib.fnmoe_router_workspace_size(T, self.hidden_size, self.expert_count, 1, ctypes.byref(need)),
+                       "router_workspace_size")
+            w = self._rws.get(need.value) if need.value else None
+            _lib.check(lib.fnmoe_router_topk_shared_ws(
                 x.data_ptr(), self.router_weight.data_ptr(), self.shared_gate_weight.data_ptr(), T,
                 self.hidden_size, self.expert_count, self.top_k, self.renorm_blend, inds.data_ptr(),
-                scores.data_ptr(), mass.data_ptr(), logits.data_ptr(), sl.data_ptr(), sg.data_ptr(), _stream()),
-                "router_topk_shared")
+                scores.data_ptr(), mass.data_ptr(), logits.data_ptr(), sl.data_ptr(), sg.data_ptr(),
+                w.data_ptr() if w is not None else None, w.numel() if w is not None else 0, _stream()),
+                "router_topk_shared_ws")
         return inds, scores, sg
 
     def run_experts(self, x_ptr: int, ids_ptr: int, rows: int, slots: int, out_ptr: int) -> None:

@@ -76,6 +76,22 @@ def test_workspace_size_and_validation_without_gpu():
     assert "shared_gate" in _lib.last_error(lib)
 
 
+def test_router_workspace_size_without_gpu():
+    """The workspace router needs scratch from 64 tokens (H a multiple of 128
+    up to 4096), none below; bad shapes are rejected before any device call."""
+    lib = _lib.load()
+    need = ctypes.c_uint64(123)
+    assert lib.fnmoe_router_workspace_size(63, 2048, 512, 1, ctypes.byref(need)) == _lib.OK
+    assert need.value == 0
+    assert lib.fnmoe_router_workspace_size(64, 2048, 512, 1, ctypes.byref(need)) == _lib.OK
+    # byte planes 3 x 64 x 2048 + 2 x 513 x 2048 at least, plus exponents
+    assert need.value >= 3 * 64 * 2048 + 2 * 513 * 2048 + 4 * (64 + 513)
+    assert lib.fnmoe_router_workspace_size(64, 2056, 512, 1, ctypes.byref(need)) == _lib.OK
+    assert need.value == 0  # H not a multiple of 128: the GEMV path
+    assert lib.fnmoe_router_workspace_size(64, 2050, 512, 1, ctypes.byref(need)) == _lib.ERR_SHAPE
+    assert lib.fnmoe_router_workspace_size(64, 2048, 2048, 1, ctypes.byref(need)) == _lib.ERR_SHAPE
+
+
 C_PROBE = r"""
 #include <stdio.h>
 #include <stddef.h>

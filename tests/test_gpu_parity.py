@@ -131,6 +131,51 @@ def test_router_topk_bit_exact(cuda_lib, tokens, hidden, experts, zipf):
     assert_bf16_equal(_np(mass), o_mass[:, 0], "topk mass")
 
 
+@pytest.mark.parametrize("tokens,hidden", [(64, 2048), (200, 1024), (5, 2048), (70, 2056)])
+def test_router_topk_shared_workspace_bit_exact(cuda_lib, tokens, hidden):
+    """fnmoe_router_topk_shared_ws (the expert-parallel layer's router): the
+    tensor-core path from 64 tokens, the GEMV below or off the 128-byte grid;
+    logits, shared logit, top-k and shared gate bit for bit against the
+    oracle; a workspace one byte short is refused."""
+    import ctypes
+
+    import torch
+
+    from flashnext_b200 import _lib, synthetic
+    lib = _lib.ensure_device()
+    E, k = 512, 10
+    x = synthetic.bf16_normal((tokens, hidden), seed=61)
+    w = synthetic.bf16_normal((E, hidden), 0.02, seed=62)
+    wg = synthetic.bf16_normal((hidden,), 0.02, seed=63)
+    need = ctypes.c_uint64(0)
+    assert lib.fnmoe_router_workspace_size(tokens, hidden, E, 1, ctypes.byref(need)) == _lib.OK
+    assert (need.value > 0) == (tokens >= 64 and hidden % 128 == 0)
+    ws = torch.empty(max(need.value, 1), dtype=torch.uint8, device="cuda")
+    inds = torch.empty((tokens, k), dtype=torch.int32, device="cuda")
+    scores = torch.empty((tokens, k), dtype=torch.bfloat16, device="cuda")
+    mass = torch.empty((tokens,), dtype=torch.bfloat16, device="cuda")
+    logits = torch.empty((tokens, E), dtype=torch.bfloat16, device="cuda")
+    sl = torch.empty((tokens,), dtype=torch.bfloat16, device="cuda")
+    sg = torch.empty((tokens,), dtype=torch.bfloat16, device="cuda")
+
+    def call(nbytes):
+        return lib.fnmoe_router_topk_shared_ws(x.data_ptr(), w.data_ptr(), wg.data_ptr(), tokens, hidden, E, k, 1.0,
+                                               inds.data_ptr(), scores.data_ptr(), mass.data_ptr(), logits.data_ptr(),
+                                               sl.data_ptr(), sg.data_ptr(), ws.data_ptr(), nbytes, None)
+
+    if need.value:
+        assert call(need.value - 1) == _lib.ERR_WORKSPACE
+    for _ in range(2):  # twice: the split-K partial sums must start from zero again
+        assert call(need.value) == _lib.OK
+        torch.cuda.synchronize()
+        o_inds, o_scores, _, o_logits = moe.router(_np(x), _np(w), k)
+        assert_bf16_equal(_np(logits), o_logits, "logits")
+        np.testing.assert_array_equal(_np(inds), o_inds)
+        assert_bf16_equal(_np(scores), o_scores, "renormalised scores")
+        o_sl = moe.router_logits(_np(x), _np(wg).reshape(1, -1))[:, 0]
+        assert_bf16_equal(_np(sl), o_sl, "shared logit")
+
+
 @pytest.mark.parametrize("tokens", [3, 20])
 def test_router_topk_limits_bit_exact(cuda_lib, tokens):
     """The interface limits: 1,024 experts (32 logits per lane) and top-k 16,
