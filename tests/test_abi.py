@@ -90,6 +90,14 @@ def test_router_workspace_size_without_gpu():
     assert need.value == 0  # H not a multiple of 128: the GEMV path
     assert lib.fnmoe_router_workspace_size(64, 2050, 512, 1, ctypes.byref(need)) == _lib.ERR_SHAPE
     assert lib.fnmoe_router_workspace_size(64, 2048, 2048, 1, ctypes.byref(need)) == _lib.ERR_SHAPE
+    # the workspace router refuses a missing or short workspace before any device call
+    fake = [ctypes.c_void_p(256 * (i + 1)) for i in range(9)]
+    args = (fake[0], fake[1], fake[2], 64, 2048, 512, 10, ctypes.c_float(1.0), *fake[3:9])
+    assert lib.fnmoe_router_topk_shared_ws(*args, None, 0, None) == _lib.ERR_WORKSPACE
+    assert lib.fnmoe_router_topk_shared_ws(*args, fake[0], 1024, None) == _lib.ERR_WORKSPACE
+    assert "workspace" in _lib.last_error(lib)
+    assert lib.fnmoe_router_topk_shared_ws(fake[0], None, fake[2], 64, 2048, 512, 10, ctypes.c_float(1.0),
+                                           *fake[3:9], None, 0, None) == _lib.ERR_NULL
 
 
 C_PROBE = r"""
