@@ -2073,9 +2073,8 @@ cudaError_t launch_combine_f32(const float *d, const uint32_t *routes, const voi
 }
 
 // ---------------------------------------------------------------------------
-// router logits: bf16 GEMV with the canonical 32-lane order
+// router logits: exact integer dot products of the row fixed points
 // ---------------------------------------------------------------------------
-
 
 // Router logits as exact integer dot products (GEMV form).  Grid (row
 // groups, token blocks).  Each warp keeps kRouterRW router rows in registers
