@@ -71,10 +71,11 @@ def _peaks():
 
 
 # DRAM traffic of the gate/up launch per expert it streams (routed + shared):
-# dram__bytes_read.sum + dram__bytes_write.sum = 272,829,952 + 5,521,408 B from
-# one ncu capture of this workload's layer (1 layer, 192 routed experts + the
-# shared one), divided by 193.  Scaled to each run's expert count.
-NCU_GATE_UP_TRAFFIC_PER_EXPERT = (272_829_952 + 5_521_408) / 193
+# dram__bytes_read.sum 273,532,416 B (ncu, this workload's layer: 1 layer, 192
+# routed experts + the shared one) + dram__bytes_write.sum 4,458,752 B (the
+# full capture of the same launch), divided by 193.  Scaled to each run's
+# expert count.
+NCU_GATE_UP_TRAFFIC_PER_EXPERT = (273_532_416 + 4_458_752) / 193
 
 
 class ClockSampler:

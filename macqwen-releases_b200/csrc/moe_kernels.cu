@@ -1394,9 +1394,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a,
   //
   // Tiled tables: every warp asks L2 for its item's whole row-group range at
   // setup (one bulk prefetch), so all of an item's blocks are in flight at
-  // once and the ring's copies find them in L2.  Small batches (4-warp CTAs,
-  // few experts) also prefetch, from the gate/up kernel, the row tile's share
-  // of the same expert's down record, which the down kernel then reads from L2.
+  // once and the ring's copies find them in L2.  Not in the 16-warp gate/up
+  // kernel: there the rings alone keep enough bytes in flight, and the
+  // prefetch one item ahead added ~38% DRAM re-reads (lines evicted before
+  // their ring copy) at the 64-token layer.  Small batches (4-warp CTAs, few
+  // experts) also prefetch, from the gate/up kernel, the row tile's share of
+  // the same expert's down record, which the down kernel then reads from L2.
   auto setup = [&](const RawDesc &rd, int rt, Src &src) {
     ItemInfo it = item_setup<DUAL, TILED>(a, rd, rt, ROWS, wbase, O, K, xs.Gc, nblk, lane, src);
     if (TILED && it.rt * ROWS + wbase >= O) {
@@ -1404,7 +1407,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_expert_rows(ExpertCallArgs a,
       it.len = -1;
       src = Src{nullptr, nullptr};
     }
-    if (TILED && it.ok && lane == 0) {
+    if (TILED && (WARPS <= 4 || !DUAL) && it.ok && lane == 0) {
       bulk_prefetch_l2(src.w, static_cast<unsigned>(nblk) * kTileChunk);
       uint32_t rec = 0;
       if (DUAL && WARPS <= 4 && warp == 0 && a.tiled.down != nullptr &&
